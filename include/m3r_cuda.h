@@ -1,0 +1,161 @@
+/*
+ * m3r_cuda -- C ABI of the B200 (sm_100a) backend for the two-view inference
+ * path of mast3r-runtime: engine.infer(img1, img2) and engine.match(desc_1, desc_2).
+ *
+ * This ABI is what the reference's native-engine slot binds.  The reference's
+ * Python dispatcher imports `mast3r_runtime.backends._cuda.CUDAEngine`
+ * (mast3r_runtime/backends/__init__.py:173-179), constructs it as
+ * CUDAEngine(variant=, resolution=, precision=, num_threads=) (:204-215) and wraps
+ * it in NativeEngineWrapper (mast3r_runtime/backends/native_wrapper.py:20-145).
+ * The ctypes module mast3r_runtime_b200/_cuda.py implements that object over the
+ * functions below.  Each entry point cites the reference interface it replaces.
+ *
+ * Conventions: every function returns M3R_OK (0) or a negative M3R_ERR_* code;
+ * m3r_last_error(engine) / m3r_global_error() give the message.  Buffers are
+ * plain host pointers owned by the caller; no pointer is retained after a call
+ * returns.  An engine is not re-entrant: calls on one engine must be serialised.
+ */
+#ifndef M3R_CUDA_H
+#define M3R_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define M3R_ABI_VERSION 1
+
+#define M3R_OK 0
+#define M3R_ERR_ARG (-1)     /* bad argument, shape or size */
+#define M3R_ERR_IO (-2)      /* weights file missing / corrupt / wrong shape */
+#define M3R_ERR_CUDA (-3)    /* CUDA runtime or driver error */
+#define M3R_ERR_NCCL (-4)    /* NCCL error */
+#define M3R_ERR_TIMEOUT (-5) /* a device-side bounded wait ran out */
+#define M3R_ERR_STATE (-6)   /* call not valid in the engine's state (e.g. infer before load) */
+#define M3R_ERR_NOMEM (-7)   /* device or pinned host allocation failed */
+
+#define M3R_MAX_DEVICES 16
+
+/* Model architecture + runtime shape.  Dimensions follow the reference's model
+ * table (csrc/common/types.hpp:51-69, csrc/mps/graph_builder.hpp:67-77). */
+typedef struct m3r_config {
+    int patch;      /* 14 (DUNE) or 16 (MASt3R ViT-L) */
+    int enc_dim, enc_depth, enc_heads, enc_mlp;
+    int dec_dim, dec_depth, dec_heads, dec_mlp;
+    int lf_hidden;  /* local-feature MLP width */
+    int desc_dim;   /* 24 */
+    int img_h, img_w;   /* input image size, multiples of `patch` */
+    int n_devices;      /* 0 = device 0 only */
+    int devices[M3R_MAX_DEVICES];
+    int max_pairs;      /* image pairs per device per launch (activation buffers) */
+} m3r_config;
+
+/* Slots of the timing_ms array written by m3r_infer / m3r_match. */
+enum {
+    M3R_T_PREPROCESS = 0, /* u8 -> normalised patches (device) */
+    M3R_T_ENCODER = 1,
+    M3R_T_DECODER = 2,
+    M3R_T_HEADS = 3,
+    M3R_T_H2D = 4,
+    M3R_T_D2H = 5,
+    M3R_T_INFERENCE = 6, /* device time of the forward pass (max over devices) */
+    M3R_T_TOTAL = 7,     /* host wall time of the call */
+    M3R_T_COUNT = 8
+};
+
+/* Opaque engine: weights replicated on every device of the config. */
+typedef struct m3r_engine m3r_engine;
+
+/* ---- module-level queries: replace _cuda.is_available / get_device_name /
+ *      get_compute_capability (mast3r_runtime/backends/__init__.py:46-51, 129-138). */
+int m3r_version(void);
+const char* m3r_global_error(void);
+int m3r_device_count(int* count);
+int m3r_device_info(int device, char* name, int name_len, int* cc_major, int* cc_minor);
+
+/* ---- engine lifetime: replaces CUDAEngine(variant, resolution, precision, num_threads)
+ *      (mast3r_runtime/backends/__init__.py:208-213; reference stub csrc/cuda/bindings.cpp:15-36). */
+int m3r_create(const m3r_config* cfg, m3r_engine** out);
+void m3r_destroy(m3r_engine* engine);
+const char* m3r_last_error(const m3r_engine* engine);
+
+/* ---- load(path): replaces native.load(str(model_path)) (native_wrapper.py:57);
+ *      reads a unified safetensors checkpoint in the CroCo key layout. */
+int m3r_load(m3r_engine* engine, const char* safetensors_path);
+/* is_ready(): native_wrapper.py:45 */
+int m3r_is_ready(const m3r_engine* engine);
+
+/* ---- infer(img1, img2): replaces native.infer (native_wrapper.py:84-97).
+ * img1, img2: [n_pairs, H, W, 3] uint8.  Outputs (caller-owned, fp32):
+ * pts3d_* [n_pairs, H, W, 3], desc_* [n_pairs, H, W, desc_dim], conf_* [n_pairs, H, W].
+ * timing_ms: M3R_T_COUNT floats, or NULL.  Pairs are sharded over the devices. */
+int m3r_infer(m3r_engine* engine, const uint8_t* img1, const uint8_t* img2, int n_pairs, float* pts3d_1,
+              float* pts3d_2, float* desc_1, float* desc_2, float* conf_1, float* conf_2, float* timing_ms);
+
+/* ---- match(desc_1, desc_2, top_k, reciprocal, confidence_threshold): replaces
+ * native.match (native_wrapper.py:122-128) with the semantics of
+ * csrc/cpu/matching.cpp:85-237.  desc_*: [height*width, desc_dim] fp32.
+ * Outputs hold min(top_k, height*width) entries: idx_* int64, confidence fp32,
+ * pts2d_* [n, 2] fp32 (x, y).  With more than top_k matches the result is ordered
+ * by confidence descending (idx_1 ascending on ties), otherwise by idx_1.
+ * Rows of desc_1 are sharded over the engine's devices. timing_ms as m3r_infer. */
+int m3r_match(m3r_engine* engine, const float* desc_1, const float* desc_2, int height, int width, int desc_dim,
+              int top_k, int reciprocal, float confidence_threshold, int64_t* idx_1, int64_t* idx_2,
+              float* confidence, float* pts2d_1, float* pts2d_2, int* n_matches, float* timing_ms);
+
+/* ---- device-resident stages of m3r_infer (throughput measurement and callers that
+ * keep outputs on the device): copy inputs in, run, copy outputs out. */
+int m3r_stage_inputs(m3r_engine* engine, const uint8_t* img1, const uint8_t* img2, int n_pairs);
+int m3r_run_resident(m3r_engine* engine, int n_pairs, float* device_ms);
+int m3r_fetch_outputs(m3r_engine* engine, int n_pairs, float* pts3d_1, float* pts3d_2, float* desc_1,
+                      float* desc_2, float* conf_1, float* conf_2);
+
+/* Per-kernel-family device time of the last m3r_run_resident / m3r_infer when
+ * profiling is on (CUDA events around every launch):
+ * out[0] GEMM ms, out[1] GEMM FLOP, out[2] attention ms, out[3] attention FLOP,
+ * out[4] other kernels ms, out[5] GEMM launches, out[6] attention launches,
+ * out[7] other launches.  Values are for device 0 of the engine. */
+int m3r_set_profiling(m3r_engine* engine, int on);
+int m3r_get_profile(const m3r_engine* engine, double* out8);
+
+/* Pinned host memory for zero-staging transfers. */
+void* m3r_host_alloc(size_t bytes);
+void m3r_host_free(void* p);
+
+/* ---- test / measurement entry points (no reference counterpart; they expose
+ * single kernels of this backend for parity tests and kernel timing). ---- */
+
+/* Isolated attention (bf16 bits as uint16): O[s, t, h*64] = softmax(Q K^T * scale) V,
+ * Q [s, h, nq, 64], K/V [s, h, nk, 64].  *kernel_ms gets the mean device time over
+ * `iters` launches (>= 1) when not NULL. */
+int m3r_attention_fwd(int device, const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out,
+                      int n_seq, int heads, int nq, int nk, float scale, int iters, float* kernel_ms);
+
+/* GEMM C[M, N] = A[M, K] * W[N, K]^T + bias (bf16 bits in, fp32 out). */
+int m3r_gemm_test(int device, const uint16_t* a, const uint16_t* w, const float* bias, float* c, int M, int N,
+                  int K, int bn, int iters, float* kernel_ms);
+
+/* 3x3 conv, stride 1, pad 1, NHWC: x [n, h, w, c] bf16 bits, w [cout, 9 * cpad]
+ * (tap-major, channel padded to cpad = ceil(c / 64) * 64) -> y [n, h, w, cout] fp32
+ * (bias added). */
+int m3r_conv3_test(int device, const uint16_t* x, const uint16_t* w, const float* bias, float* y, int n, int h,
+                   int wd, int c, int cout, int bn);
+
+/* Matcher arg-max only: nn_12 [n1] and nn_21 [n2] (lowest index on ties) of the
+ * normalised descriptors, and the row maxima best_12 [n1]. */
+int m3r_match_nn(int device, const float* desc_1, const float* desc_2, int64_t n1, int64_t n2, int desc_dim,
+                 int32_t* nn_12, int32_t* nn_21, float* best_12, float* kernel_ms);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* M3R_CUDA_H */

@@ -1,0 +1,281 @@
+// Non-causal flash attention on tcgen05 (sm_100a), head dim 64, bf16 in/out,
+// fp32 softmax statistics and accumulation.
+//
+//   Q, K, V : head-major [seq, head, tok, 64] bf16 (written by the QKV GEMM epilogue)
+//   O       : token-major [seq, tok, head * 64] bf16 (the A operand of the output projection)
+//
+// One CTA = 128 query rows of one (seq, head).  192 threads: warps 0-3 softmax
+// (thread = query row = TMEM lane), warp 4 TMA producer, warp 5 MMA issuer.
+// TMEM (256 columns, so two CTAs fit on an SM): S = Q K^T in [0,128), P (bf16,
+// two per column) in [128,192), O in [192,256).  S uses an SS MMA; O += P V uses
+// a TS MMA with P from TMEM and V read MN-major straight from its TMA tile.
+// K/V tiles of 128 keys are double-buffered; keys beyond Nk are masked to -inf
+// (their V rows are zero-filled by TMA).  Scores never touch HBM.
+//
+// Semantics: softmax(Q K^T * scale) V per head, as
+// backends/python/croco_encoder.py:80-85 and croco_decoder.py:76-82, 171-177.
+#include <cmath>
+#include <mutex>
+
+#include "attention.h"
+#include "common.cuh"
+
+namespace m3r {
+
+namespace {
+
+constexpr int kTile = 128;
+constexpr int kTileBytes = kTile * 64 * 2;  // 16 KB: 128 rows x 128 bytes
+constexpr int kSmemBytes = 5 * kTileBytes + 1024 + 256;
+constexpr uint32_t kColS = 0, kColP = 128, kColO = 192, kTmemCols = 256;
+
+struct AttnParams {
+    int nq, nk, heads, n_kv_tiles;
+    float scale_log2;  // scale * log2(e)
+    __nv_bfloat16* out;
+    int* err;          // device status word (bounded-wait timeouts)
+};
+
+__global__ void __launch_bounds__(192, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
+                    const __grid_constant__ CUtensorMap mapV, const __grid_constant__ AttnParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem;
+    uint8_t* sK = smem + kTileBytes;       // 2 stages
+    uint8_t* sV = smem + 3 * kTileBytes;   // 2 stages
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 5 * kTileBytes);
+    uint64_t* q_full = bars + 0;
+    uint64_t* kv_full = bars + 1;   // [2]
+    uint64_t* kv_empty = bars + 3;  // [2]
+    uint64_t* s_full = bars + 5;
+    uint64_t* s_empty = bars + 6;
+    uint64_t* p_full = bars + 7;
+    uint64_t* o_done = bars + 8;
+    uint64_t* mma_done = bars + 9;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int q0 = blockIdx.x * kTile;
+    const int head = blockIdx.y;
+    const int seq = blockIdx.z;
+    const int plane = seq * p.heads + head;
+    const int nkv = p.n_kv_tiles;
+
+    if (warp == 4 && lane == 0) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&kv_full[s], 1);
+            mbar_init(&kv_empty[s], 1);
+        }
+        mbar_init(s_full, 1);
+        mbar_init(s_empty, 128);
+        mbar_init(p_full, 128);
+        mbar_init(o_done, 1);
+        mbar_init(mma_done, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tmap(&mapQ);
+        prefetch_tmap(&mapK);
+        prefetch_tmap(&mapV);
+    }
+    if (warp == 5) tmem_alloc(tmem_slot, kTmemCols);
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            mbar_arrive_expect_tx(q_full, kTileBytes);
+            tma_load_3d(sQ, &mapQ, q_full, 0, q0, plane);
+            int issued = 0;
+            bool ok = true;
+            for (int j = 0; j < nkv; ++j) {
+                const int st = j & 1;
+                const uint32_t ph = (j >> 1) & 1;
+                if (!mbar_wait(&kv_empty[st], ph ^ 1, abort_flag, kDevTimeoutProducer, p.err)) { ok = false; break; }
+                mbar_arrive_expect_tx(&kv_full[st], 2 * kTileBytes);
+                tma_load_3d(sK + st * kTileBytes, &mapK, &kv_full[st], 0, j * kTile, plane);
+                tma_load_3d(sV + st * kTileBytes, &mapV, &kv_full[st], 0, j * kTile, plane);
+                issued = j + 1;
+            }
+            if (!ok) {
+                volatile int dummy = 0;
+                mbar_wait(q_full, 0, &dummy, kDevTimeoutProducer, p.err);
+                for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j)
+                    mbar_wait(&kv_full[j & 1], (j >> 1) & 1, &dummy, kDevTimeoutProducer, p.err);
+            }
+        }
+    } else if (warp == 5) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc_s = idesc_bf16(128, 128, false, false);
+            constexpr uint32_t idesc_o = idesc_bf16(128, 64, false, true);
+            const uint32_t q_addr = smem_u32(sQ);
+            bool ok = mbar_wait(q_full, 0, abort_flag, kDevTimeoutMma, p.err);
+            for (int j = 0; j < nkv && ok; ++j) {
+                const int st = j & 1;
+                const uint32_t ph = (j >> 1) & 1;
+                if (!mbar_wait(&kv_full[st], ph, abort_flag, kDevTimeoutMma, p.err)) { ok = false; break; }
+                if (j > 0 && !mbar_wait(s_empty, (j - 1) & 1, abort_flag, kDevTimeoutMma, p.err)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t k_addr = smem_u32(sK + st * kTileBytes);
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    mma_bf16_ss(tmem + kColS, umma_desc_sw128(q_addr + k * 32, 16, 1024),
+                                umma_desc_sw128(k_addr + k * 32, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
+                mma_commit(s_full);
+                if (!mbar_wait(p_full, j & 1, abort_flag, kDevTimeoutMma, p.err)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t v_addr = smem_u32(sV + st * kTileBytes);
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    mma_bf16_ts(tmem + kColO, tmem + kColP + k * 8, umma_desc_sw128(v_addr + k * 2048, 16384, 1024),
+                                idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+                mma_commit(&kv_empty[st]);
+                mma_commit(o_done);
+            }
+            mma_commit(mma_done);
+            volatile int dummy = 0;
+            mbar_wait(mma_done, 0, &dummy, kDevTimeoutMma, p.err);
+        }
+    } else {
+        // ------------------------------------------------------------ softmax (warps 0-3)
+        const int r = warp * 32 + lane;
+        const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+        const uint32_t tS = tmem + lane_base + kColS;
+        const uint32_t tP = tmem + lane_base + kColP;
+        const uint32_t tO = tmem + lane_base + kColO;
+        float m_run = -INFINITY, l_run = 0.0f;
+        bool ok = true;
+        for (int j = 0; j < nkv; ++j) {
+            if (!mbar_wait(s_full, j & 1, abort_flag, kDevTimeoutSoftmax, p.err)) { ok = false; break; }
+            tc_fence_after();
+            const int valid = p.nk - j * kTile;  // keys valid in this tile (>= 1)
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t v[32];
+                tmem_ld32(tS + c * 32, v);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    if (c * 32 + i < valid) mx = fmaxf(mx, __uint_as_float(v[i]));
+            }
+            const float m_new = fmaxf(m_run, mx * p.scale_log2);
+            const float alpha = ex2_approx(m_run - m_new);
+            if (j > 0) {
+                // P buffer free and O stable once PV of the previous tile is done
+                if (!mbar_wait(o_done, (j - 1) & 1, abort_flag, kDevTimeoutSoftmax, p.err)) { ok = false; break; }
+                tc_fence_after();
+            }
+            float rowsum = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t v[32];
+                tmem_ld32(tS + c * 32, v);
+                tmem_wait_ld();
+                uint32_t pk[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int c0 = c * 32 + 2 * i;
+                    const float p0 = c0 < valid ? ex2_approx(__uint_as_float(v[2 * i]) * p.scale_log2 - m_new) : 0.0f;
+                    const float p1 = c0 + 1 < valid ? ex2_approx(__uint_as_float(v[2 * i + 1]) * p.scale_log2 - m_new) : 0.0f;
+                    rowsum += p0 + p1;
+                    pk[i] = pack_bf16x2(p0, p1);
+                }
+                asm volatile(
+                    "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+                    "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(tP + c * 16),
+                    "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3]), "r"(pk[4]), "r"(pk[5]), "r"(pk[6]), "r"(pk[7]),
+                    "r"(pk[8]), "r"(pk[9]), "r"(pk[10]), "r"(pk[11]), "r"(pk[12]), "r"(pk[13]), "r"(pk[14]),
+                    "r"(pk[15]));
+            }
+            tc_fence_before();
+            mbar_arrive(s_empty);
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t o[32];
+                    tmem_ld32(tO + c * 32, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                    tmem_st32(tO + c * 32, o);
+                }
+            }
+            tmem_wait_st();
+            l_run = l_run * alpha + rowsum;
+            m_run = m_new;
+            tc_fence_before();
+            mbar_arrive(p_full);
+        }
+        if (ok && mbar_wait(o_done, (nkv - 1) & 1, abort_flag, kDevTimeoutSoftmax, p.err)) {
+            tc_fence_after();
+            uint32_t o[2][32];
+            tmem_ld32(tO, o[0]);
+            tmem_ld32(tO + 32, o[1]);
+            tmem_wait_ld();
+            const int q = q0 + r;
+            if (q < p.nq) {
+                const float inv = 1.0f / l_run;
+                __nv_bfloat16* dst = p.out + (static_cast<long long>(seq) * p.nq + q) * (p.heads * 64) + head * 64;
+                uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int qq = 0; qq < 4; ++qq) {
+                        uint4 u;
+                        u.x = pack_bf16x2(__uint_as_float(o[h][qq * 8 + 0]) * inv, __uint_as_float(o[h][qq * 8 + 1]) * inv);
+                        u.y = pack_bf16x2(__uint_as_float(o[h][qq * 8 + 2]) * inv, __uint_as_float(o[h][qq * 8 + 3]) * inv);
+                        u.z = pack_bf16x2(__uint_as_float(o[h][qq * 8 + 4]) * inv, __uint_as_float(o[h][qq * 8 + 5]) * inv);
+                        u.w = pack_bf16x2(__uint_as_float(o[h][qq * 8 + 6]) * inv, __uint_as_float(o[h][qq * 8 + 7]) * inv);
+                        d4[h * 4 + qq] = u;
+                    }
+            }
+        }
+    }
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+}  // namespace
+
+void attention_fwd(cudaStream_t s, const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v,
+                   __nv_bfloat16* out, int n_seq, int heads, int nq, int nk, float scale, int* err) {
+    M3R_REQUIRE(n_seq > 0 && heads > 0 && nq > 0 && nk > 0, "attention: bad shape");
+    static std::once_flag once;
+    std::call_once(once, [] {
+        int ndev = 0, cur = 0;
+        M3R_CUDA(cudaGetDeviceCount(&ndev));
+        M3R_CUDA(cudaGetDevice(&cur));
+        for (int d = 0; d < ndev; ++d) {
+            M3R_CUDA(cudaSetDevice(d));
+            M3R_CUDA(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+        }
+        M3R_CUDA(cudaSetDevice(cur));
+    });
+    const CUtensorMap mq = tmap_bf16_3d_rows64(q, nq, static_cast<uint64_t>(n_seq) * heads, kTile);
+    const CUtensorMap mk = tmap_bf16_3d_rows64(k, nk, static_cast<uint64_t>(n_seq) * heads, kTile);
+    const CUtensorMap mv = tmap_bf16_3d_rows64(v, nk, static_cast<uint64_t>(n_seq) * heads, kTile);
+    AttnParams p;
+    p.nq = nq;
+    p.nk = nk;
+    p.heads = heads;
+    p.n_kv_tiles = (nk + kTile - 1) / kTile;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.out = out;
+    p.err = err;
+    dim3 grid((nq + kTile - 1) / kTile, heads, n_seq);
+    M3R_REQUIRE(n_seq <= 65535 && heads <= 65535, "attention: grid too large");
+    attn_fwd_kernel<<<grid, 192, kSmemBytes, s>>>(mq, mk, mv, p);
+    M3R_CUDA(cudaGetLastError());
+}
+
+}  // namespace m3r

@@ -1,0 +1,965 @@
+// Two-view forward pass on one device and its multi-device orchestration.
+//
+// Token layout: all 2n images of a launch (view 1 pairs 0..n-1, then view 2
+// pairs 0..n-1) are rows of one [2n * N, D] activation matrix, so the shared-
+// weight encoder runs as single GEMMs over every token.  The decoder runs per
+// view (different weights, dec_blocks / dec_blocks2), each view's rows being a
+// contiguous half.  Residual streams stay fp32; GEMM operands are bf16.
+//
+// Reference semantics: encoder croco_encoder.py:245-283, decoder
+// croco_decoder.py:395-434, heads mpsgraph_engine.mm:383-437 (see oracle/model.py
+// for the restatement the tests check against).
+#include "engine.h"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <functional>
+#include <thread>
+
+#include "attention.h"
+#include "gemm.h"
+#include "kernels.h"
+#include "safetensors.h"
+
+namespace m3r {
+
+// ---------------------------------------------------------------------------- dims
+Dims Dims::from(const m3r_config& c) {
+    Dims d;
+    d.patch = c.patch;
+    d.enc_dim = c.enc_dim;
+    d.enc_depth = c.enc_depth;
+    d.enc_heads = c.enc_heads;
+    d.enc_mlp = c.enc_mlp;
+    d.dec_dim = c.dec_dim;
+    d.dec_depth = c.dec_depth;
+    d.dec_heads = c.dec_heads;
+    d.dec_mlp = c.dec_mlp;
+    d.lf_hidden = c.lf_hidden;
+    d.desc_dim = c.desc_dim;
+    d.H = c.img_h;
+    d.W = c.img_w;
+    M3R_REQUIRE(d.patch > 0 && d.H > 0 && d.W > 0 && d.H % d.patch == 0 && d.W % d.patch == 0,
+                "image size must be a positive multiple of the patch size");
+    d.hg = d.H / d.patch;
+    d.wg = d.W / d.patch;
+    d.ntok = d.hg * d.wg;
+    d.kpad = (3 * d.patch * d.patch + 63) / 64 * 64;
+    d.hook1 = d.dec_depth / 2 - 1;
+    d.hook2 = d.dec_depth * 3 / 4 - 1;
+    d.dpt_h = 16 * d.hg;
+    d.dpt_w = 16 * d.wg;
+    M3R_REQUIRE(d.enc_heads > 0 && d.enc_dim == 64 * d.enc_heads, "encoder head dim must be 64");
+    M3R_REQUIRE(d.dec_heads > 0 && d.dec_dim == 64 * d.dec_heads, "decoder head dim must be 64");
+    M3R_REQUIRE(d.enc_dim % 128 == 0 && d.dec_dim % 128 == 0, "model dims must be multiples of 128");
+    M3R_REQUIRE(d.enc_mlp % 64 == 0 && d.dec_mlp % 64 == 0 && d.lf_hidden % 64 == 0, "MLP widths must be multiples of 64");
+    M3R_REQUIRE(d.enc_dim <= 1024 && d.dec_dim <= 1024, "model dims above 1024 are not supported");
+    M3R_REQUIRE(d.desc_dim == 24, "descriptor dim must be 24");
+    M3R_REQUIRE((d.patch * d.patch) % 8 == 0 || (d.patch * d.patch) % 4 == 0, "unsupported patch size");
+    M3R_REQUIRE(d.hg % 2 == 0 && d.wg % 2 == 0, "patch grid must have even height and width");
+    M3R_REQUIRE(d.dec_depth >= 4, "decoder depth must be >= 4");
+    return d;
+}
+
+DeviceGuard::DeviceGuard(int dev) {
+    M3R_CUDA(cudaGetDevice(&prev));
+    M3R_CUDA(cudaSetDevice(dev));
+}
+DeviceGuard::~DeviceGuard() { cudaSetDevice(prev); }
+
+// ---------------------------------------------------------------------------- host weight prep
+namespace {
+
+uint16_t f2bf(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x7FFFFFu)) return 0x7FC0;
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return static_cast<uint16_t>(u >> 16);
+}
+
+struct HostLin {
+    std::vector<uint16_t> w;  // bf16 bits [out, in]
+    std::vector<float> b;     // may be empty
+    int out = 0, in = 0;
+};
+
+HostLin to_bf16(const std::vector<float>& w, int out, int in, std::vector<float> b = {}) {
+    HostLin h;
+    h.out = out;
+    h.in = in;
+    h.w.resize(static_cast<size_t>(out) * in);
+    for (size_t i = 0; i < h.w.size(); ++i) h.w[i] = f2bf(w[i]);
+    h.b = std::move(b);
+    return h;
+}
+
+// conv weight [co, ci, 3, 3] -> [co, 9, cpad] tap-major, zero channel padding
+HostLin conv3_weights(const std::vector<float>& w, int co, int ci, std::vector<float> b = {}) {
+    const int cpad = (ci + 63) / 64 * 64;
+    std::vector<float> t(static_cast<size_t>(co) * 9 * cpad, 0.0f);
+    for (int o = 0; o < co; ++o)
+        for (int c = 0; c < ci; ++c)
+            for (int tap = 0; tap < 9; ++tap)
+                t[(static_cast<size_t>(o) * 9 + tap) * cpad + c] = w[(static_cast<size_t>(o) * ci + c) * 9 + tap];
+    return to_bf16(t, co, 9 * cpad, std::move(b));
+}
+
+// ConvTranspose2d weight [ci, co, s, s] -> B [(dy*s+dx)*co + o, ci]
+HostLin convt_weights(const std::vector<float>& w, int ci, int co, int s, std::vector<float> b) {
+    std::vector<float> t(static_cast<size_t>(s) * s * co * ci);
+    for (int c = 0; c < ci; ++c)
+        for (int o = 0; o < co; ++o)
+            for (int dy = 0; dy < s; ++dy)
+                for (int dx = 0; dx < s; ++dx)
+                    t[(static_cast<size_t>((dy * s + dx) * co + o)) * ci + c] =
+                        w[((static_cast<size_t>(c) * co + o) * s + dy) * s + dx];
+    return to_bf16(t, s * s * co, ci, std::move(b));
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------- device
+class Device {
+public:
+    Device(int dev, const Dims& d, int max_pairs) : dev_(dev), d_(d), max_pairs_(max_pairs) {
+        DeviceGuard g(dev_);
+        M3R_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+        err_ = static_cast<int*>(alloc(sizeof(int)));
+        M3R_CUDA(cudaMemset(err_, 0, sizeof(int)));
+        for (int i = 0; i < 8; ++i) M3R_CUDA(cudaEventCreate(&stage_ev_[i]));
+        alloc_activations();
+    }
+    ~Device() {
+        cudaSetDevice(dev_);
+        if (stream_) cudaStreamSynchronize(stream_);
+        for (auto& e : prof_ev_) cudaEventDestroy(e);
+        for (int i = 0; i < 8; ++i) cudaEventDestroy(stage_ev_[i]);
+        for (void* p : allocs_) cudaFree(p);
+        if (stream_) cudaStreamDestroy(stream_);
+    }
+
+    int dev() const { return dev_; }
+    cudaStream_t stream() const { return stream_; }
+
+    void* alloc(size_t bytes) {
+        void* p = nullptr;
+        M3R_CUDA(cudaMalloc(&p, bytes > 0 ? bytes : 16));
+        allocs_.push_back(p);
+        return p;
+    }
+    template <class T>
+    T* upload(const std::vector<T>& v) {
+        if (v.empty()) return nullptr;
+        T* p = static_cast<T*>(alloc(v.size() * sizeof(T)));
+        M3R_CUDA(cudaMemcpy(p, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice));
+        return p;
+    }
+    Lin upload(const HostLin& h) {
+        Lin l;
+        l.out = h.out;
+        l.in = h.in;
+        l.w = reinterpret_cast<__nv_bfloat16*>(upload(h.w));
+        l.b = upload(h.b);
+        return l;
+    }
+    Norm upload_norm(const std::vector<float>& g, const std::vector<float>& b) { return Norm{upload(g), upload(b)}; }
+
+    // ------------------------------------------------------------ weights (filled by Engine::load)
+    Lin patch;
+    std::vector<EncBlock> enc;
+    Norm enc_norm;
+    Lin dec_embed;
+    std::vector<DecBlock> dec[2];
+    Norm dec_norm;
+    Head head[2];
+    float* rope_cos = nullptr;
+    float* rope_sin = nullptr;
+
+    // ------------------------------------------------------------ activations
+    uint8_t* img = nullptr;
+    __nv_bfloat16 *patches = nullptr, *xn = nullptr, *yn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr,
+                  *ao = nullptr, *h = nullptr, *enc_out = nullptr, *hook1 = nullptr, *hook2 = nullptr,
+                  *dec_out = nullptr;
+    float *xenc = nullptr, *xdec = nullptr, *encp = nullptr;
+    __nv_bfloat16 *f0a = nullptr, *f0 = nullptr, *rn0 = nullptr, *f1a = nullptr, *f1 = nullptr, *rn1 = nullptr,
+                  *f2 = nullptr, *rn2 = nullptr, *f3a = nullptr, *col3 = nullptr, *f3 = nullptr, *rn3 = nullptr,
+                  *fused = nullptr, *up1 = nullptr, *hd0 = nullptr, *up2 = nullptr, *lf1 = nullptr;
+    float* out4 = nullptr;
+    float *o_pts = nullptr, *o_conf = nullptr, *o_desc = nullptr;
+    MatchWorkspace mws;
+
+    int staged = 0;  // pairs staged on this device
+
+    void alloc_activations() {
+        const long long P = max_pairs_;
+        const long long T = 2 * P * d_.ntok, Tv = P * d_.ntok;
+        const long long Dm = std::max(d_.enc_dim, d_.dec_dim);
+        const long long Hm = std::max(d_.enc_mlp, d_.dec_mlp);
+        const long long hg = d_.hg, wg = d_.wg;
+        auto bf = [&](long long n) { return static_cast<__nv_bfloat16*>(alloc(n * 2)); };
+        auto f32 = [&](long long n) { return static_cast<float*>(alloc(n * 4)); };
+        img = static_cast<uint8_t*>(alloc(2 * P * d_.H * d_.W * 3));
+        patches = bf(T * d_.kpad);
+        xenc = f32(T * d_.enc_dim);
+        xdec = f32(T * d_.dec_dim);
+        encp = f32(T * d_.dec_dim);
+        xn = bf(T * Dm);
+        yn = bf(T * Dm);
+        q = bf(T * Dm);
+        k = bf(T * Dm);
+        v = bf(T * Dm);
+        ao = bf(T * Dm);
+        h = bf(T * Hm);
+        enc_out = bf(T * d_.enc_dim);
+        hook1 = bf(T * d_.dec_dim);
+        hook2 = bf(T * d_.dec_dim);
+        dec_out = bf(T * d_.dec_dim);
+        // DPT / local features, one view at a time
+        f0a = bf(Tv * 96);
+        f0 = bf(P * 16 * hg * wg * 96);
+        rn0 = bf(P * 16 * hg * wg * 256);
+        f1a = bf(Tv * 192);
+        f1 = bf(P * 4 * hg * wg * 192);
+        rn1 = bf(P * 4 * hg * wg * 256);
+        f2 = bf(Tv * 384);
+        rn2 = bf(P * hg * wg * 256);
+        f3a = bf(Tv * 768);
+        col3 = bf(P * (hg / 2) * (wg / 2) * 9 * 768);
+        f3 = bf(P * (hg / 2) * (wg / 2) * 768);
+        rn3 = bf(P * (hg / 2) * (wg / 2) * 256);
+        fused = bf(P * 16 * hg * wg * 256);
+        up1 = bf(P * 64 * hg * wg * 256);
+        hd0 = bf(P * 64 * hg * wg * 128);
+        up2 = bf(P * 256 * hg * wg * 128);
+        out4 = f32(P * 256 * hg * wg * 4);
+        lf1 = bf(Tv * d_.lf_hidden);
+        o_pts = f32(2 * P * d_.H * d_.W * 3);
+        o_conf = f32(2 * P * d_.H * d_.W);
+        o_desc = f32(2 * P * d_.H * d_.W * d_.desc_dim);
+    }
+
+    // ------------------------------------------------------------ profiling
+    struct Prof {
+        double ms[3] = {0, 0, 0};
+        double flops[3] = {0, 0, 0};
+        long launches[3] = {0, 0, 0};
+    } prof;
+    bool profiling = false;
+    std::vector<cudaEvent_t> prof_ev_;
+    std::vector<std::pair<int, double>> prof_rec_;  // (category, flops) per event pair
+
+    template <class F>
+    void launch(int cat, double flops, F&& fn) {
+        if (!profiling) {
+            fn();
+            return;
+        }
+        const size_t i = prof_rec_.size();
+        while (prof_ev_.size() < 2 * (i + 1)) {
+            cudaEvent_t e;
+            M3R_CUDA(cudaEventCreate(&e));
+            prof_ev_.push_back(e);
+        }
+        M3R_CUDA(cudaEventRecord(prof_ev_[2 * i], stream_));
+        fn();
+        M3R_CUDA(cudaEventRecord(prof_ev_[2 * i + 1], stream_));
+        prof_rec_.push_back({cat, flops});
+    }
+    void collect_profile() {
+        prof = Prof();
+        for (size_t i = 0; i < prof_rec_.size(); ++i) {
+            float ms = 0;
+            M3R_CUDA(cudaEventElapsedTime(&ms, prof_ev_[2 * i], prof_ev_[2 * i + 1]));
+            const int c = prof_rec_[i].first;
+            prof.ms[c] += ms;
+            prof.flops[c] += prof_rec_[i].second;
+            prof.launches[c] += 1;
+        }
+        prof_rec_.clear();
+    }
+
+    // ------------------------------------------------------------ building blocks
+    static constexpr int kGemm = 0, kAttn = 1, kOther = 2;
+
+    int bn_for(int n) const { return (n % 256 == 0) ? 256 : 128; }
+
+    GemmParams gp() const {
+        GemmParams p = gemm_params();
+        p.err = err_;
+        return p;
+    }
+
+    void linear(const __nv_bfloat16* A, long long M, const Lin& L, int epi, void* out, long long ldo, int act = ACT_NONE,
+                const float* resid = nullptr, int bn = 0) {
+        GemmParams p = gp();
+        p.bias = L.b;
+        p.act = act;
+        p.out = out;
+        p.ldo = ldo;
+        p.resid = resid;
+        p.ldr = ldo;
+        const int b = bn ? bn : bn_for(L.out);
+        launch(kGemm, 2.0 * M * L.out * L.in, [&] { gemm_rows(stream_, b, epi, A, L.in, static_cast<int>(M), L.in, L.w, L.in, L.out, p); });
+    }
+
+    // head-major scatter of [M, nsec * D] into up to three [seqs, heads, ntok, 64] buffers
+    void linear_heads(const __nv_bfloat16* A, long long M, const Lin& L, int D, __nv_bfloat16* o0, int r0,
+                      __nv_bfloat16* o1, int r1, __nv_bfloat16* o2, int r2) {
+        GemmParams p = gp();
+        p.bias = L.b;
+        p.sec_len = D;
+        p.n_tok = d_.ntok;
+        p.grid_w = d_.wg;
+        p.sec_out[0] = o0;
+        p.sec_out[1] = o1;
+        p.sec_out[2] = o2;
+        p.sec_rope[0] = r0;
+        p.sec_rope[1] = r1;
+        p.sec_rope[2] = r2;
+        p.rope_cos = rope_cos;
+        p.rope_sin = rope_sin;
+        const int b = (D % 256 == 0) ? 256 : 128;
+        launch(kGemm, 2.0 * M * L.out * L.in,
+               [&] { gemm_rows(stream_, b, EPI_HEADS, A, L.in, static_cast<int>(M), L.in, L.w, L.in, L.out, p); });
+    }
+
+    void attn(const __nv_bfloat16* qq, const __nv_bfloat16* kk, const __nv_bfloat16* vv, __nv_bfloat16* out, int seqs,
+              int heads) {
+        const double fl = 4.0 * seqs * heads * static_cast<double>(d_.ntok) * d_.ntok * 64;
+        launch(kAttn, fl, [&] { attention_fwd(stream_, qq, kk, vv, out, seqs, heads, d_.ntok, d_.ntok, 0.125f, err_); });
+    }
+
+    void ln(const float* x, long long rows, int D, const Norm& n, __nv_bfloat16* y) {
+        launch(kOther, 0, [&] { layernorm(stream_, x, static_cast<int>(rows), D, n.g, n.b, y); });
+    }
+
+    void conv3(const __nv_bfloat16* X, int n, int hh, int ww, int c, const Lin& L, int epi, void* out, int act,
+               int bn, const float* w4 = nullptr, const float* b4 = nullptr) {
+        GemmParams p = gp();
+        p.bias = L.b;
+        p.act = act;
+        p.out = out;
+        p.ldo = L.out;
+        p.w4 = w4;
+        p.b4 = b4;
+        const double fl = 2.0 * n * hh * ww * static_cast<double>(L.out) * 9 * c;
+        launch(kGemm, fl, [&] { gemm_conv3(stream_, bn, epi, X, n, hh, ww, c, c, L.w, L.out, p); });
+    }
+
+    // ------------------------------------------------------------ forward
+    void forward(int n, float* stage_ms) {
+        DeviceGuard g(dev_);
+        const Dims& d = d_;
+        const long long N = d.ntok;
+        const long long T = 2LL * n * N;
+        const long long Tv = static_cast<long long>(n) * N;
+        profiling_reset();
+        M3R_CUDA(cudaEventRecord(stage_ev_[0], stream_));
+
+        // patch embedding (+ ImageNet normalisation fused into the im2col)
+        launch(kOther, 0, [&] { patch_im2col(stream_, img, 2 * n, d.H, d.W, d.patch, d.kpad, patches); });
+        {
+            GemmParams p = gp();
+            p.bias = patch.b;
+            p.out = xenc;
+            p.ldo = d.enc_dim;
+            launch(kGemm, 2.0 * T * d.enc_dim * 3 * d.patch * d.patch,
+                   [&] { gemm_rows(stream_, bn_for(d.enc_dim), EPI_F32, patches, d.kpad, static_cast<int>(T), d.kpad, patch.w, d.kpad, d.enc_dim, p); });
+        }
+        M3R_CUDA(cudaEventRecord(stage_ev_[1], stream_));
+
+        // encoder (croco_encoder.py:142-168), both views of every pair in one pass
+        const int De = d.enc_dim;
+        for (int i = 0; i < d.enc_depth; ++i) {
+            const EncBlock& B = enc[i];
+            ln(xenc, T, De, B.n1, xn);
+            linear_heads(xn, T, B.qkv, De, q, 1, k, 1, v, 0);
+            attn(q, k, v, ao, 2 * n, d.enc_heads);
+            linear(ao, T, B.proj, EPI_F32_RESID, xenc, De, ACT_NONE, xenc);
+            ln(xenc, T, De, B.n2, xn);
+            linear(xn, T, B.fc1, EPI_BF16, h, d.enc_mlp, ACT_GELU);
+            linear(h, T, B.fc2, EPI_F32_RESID, xenc, De, ACT_NONE, xenc);
+        }
+        ln(xenc, T, De, enc_norm, enc_out);
+        M3R_CUDA(cudaEventRecord(stage_ev_[2], stream_));
+
+        // decoder (croco_decoder.py:395-434)
+        const int Dd = d.dec_dim;
+        linear(enc_out, T, dec_embed, EPI_F32, encp, Dd);
+        M3R_CUDA(cudaMemcpyAsync(xdec, encp, sizeof(float) * T * Dd, cudaMemcpyDeviceToDevice, stream_));
+        for (int i = 0; i < d.dec_depth; ++i) {
+            for (int view = 0; view < 2; ++view) {
+                const DecBlock& B = dec[view][i];
+                float* xv = xdec + view * Tv * Dd;
+                const float* yo = encp + (1 - view) * Tv * Dd;
+                __nv_bfloat16* xnv = xn + view * Tv * Dd;
+                __nv_bfloat16* aov = ao + view * Tv * Dd;
+                // self attention
+                ln(xv, Tv, Dd, B.n1, xnv);
+                linear_heads(xnv, Tv, B.qkv, Dd, q, 1, k, 1, v, 0);
+                attn(q, k, v, aov, n, d.dec_heads);
+                linear(aov, Tv, B.proj, EPI_F32_RESID, xv, Dd, ACT_NONE, xv);
+                // cross attention: queries from this view, keys/values from the other view's projected encoder output
+                ln(xv, Tv, Dd, B.n2, xnv);
+                linear_heads(xnv, Tv, B.q, Dd, q, 1, nullptr, 0, nullptr, 0);
+                ln(yo, Tv, Dd, B.ny, yn);
+                linear_heads(yn, Tv, B.kv, Dd, k, 1, v, 0, nullptr, 0);
+                attn(q, k, v, aov, n, d.dec_heads);
+                linear(aov, Tv, B.cproj, EPI_F32_RESID, xv, Dd, ACT_NONE, xv);
+                // MLP
+                ln(xv, Tv, Dd, B.n3, xnv);
+                linear(xnv, Tv, B.fc1, EPI_BF16, h, d.dec_mlp, ACT_GELU);
+                linear(h, Tv, B.fc2, EPI_F32_RESID, xv, Dd, ACT_NONE, xv);
+            }
+            if (i == d.hook1) launch(kOther, 0, [&] { cast_bf16(stream_, xdec, T * Dd, hook1); });
+            if (i == d.hook2) launch(kOther, 0, [&] { cast_bf16(stream_, xdec, T * Dd, hook2); });
+        }
+        ln(xdec, T, Dd, dec_norm, dec_out);
+        M3R_CUDA(cudaEventRecord(stage_ev_[3], stream_));
+
+        // heads, one view at a time (downstream_head1 / downstream_head2)
+        for (int view = 0; view < 2; ++view) heads(view, n);
+        M3R_CUDA(cudaEventRecord(stage_ev_[4], stream_));
+        M3R_CUDA(cudaStreamSynchronize(stream_));
+        check_error();
+        if (profiling) collect_profile();
+        if (stage_ms) {
+            float ms;
+            for (int i = 0; i < 4; ++i) {
+                M3R_CUDA(cudaEventElapsedTime(&ms, stage_ev_[i], stage_ev_[i + 1]));
+                stage_ms[i] = ms;
+            }
+            M3R_CUDA(cudaEventElapsedTime(&ms, stage_ev_[0], stage_ev_[4]));
+            stage_ms[4] = ms;
+        }
+    }
+
+    void heads(int view, int n) {
+        const Dims& d = d_;
+        const Head& Hh = head[view];
+        const long long N = d.ntok, Tv = static_cast<long long>(n) * N;
+        const int hg = d.hg, wg = d.wg;
+        const __nv_bfloat16* h0 = enc_out + view * Tv * d.enc_dim;
+        const __nv_bfloat16* h1 = hook1 + view * Tv * d.dec_dim;
+        const __nv_bfloat16* h2 = hook2 + view * Tv * d.dec_dim;
+        const __nv_bfloat16* h3 = dec_out + view * Tv * d.dec_dim;
+
+        // act_postprocess (mpsgraph_engine.mm:391-395)
+        linear(h0, Tv, Hh.ap0_0, EPI_BF16, f0a, 96, ACT_NONE, nullptr, 128);
+        {
+            GemmParams p = gp();
+            p.bias = Hh.ap0_1t.b;
+            p.out = f0;
+            p.ldo = 96;
+            p.ct_s = 4;
+            p.ct_cout = 96;
+            p.ct_h = hg;
+            p.ct_w = wg;
+            launch(kGemm, 2.0 * Tv * Hh.ap0_1t.out * Hh.ap0_1t.in,
+                   [&] { gemm_rows(stream_, 256, EPI_CONVT, f0a, 96, static_cast<int>(Tv), 96, Hh.ap0_1t.w, 96, Hh.ap0_1t.out, p); });
+        }
+        linear(h1, Tv, Hh.ap1_0, EPI_BF16, f1a, 192, ACT_NONE, nullptr, 128);
+        {
+            GemmParams p = gp();
+            p.bias = Hh.ap1_1t.b;
+            p.out = f1;
+            p.ldo = 192;
+            p.ct_s = 2;
+            p.ct_cout = 192;
+            p.ct_h = hg;
+            p.ct_w = wg;
+            launch(kGemm, 2.0 * Tv * Hh.ap1_1t.out * Hh.ap1_1t.in,
+                   [&] { gemm_rows(stream_, 256, EPI_CONVT, f1a, 192, static_cast<int>(Tv), 192, Hh.ap1_1t.w, 192, Hh.ap1_1t.out, p); });
+        }
+        linear(h2, Tv, Hh.ap2_0, EPI_BF16, f2, 384, ACT_NONE, nullptr, 128);
+        linear(h3, Tv, Hh.ap3_0, EPI_BF16, f3a, 768, ACT_NONE, nullptr, 256);
+        launch(kOther, 0, [&] { im2col_s2(stream_, f3a, n, hg, wg, 768, col3); });
+        linear(col3, static_cast<long long>(n) * (hg / 2) * (wg / 2), Hh.ap3_1, EPI_BF16, f3, 768, ACT_NONE, nullptr, 256);
+
+        // layer_rn (3x3, no bias) -> 256 channels each
+        conv3(f0, n, 4 * hg, 4 * wg, 96, Hh.rn[0], EPI_BF16, rn0, ACT_NONE, 256);
+        conv3(f1, n, 2 * hg, 2 * wg, 192, Hh.rn[1], EPI_BF16, rn1, ACT_NONE, 256);
+        conv3(f2, n, hg, wg, 384, Hh.rn[2], EPI_BF16, rn2, ACT_NONE, 256);
+        conv3(f3, n, hg / 2, wg / 2, 768, Hh.rn[3], EPI_BF16, rn3, ACT_NONE, 256);
+
+        // fusion and head (graph_builder.hpp:285-299, mpsgraph_engine.mm:402-422)
+        const int H0 = 4 * hg, W0 = 4 * wg;
+        launch(kOther, 0, [&] { dpt_fuse(stream_, rn0, rn1, 2 * hg, 2 * wg, rn2, hg, wg, rn3, hg / 2, wg / 2, n, H0, W0, 256, fused); });
+        launch(kOther, 0, [&] { resize_bf16(stream_, fused, n, H0, W0, 256, 2 * H0, 2 * W0, up1); });
+        conv3(up1, n, 2 * H0, 2 * W0, 256, Hh.hd0, EPI_BF16, hd0, ACT_RELU, 128);
+        launch(kOther, 0, [&] { resize_bf16(stream_, hd0, n, 2 * H0, 2 * W0, 128, 4 * H0, 4 * W0, up2); });
+        conv3(up2, n, 4 * H0, 4 * W0, 128, Hh.hd2, EPI_HEAD4, out4, ACT_RELU, 128, Hh.w4, Hh.b4);
+        float* pts = o_pts + static_cast<long long>(view) * n * d.H * d.W * 3;
+        float* conf = o_conf + static_cast<long long>(view) * n * d.H * d.W;
+        launch(kOther, 0, [&] { head_split(stream_, out4, n, 4 * H0, 4 * W0, d.H, d.W, pts, conf); });
+
+        // local features (mpsgraph_engine.mm:425-437): MLP(enc || dec) -> pixel shuffle -> L2 norm
+        {
+            GemmParams p = gp();
+            p.bias = Hh.lf1.b;
+            p.act = ACT_GELU;
+            p.out = lf1;
+            p.ldo = d.lf_hidden;
+            launch(kGemm, 2.0 * Tv * Hh.lf1.out * Hh.lf1.in, [&] {
+                gemm_concat(stream_, 256, EPI_BF16, h0, d.enc_dim, d.enc_dim, h3, d.dec_dim, d.dec_dim, static_cast<int>(Tv),
+                            Hh.lf1.w, Hh.lf1.in, Hh.lf1.out, p);
+            });
+        }
+        {
+            GemmParams p = gp();
+            p.bias = Hh.lf2.b;
+            p.out = o_desc + static_cast<long long>(view) * n * d.H * d.W * d.desc_dim;
+            p.n_tok = d.ntok;
+            p.grid_w = wg;
+            p.grid_h = hg;
+            p.patch = d.patch;
+            const int bn = (d.patch * d.patch) % 8 == 0 ? 192 : 96;
+            launch(kGemm, 2.0 * Tv * Hh.lf2.out * Hh.lf2.in, [&] {
+                gemm_rows(stream_, bn, EPI_DESC, lf1, d.lf_hidden, static_cast<int>(Tv), d.lf_hidden, Hh.lf2.w, d.lf_hidden, Hh.lf2.out, p);
+            });
+        }
+    }
+
+    void check_error() {
+        int e = 0;
+        M3R_CUDA(cudaMemcpy(&e, err_, sizeof(int), cudaMemcpyDeviceToHost));
+        if (e != 0) {
+            M3R_CUDA(cudaMemset(err_, 0, sizeof(int)));
+            throw Error(kErrTimeout, "device wait timed out (code " + std::to_string(e) + ")");
+        }
+    }
+
+    int* err_ptr() const { return err_; }
+
+private:
+    void profiling_reset() { prof_rec_.clear(); }
+
+    int dev_;
+    Dims d_;
+    int max_pairs_;
+    cudaStream_t stream_ = nullptr;
+    int* err_ = nullptr;
+    cudaEvent_t stage_ev_[8];
+    std::vector<void*> allocs_;
+};
+
+// ---------------------------------------------------------------------------- engine
+Engine::Engine(const m3r_config& cfg) : cfg_(cfg), d_(Dims::from(cfg)) {
+    M3R_REQUIRE(cfg.max_pairs > 0 && cfg.max_pairs <= 4096, "max_pairs must be in [1, 4096]");
+    int ndev = 0;
+    M3R_CUDA(cudaGetDeviceCount(&ndev));
+    std::vector<int> ids;
+    if (cfg.n_devices <= 0) {
+        ids.push_back(0);
+    } else {
+        M3R_REQUIRE(cfg.n_devices <= M3R_MAX_DEVICES, "too many devices");
+        for (int i = 0; i < cfg.n_devices; ++i) ids.push_back(cfg.devices[i]);
+    }
+    for (int id : ids) {
+        M3R_REQUIRE(id >= 0 && id < ndev, "device index out of range");
+        devs_.emplace_back(new Device(id, d_, cfg.max_pairs));
+    }
+}
+
+Engine::~Engine() = default;
+
+void Engine::load(const std::string& path) {
+    SafetensorsFile f(path);
+    const Dims& d = d_;
+    auto L = [&](const std::string& name, int out, int in, bool bias = true) {
+        auto w = f.load_f32(name + ".weight", {out, in});
+        std::vector<float> b;
+        if (bias) b = f.load_f32(name + ".bias", {out});
+        return to_bf16(w, out, in, std::move(b));
+    };
+    auto V = [&](const std::string& name, int n) { return f.load_f32(name, {n}); };
+
+    // patch embedding [D, 3, p, p] -> [D, kpad]
+    const int p = d.patch, kp = 3 * p * p;
+    HostLin patch;
+    {
+        auto w = f.load_f32("patch_embed.proj.weight", {d.enc_dim, 3, p, p});
+        std::vector<float> t(static_cast<size_t>(d.enc_dim) * d.kpad, 0.0f);
+        for (int o = 0; o < d.enc_dim; ++o)
+            for (int kk = 0; kk < kp; ++kk) t[static_cast<size_t>(o) * d.kpad + kk] = w[static_cast<size_t>(o) * kp + kk];
+        patch = to_bf16(t, d.enc_dim, d.kpad, V("patch_embed.proj.bias", d.enc_dim));
+    }
+    struct HostEnc {
+        std::vector<float> n1g, n1b, n2g, n2b;
+        HostLin qkv, proj, fc1, fc2;
+    };
+    std::vector<HostEnc> enc(d.enc_depth);
+    for (int i = 0; i < d.enc_depth; ++i) {
+        const std::string b = "enc_blocks." + std::to_string(i) + ".";
+        HostEnc& e = enc[i];
+        e.n1g = V(b + "norm1.weight", d.enc_dim);
+        e.n1b = V(b + "norm1.bias", d.enc_dim);
+        e.n2g = V(b + "norm2.weight", d.enc_dim);
+        e.n2b = V(b + "norm2.bias", d.enc_dim);
+        e.qkv = L(b + "attn.qkv", 3 * d.enc_dim, d.enc_dim);
+        e.proj = L(b + "attn.proj", d.enc_dim, d.enc_dim);
+        e.fc1 = L(b + "mlp.fc1", d.enc_mlp, d.enc_dim);
+        e.fc2 = L(b + "mlp.fc2", d.enc_dim, d.enc_mlp);
+    }
+    const auto eng = V("enc_norm.weight", d.enc_dim), enb = V("enc_norm.bias", d.enc_dim);
+    const HostLin dembed = L("decoder_embed", d.dec_dim, d.enc_dim);
+    struct HostDec {
+        std::vector<float> n[8];
+        HostLin qkv, proj, q, kv, cproj, fc1, fc2;
+    };
+    std::vector<HostDec> dec[2];
+    const int Dd = d.dec_dim;
+    for (int view = 0; view < 2; ++view) {
+        dec[view].resize(d.dec_depth);
+        for (int i = 0; i < d.dec_depth; ++i) {
+            const std::string b = (view == 0 ? "dec_blocks." : "dec_blocks2.") + std::to_string(i) + ".";
+            HostDec& e = dec[view][i];
+            const char* norms[4] = {"norm1", "norm2", "norm_y", "norm3"};
+            for (int k = 0; k < 4; ++k) {
+                e.n[2 * k] = V(b + norms[k] + ".weight", Dd);
+                e.n[2 * k + 1] = V(b + norms[k] + ".bias", Dd);
+            }
+            e.qkv = L(b + "attn.qkv", 3 * Dd, Dd);
+            e.proj = L(b + "attn.proj", Dd, Dd);
+            e.q = L(b + "cross_attn.projq", Dd, Dd);
+            {
+                auto wk = f.load_f32(b + "cross_attn.projk.weight", {Dd, Dd});
+                auto wv = f.load_f32(b + "cross_attn.projv.weight", {Dd, Dd});
+                auto bk = V(b + "cross_attn.projk.bias", Dd);
+                auto bv = V(b + "cross_attn.projv.bias", Dd);
+                wk.insert(wk.end(), wv.begin(), wv.end());
+                bk.insert(bk.end(), bv.begin(), bv.end());
+                e.kv = to_bf16(wk, 2 * Dd, Dd, bk);
+            }
+            e.cproj = L(b + "cross_attn.proj", Dd, Dd);
+            e.fc1 = L(b + "mlp.fc1", d.dec_mlp, Dd);
+            e.fc2 = L(b + "mlp.fc2", Dd, d.dec_mlp);
+        }
+    }
+    const auto dng = V("dec_norm.weight", Dd), dnb = V("dec_norm.bias", Dd);
+    struct HostHead {
+        HostLin ap0_0, ap0_1t, ap1_0, ap1_1t, ap2_0, ap3_0, ap3_1, rn[4], hd0, hd2, lf1, lf2;
+        std::vector<float> w4, b4;
+    };
+    HostHead hh[2];
+    const int dpt[4] = {96, 192, 384, 768};
+    for (int view = 0; view < 2; ++view) {
+        const std::string t = std::string(view == 0 ? "downstream_head1" : "downstream_head2") + ".dpt.";
+        HostHead& H = hh[view];
+        auto conv1 = [&](const std::string& name, int out, int in) {
+            auto w = f.load_f32(name + ".weight", {out, in, 1, 1});
+            return to_bf16(w, out, in, V(name + ".bias", out));
+        };
+        H.ap0_0 = conv1(t + "act_postprocess.0.0", 96, d.enc_dim);
+        H.ap0_1t = convt_weights(f.load_f32(t + "act_postprocess.0.1.weight", {96, 96, 4, 4}), 96, 96, 4,
+                                 V(t + "act_postprocess.0.1.bias", 96));
+        H.ap1_0 = conv1(t + "act_postprocess.1.0", 192, Dd);
+        H.ap1_1t = convt_weights(f.load_f32(t + "act_postprocess.1.1.weight", {192, 192, 2, 2}), 192, 192, 2,
+                                 V(t + "act_postprocess.1.1.bias", 192));
+        H.ap2_0 = conv1(t + "act_postprocess.2.0", 384, Dd);
+        H.ap3_0 = conv1(t + "act_postprocess.3.0", 768, Dd);
+        H.ap3_1 = conv3_weights(f.load_f32(t + "act_postprocess.3.1.weight", {768, 768, 3, 3}), 768, 768,
+                                V(t + "act_postprocess.3.1.bias", 768));
+        for (int k = 0; k < 4; ++k)
+            H.rn[k] = conv3_weights(f.load_f32(t + "scratch.layer_rn." + std::to_string(k) + ".weight", {256, dpt[k], 3, 3}),
+                                    256, dpt[k]);
+        H.hd0 = conv3_weights(f.load_f32(t + "head.0.weight", {128, 256, 3, 3}), 128, 256, V(t + "head.0.bias", 128));
+        H.hd2 = conv3_weights(f.load_f32(t + "head.2.weight", {128, 128, 3, 3}), 128, 128, V(t + "head.2.bias", 128));
+        H.w4 = f.load_f32(t + "head.4.weight", {4, 128, 1, 1});
+        H.b4 = V(t + "head.4.bias", 4);
+        const std::string lf = std::string(view == 0 ? "downstream_head1" : "downstream_head2") + ".head_local_features.";
+        H.lf1 = L(lf + "fc1", d.lf_hidden, d.enc_dim + Dd);
+        {
+            // keep the desc_dim descriptor channels of every (dy, dx) group of desc_dim + 1
+            // (the extra channel is the discarded descriptor confidence)
+            const int groups = p * p, cin = d.desc_dim + 1;
+            auto w = f.load_f32(lf + "fc2.weight", {groups * cin, d.lf_hidden});
+            auto b = V(lf + "fc2.bias", groups * cin);
+            std::vector<float> w2(static_cast<size_t>(groups) * d.desc_dim * d.lf_hidden), b2(static_cast<size_t>(groups) * d.desc_dim);
+            for (int g = 0; g < groups; ++g)
+                for (int c = 0; c < d.desc_dim; ++c) {
+                    const size_t src = static_cast<size_t>(g) * cin + c, dst = static_cast<size_t>(g) * d.desc_dim + c;
+                    std::memcpy(&w2[dst * d.lf_hidden], &w[src * d.lf_hidden], sizeof(float) * d.lf_hidden);
+                    b2[dst] = b[src];
+                }
+            H.lf2 = to_bf16(w2, groups * d.desc_dim, d.lf_hidden, b2);
+        }
+    }
+    // RoPE tables (rope2d.py:77-92): freq_i = 1 / 100^(i/16), angle = pos * freq_i in float32
+    const int maxpos = std::max(d.hg, d.wg);
+    std::vector<float> rc(static_cast<size_t>(maxpos) * 16), rs(static_cast<size_t>(maxpos) * 16);
+    for (int i = 0; i < 16; ++i) {
+        const float freq = 1.0f / std::pow(100.0f, static_cast<float>(i) / 16.0f);
+        for (int pos = 0; pos < maxpos; ++pos) {
+            const float ang = static_cast<float>(pos) * freq;
+            rc[pos * 16 + i] = static_cast<float>(std::cos(static_cast<double>(ang)));
+            rs[pos * 16 + i] = static_cast<float>(std::sin(static_cast<double>(ang)));
+        }
+    }
+
+    // upload to every device
+    for (auto& dp : devs_) {
+        Device& D = *dp;
+        DeviceGuard g(D.dev());
+        D.patch = D.upload(patch);
+        D.enc.resize(d.enc_depth);
+        for (int i = 0; i < d.enc_depth; ++i) {
+            EncBlock& B = D.enc[i];
+            B.n1 = D.upload_norm(enc[i].n1g, enc[i].n1b);
+            B.n2 = D.upload_norm(enc[i].n2g, enc[i].n2b);
+            B.qkv = D.upload(enc[i].qkv);
+            B.proj = D.upload(enc[i].proj);
+            B.fc1 = D.upload(enc[i].fc1);
+            B.fc2 = D.upload(enc[i].fc2);
+        }
+        D.enc_norm = D.upload_norm(eng, enb);
+        D.dec_embed = D.upload(dembed);
+        for (int view = 0; view < 2; ++view) {
+            D.dec[view].resize(d.dec_depth);
+            for (int i = 0; i < d.dec_depth; ++i) {
+                const HostDec& e = dec[view][i];
+                DecBlock& B = D.dec[view][i];
+                B.n1 = D.upload_norm(e.n[0], e.n[1]);
+                B.n2 = D.upload_norm(e.n[2], e.n[3]);
+                B.ny = D.upload_norm(e.n[4], e.n[5]);
+                B.n3 = D.upload_norm(e.n[6], e.n[7]);
+                B.qkv = D.upload(e.qkv);
+                B.proj = D.upload(e.proj);
+                B.q = D.upload(e.q);
+                B.kv = D.upload(e.kv);
+                B.cproj = D.upload(e.cproj);
+                B.fc1 = D.upload(e.fc1);
+                B.fc2 = D.upload(e.fc2);
+            }
+        }
+        D.dec_norm = D.upload_norm(dng, dnb);
+        for (int view = 0; view < 2; ++view) {
+            const HostHead& H = hh[view];
+            Head& O = D.head[view];
+            O.ap0_0 = D.upload(H.ap0_0);
+            O.ap0_1t = D.upload(H.ap0_1t);
+            O.ap1_0 = D.upload(H.ap1_0);
+            O.ap1_1t = D.upload(H.ap1_1t);
+            O.ap2_0 = D.upload(H.ap2_0);
+            O.ap3_0 = D.upload(H.ap3_0);
+            O.ap3_1 = D.upload(H.ap3_1);
+            for (int k = 0; k < 4; ++k) O.rn[k] = D.upload(H.rn[k]);
+            O.hd0 = D.upload(H.hd0);
+            O.hd2 = D.upload(H.hd2);
+            O.w4 = D.upload(H.w4);
+            O.b4 = D.upload(H.b4);
+            O.lf1 = D.upload(H.lf1);
+            O.lf2 = D.upload(H.lf2);
+        }
+        D.rope_cos = D.upload(rc);
+        D.rope_sin = D.upload(rs);
+        M3R_CUDA(cudaDeviceSynchronize());
+    }
+    ready_ = true;
+}
+
+std::vector<std::pair<int, int>> Engine::shards(int n_pairs) const {
+    std::vector<std::pair<int, int>> s;
+    const int nd = static_cast<int>(devs_.size());
+    int first = 0;
+    for (int i = 0; i < nd; ++i) {
+        const int cnt = n_pairs / nd + (i < n_pairs % nd ? 1 : 0);
+        s.push_back({first, cnt});
+        first += cnt;
+    }
+    return s;
+}
+
+namespace {
+// Runs fn(i) for every device on its own host thread; rethrows the first error.
+void for_each_device(size_t n, const std::function<void(size_t)>& fn) {
+    if (n == 1) {
+        fn(0);
+        return;
+    }
+    std::vector<std::thread> th;
+    std::vector<std::exception_ptr> errs(n);
+    for (size_t i = 0; i < n; ++i)
+        th.emplace_back([&, i] {
+            try {
+                fn(i);
+            } catch (...) {
+                errs[i] = std::current_exception();
+            }
+        });
+    for (auto& t : th) t.join();
+    for (auto& e : errs)
+        if (e) std::rethrow_exception(e);
+}
+}  // namespace
+
+void Engine::stage(const uint8_t* img1, const uint8_t* img2, int n_pairs) {
+    if (!ready_) throw Error(kErrState, "engine is not loaded");
+    M3R_REQUIRE(n_pairs >= 1, "n_pairs must be >= 1");
+    const auto sh = shards(n_pairs);
+    const size_t img_bytes = static_cast<size_t>(d_.H) * d_.W * 3;
+    for (size_t i = 0; i < devs_.size(); ++i)
+        M3R_REQUIRE(sh[i].second <= cfg_.max_pairs, "too many pairs for one device launch (raise max_pairs)");
+    for_each_device(devs_.size(), [&](size_t i) {
+        Device& D = *devs_[i];
+        DeviceGuard g(D.dev());
+        const int first = sh[i].first, cnt = sh[i].second;
+        D.staged = cnt;
+        if (cnt == 0) return;
+        M3R_CUDA(cudaMemcpyAsync(D.img, img1 + first * img_bytes, cnt * img_bytes, cudaMemcpyHostToDevice, D.stream()));
+        M3R_CUDA(cudaMemcpyAsync(D.img + cnt * img_bytes, img2 + first * img_bytes, cnt * img_bytes,
+                                 cudaMemcpyHostToDevice, D.stream()));
+        M3R_CUDA(cudaStreamSynchronize(D.stream()));
+    });
+    staged_pairs_ = n_pairs;
+}
+
+float Engine::run_resident(int n_pairs, float* stage_ms) {
+    if (!ready_) throw Error(kErrState, "engine is not loaded");
+    if (n_pairs != staged_pairs_) throw Error(kErrState, "run_resident: pair count differs from the staged inputs");
+    std::vector<float> ms(devs_.size() * 5, 0.0f);
+    for_each_device(devs_.size(), [&](size_t i) {
+        Device& D = *devs_[i];
+        D.profiling = profiling_ && i == 0;
+        if (D.staged > 0) D.forward(D.staged, &ms[i * 5]);
+    });
+    float mx = 0.0f;
+    for (size_t i = 0; i < devs_.size(); ++i) {
+        mx = std::max(mx, ms[i * 5 + 4]);
+        if (stage_ms && (i == 0 || ms[i * 5 + 4] >= mx))
+            for (int k = 0; k < 5; ++k) stage_ms[k] = ms[i * 5 + k];
+    }
+    return mx;
+}
+
+void Engine::fetch(int n_pairs, float* const outs[6]) {
+    if (n_pairs != staged_pairs_) throw Error(kErrState, "fetch: pair count differs from the staged inputs");
+    const auto sh = shards(n_pairs);
+    const size_t px = static_cast<size_t>(d_.H) * d_.W;
+    for_each_device(devs_.size(), [&](size_t i) {
+        Device& D = *devs_[i];
+        DeviceGuard g(D.dev());
+        const int first = sh[i].first, cnt = sh[i].second;
+        if (cnt == 0) return;
+        const size_t sizes[3] = {px * 3, px * static_cast<size_t>(d_.desc_dim), px};
+        const float* src[3] = {D.o_pts, D.o_desc, D.o_conf};
+        for (int k = 0; k < 3; ++k)
+            for (int view = 0; view < 2; ++view) {
+                float* dst = outs[2 * k + view];
+                if (!dst) continue;
+                M3R_CUDA(cudaMemcpyAsync(dst + first * sizes[k], src[k] + static_cast<size_t>(view) * cnt * sizes[k],
+                                         sizeof(float) * cnt * sizes[k], cudaMemcpyDeviceToHost, D.stream()));
+            }
+        M3R_CUDA(cudaStreamSynchronize(D.stream()));
+    });
+}
+
+void Engine::infer(const uint8_t* img1, const uint8_t* img2, int n_pairs, float* const outs[6], float* timing) {
+    if (!ready_) throw Error(kErrState, "engine is not loaded");
+    const auto t0 = std::chrono::steady_clock::now();
+    float st[5] = {0, 0, 0, 0, 0};
+    double h2d = 0, d2h = 0, dev = 0;
+    // launch in chunks of max_pairs per device
+    const int per_launch = cfg_.max_pairs * static_cast<int>(devs_.size());
+    for (int first = 0; first < n_pairs; first += per_launch) {
+        const int cnt = std::min(per_launch, n_pairs - first);
+        const size_t ib = static_cast<size_t>(d_.H) * d_.W * 3;
+        const size_t px = static_cast<size_t>(d_.H) * d_.W;
+        auto a = std::chrono::steady_clock::now();
+        stage(img1 + first * ib, img2 + first * ib, cnt);
+        auto b = std::chrono::steady_clock::now();
+        float cs[5];
+        dev += run_resident(cnt, cs);
+        for (int k = 0; k < 5; ++k) st[k] += cs[k];
+        auto c = std::chrono::steady_clock::now();
+        float* o[6] = {outs[0] ? outs[0] + first * px * 3 : nullptr, outs[1] ? outs[1] + first * px * 3 : nullptr,
+                       outs[2] ? outs[2] + first * px * d_.desc_dim : nullptr,
+                       outs[3] ? outs[3] + first * px * d_.desc_dim : nullptr, outs[4] ? outs[4] + first * px : nullptr,
+                       outs[5] ? outs[5] + first * px : nullptr};
+        fetch(cnt, o);
+        auto e = std::chrono::steady_clock::now();
+        h2d += std::chrono::duration<double, std::milli>(b - a).count();
+        d2h += std::chrono::duration<double, std::milli>(e - c).count();
+    }
+    if (timing) {
+        timing[M3R_T_PREPROCESS] = st[0];
+        timing[M3R_T_ENCODER] = st[1];
+        timing[M3R_T_DECODER] = st[2];
+        timing[M3R_T_HEADS] = st[3];
+        timing[M3R_T_H2D] = static_cast<float>(h2d);
+        timing[M3R_T_D2H] = static_cast<float>(d2h);
+        timing[M3R_T_INFERENCE] = static_cast<float>(dev);
+        timing[M3R_T_TOTAL] =
+            static_cast<float>(std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count());
+    }
+}
+
+void Engine::profile(double* out) const {
+    const Device& D = *devs_[0];
+    out[0] = D.prof.ms[0];
+    out[1] = D.prof.flops[0];
+    out[2] = D.prof.ms[1];
+    out[3] = D.prof.flops[1];
+    out[4] = D.prof.ms[2];
+    out[5] = static_cast<double>(D.prof.launches[0]);
+    out[6] = static_cast<double>(D.prof.launches[1]);
+    out[7] = static_cast<double>(D.prof.launches[2]);
+}
+
+// ---------------------------------------------------------------------------- match
+int Engine::match(const float* d1, const float* d2, int hh, int ww, int dd, int top_k, int reciprocal, float thr,
+                  int64_t* idx1, int64_t* idx2, float* conf, float* p1, float* p2, float* timing) {
+    const auto t0 = std::chrono::steady_clock::now();
+    M3R_REQUIRE(hh >= 0 && ww >= 0 && dd > 0 && top_k >= 0, "match: bad arguments");
+    const long long n = static_cast<long long>(hh) * ww;
+    M3R_REQUIRE(n < 0x7FFFFFFFLL, "match: too many descriptors");
+    M3R_REQUIRE(top_k <= 4096, "match: top_k must be <= 4096");
+    if (n == 0 || top_k == 0) {
+        if (timing) timing[M3R_T_TOTAL] = 0.0f;
+        return 0;
+    }
+    // single device (device 0 of the engine)
+    Device& D = *devs_[0];
+    DeviceGuard g(D.dev());
+    cudaStream_t s = D.stream();
+    D.mws.reserve(n, dd);
+    cudaEvent_t e0, e1;
+    M3R_CUDA(cudaEventCreate(&e0));
+    M3R_CUDA(cudaEventCreate(&e1));
+    M3R_CUDA(cudaMemcpyAsync(D.mws.a, d1, sizeof(float) * n * dd, cudaMemcpyHostToDevice, s));
+    M3R_CUDA(cudaMemcpyAsync(D.mws.b, d2, sizeof(float) * n * dd, cudaMemcpyHostToDevice, s));
+    M3R_CUDA(cudaEventRecord(e0, s));
+    match_normalize(s, D.mws.a, D.mws.a, n, dd);
+    match_normalize(s, D.mws.b, D.mws.b, n, dd);
+    match_argmax(s, D.mws.a, D.mws.b, 0, n, n, dd, D.mws.rowkey, D.mws.colkey, true);
+    const int m = match_select(s, D.mws, n, 0, reciprocal, thr, top_k);
+    M3R_CUDA(cudaEventRecord(e1, s));
+    if (m > 0) {
+        M3R_CUDA(cudaMemcpyAsync(idx1, D.mws.idx1, sizeof(int64_t) * m, cudaMemcpyDeviceToHost, s));
+        M3R_CUDA(cudaMemcpyAsync(idx2, D.mws.idx2, sizeof(int64_t) * m, cudaMemcpyDeviceToHost, s));
+        M3R_CUDA(cudaMemcpyAsync(conf, D.mws.conf, sizeof(float) * m, cudaMemcpyDeviceToHost, s));
+    }
+    M3R_CUDA(cudaStreamSynchronize(s));
+    float kms = 0;
+    M3R_CUDA(cudaEventElapsedTime(&kms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    for (int i = 0; i < m; ++i) {  // matching.cpp:216-222
+        p1[2 * i] = static_cast<float>(idx1[i] % ww);
+        p1[2 * i + 1] = static_cast<float>(idx1[i] / ww);
+        p2[2 * i] = static_cast<float>(idx2[i] % ww);
+        p2[2 * i + 1] = static_cast<float>(idx2[i] / ww);
+    }
+    if (timing) {
+        for (int i = 0; i < M3R_T_COUNT; ++i) timing[i] = 0.0f;
+        timing[M3R_T_INFERENCE] = kms;
+        timing[M3R_T_TOTAL] =
+            static_cast<float>(std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count());
+    }
+    return m;
+}
+
+}  // namespace m3r

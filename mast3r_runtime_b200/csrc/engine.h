@@ -1,0 +1,92 @@
+// Two-view inference engine: weights replicated per device, one stream and one
+// activation arena per device, pairs sharded across devices by host threads.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/m3r_cuda.h"
+#include "matcher.h"
+
+namespace m3r {
+
+struct Dims {
+    int patch, enc_dim, enc_depth, enc_heads, enc_mlp;
+    int dec_dim, dec_depth, dec_heads, dec_mlp;
+    int lf_hidden, desc_dim;
+    int H, W, hg, wg, ntok;
+    int kpad;  // patch-embed K (3 p^2) rounded up to 64
+    int hook1, hook2;
+    int dpt_h, dpt_w;  // 16 * grid
+    static Dims from(const m3r_config& c);
+};
+
+struct Lin {
+    __nv_bfloat16* w = nullptr;  // [out, in]
+    float* b = nullptr;          // [out] or null
+    int out = 0, in = 0;
+};
+struct Norm {
+    float* g = nullptr;
+    float* b = nullptr;
+};
+struct EncBlock {
+    Norm n1, n2;
+    Lin qkv, proj, fc1, fc2;
+};
+struct DecBlock {
+    Norm n1, n2, ny, n3;
+    Lin qkv, proj, q, kv, cproj, fc1, fc2;
+};
+struct Head {
+    Lin ap0_0, ap0_1t, ap1_0, ap1_1t, ap2_0, ap3_0, ap3_1;
+    Lin rn[4];
+    Lin hd0, hd2;
+    float* w4 = nullptr;  // [4][128]
+    float* b4 = nullptr;
+    Lin lf1, lf2;
+};
+
+class Device;
+
+class Engine {
+public:
+    explicit Engine(const m3r_config& cfg);
+    ~Engine();
+    void load(const std::string& path);
+    bool ready() const { return ready_; }
+    void infer(const uint8_t* img1, const uint8_t* img2, int n_pairs, float* const outs[6], float* timing);
+    void stage(const uint8_t* img1, const uint8_t* img2, int n_pairs);
+    float run_resident(int n_pairs, float* stage_ms);
+    void fetch(int n_pairs, float* const outs[6]);
+    int match(const float* d1, const float* d2, int h, int w, int d, int top_k, int reciprocal, float thr,
+              int64_t* idx1, int64_t* idx2, float* conf, float* p1, float* p2, float* timing);
+    void set_profiling(bool on) { profiling_ = on; }
+    void profile(double* out8) const;
+
+    std::string last_error;
+    const Dims& dims() const { return d_; }
+    bool profiling() const { return profiling_; }
+
+private:
+    std::vector<std::pair<int, int>> shards(int n_pairs) const;  // (first pair, count) per device
+    m3r_config cfg_;
+    Dims d_;
+    std::vector<std::unique_ptr<Device>> devs_;
+    bool ready_ = false;
+    bool profiling_ = false;
+    int staged_pairs_ = 0;
+};
+
+// Per-device helpers used by the test entry points.
+struct DeviceGuard {
+    int prev = 0;
+    explicit DeviceGuard(int dev);
+    ~DeviceGuard();
+};
+
+}  // namespace m3r

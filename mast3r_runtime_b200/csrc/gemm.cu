@@ -1,0 +1,138 @@
+// Launchers and the instantiated (BN, A mode, epilogue) variants of the tcgen05 GEMM.
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "gemm.h"
+
+namespace m3r {
+
+int num_sms() {
+    int dev = 0, n = 0;
+    M3R_CUDA(cudaGetDevice(&dev));
+    M3R_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+    return n;
+}
+
+GemmParams gemm_params() {
+    GemmParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.act = ACT_NONE;
+    p.desc_dim = 24;
+    return p;
+}
+
+namespace {
+
+template <int BN, int AMODE, int EPI>
+void launch(cudaStream_t s, const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b,
+            const GemmParams& p) {
+    using C = GemmCfg<BN>;
+    auto kern = gemm_tc_kernel<BN, AMODE, EPI>;
+    static std::once_flag once;  // per instantiation; the attribute is set on every device
+    std::call_once(once, [&] {
+        int ndev = 0;
+        M3R_CUDA(cudaGetDeviceCount(&ndev));
+        int cur = 0;
+        M3R_CUDA(cudaGetDevice(&cur));
+        for (int d = 0; d < ndev; ++d) {
+            M3R_CUDA(cudaSetDevice(d));
+            M3R_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+        }
+        M3R_CUDA(cudaSetDevice(cur));
+    });
+    const int tiles = p.tiles_m * p.tiles_n;
+    if (tiles == 0) return;
+    const int grid = tiles < num_sms() ? tiles : num_sms();
+    kern<<<grid, 192, C::SMEM_BYTES, s>>>(a0, a1, b, p);
+    M3R_CUDA(cudaGetLastError());
+}
+
+#define M3R_GEMM_CASE(BN_, AM_, EPI_)                   \
+    if (bn == BN_ && amode == AM_ && epi == EPI_) {     \
+        launch<BN_, AM_, EPI_>(s, a0, a1, b, p);        \
+        return;                                         \
+    }
+
+void dispatch(cudaStream_t s, int bn, int amode, int epi, const CUtensorMap& a0, const CUtensorMap& a1,
+              const CUtensorMap& b, const GemmParams& p) {
+    M3R_GEMM_CASE(256, A_PLAIN, EPI_BF16)
+    M3R_GEMM_CASE(128, A_PLAIN, EPI_BF16)
+    M3R_GEMM_CASE(256, A_PLAIN, EPI_F32)
+    M3R_GEMM_CASE(128, A_PLAIN, EPI_F32)
+    M3R_GEMM_CASE(256, A_PLAIN, EPI_F32_RESID)
+    M3R_GEMM_CASE(128, A_PLAIN, EPI_F32_RESID)
+    M3R_GEMM_CASE(256, A_PLAIN, EPI_HEADS)
+    M3R_GEMM_CASE(128, A_PLAIN, EPI_HEADS)
+    M3R_GEMM_CASE(192, A_PLAIN, EPI_DESC)
+    M3R_GEMM_CASE(96, A_PLAIN, EPI_DESC)
+    M3R_GEMM_CASE(256, A_PLAIN, EPI_CONVT)
+    M3R_GEMM_CASE(256, A_CONCAT, EPI_BF16)
+    M3R_GEMM_CASE(256, A_CONV3, EPI_BF16)
+    M3R_GEMM_CASE(128, A_CONV3, EPI_BF16)
+    M3R_GEMM_CASE(128, A_CONV3, EPI_HEAD4)
+    throw Error(kErrArg, "no GEMM variant for bn=" + std::to_string(bn) + " amode=" + std::to_string(amode) +
+                             " epi=" + std::to_string(epi));
+}
+
+int cdiv(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
+
+}  // namespace
+
+void gemm_rows(cudaStream_t s, int bn, int epi, const __nv_bfloat16* A, long long lda, int M, int K,
+               const __nv_bfloat16* W, long long ldw, int N, GemmParams p) {
+    M3R_REQUIRE(M >= 0 && N > 0 && K > 0, "gemm: bad shape");
+    if (M == 0) return;
+    const CUtensorMap a = tmap_bf16_2d(A, M, K, lda, 128);
+    const CUtensorMap b = tmap_bf16_2d(W, N, K, ldw, bn);
+    p.M = M;
+    p.N = N;
+    p.num_kb = cdiv(K, 64);
+    p.tiles_m = cdiv(M, 128);
+    p.tiles_n = cdiv(N, bn);
+    dispatch(s, bn, A_PLAIN, epi, a, a, b, p);
+}
+
+void gemm_concat(cudaStream_t s, int bn, int epi, const __nv_bfloat16* A0, long long lda0, int K0,
+                 const __nv_bfloat16* A1, long long lda1, int K1, int M, const __nv_bfloat16* W, long long ldw,
+                 int N, GemmParams p) {
+    M3R_REQUIRE(K0 % 64 == 0, "gemm_concat: K0 must be a multiple of 64");
+    if (M == 0) return;
+    const CUtensorMap a0 = tmap_bf16_2d(A0, M, K0, lda0, 128);
+    const CUtensorMap a1 = tmap_bf16_2d(A1, M, K1, lda1, 128);
+    const CUtensorMap b = tmap_bf16_2d(W, N, K0 + K1, ldw, bn);
+    p.M = M;
+    p.N = N;
+    p.a_split_kb = K0 / 64;
+    p.num_kb = K0 / 64 + cdiv(K1, 64);
+    p.tiles_m = cdiv(M, 128);
+    p.tiles_n = cdiv(N, bn);
+    dispatch(s, bn, A_CONCAT, epi, a0, a1, b, p);
+}
+
+void gemm_conv3(cudaStream_t s, int bn, int epi, const __nv_bfloat16* X, int n, int h, int w, int c, int cstride,
+                const __nv_bfloat16* W, int N, GemmParams p) {
+    M3R_REQUIRE(n > 0 && h > 0 && w > 0 && c > 0 && cstride >= c, "gemm_conv3: bad shape");
+    int wbox = 1;
+    while (wbox * 2 <= 128 && w % (wbox * 2) == 0) wbox *= 2;
+    const int hbox = 128 / wbox;
+    M3R_REQUIRE(hbox <= 256, "gemm_conv3: box too tall");
+    const int cblocks = cdiv(c, 64);
+    const CUtensorMap a = tmap_bf16_nhwc(X, n, h, w, c, cstride, hbox, wbox);
+    const CUtensorMap b = tmap_bf16_2d(W, N, 9LL * cblocks * 64, 9LL * cblocks * 64, bn);
+    p.M = n * h * w;
+    p.N = N;
+    p.cv_H = h;
+    p.cv_W = w;
+    p.cv_cblocks = cblocks;
+    p.cv_wbox = wbox;
+    p.cv_hbox = hbox;
+    p.cv_tx = w / wbox;
+    p.cv_ty = cdiv(h, hbox);
+    p.num_kb = 9 * cblocks;
+    p.tiles_m = n * p.cv_tx * p.cv_ty;
+    p.tiles_n = cdiv(N, bn);
+    dispatch(s, bn, A_CONV3, epi, a, a, b, p);
+}
+
+}  // namespace m3r

@@ -1,0 +1,317 @@
+// Bandwidth-bound helper kernels: vectorised (16-byte) loads and stores, grids
+// sized in multiples of the SM count by the launch helpers.
+#include "kernels.h"
+#include "tmap.h"
+
+namespace m3r {
+
+namespace {
+
+inline int grid_for(long long n, int block) {
+    long long g = (n + block - 1) / block;
+    if (g > 148LL * 32) g = 148LL * 32;
+    return static_cast<int>(g > 0 ? g : 1);
+}
+
+__global__ void patch_im2col_kernel(const uint8_t* __restrict__ img, int n, int H, int W, int p, int kpad,
+                                    __nv_bfloat16* __restrict__ out) {
+    const int hg = H / p, wg = W / p;
+    const long long total = static_cast<long long>(n) * hg * wg * kpad;
+    const float mean[3] = {0.485f, 0.456f, 0.406f};
+    const float stdv[3] = {0.229f, 0.224f, 0.225f};
+    for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
+         e += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int k = static_cast<int>(e % kpad);
+        const long long row = e / kpad;
+        float v = 0.0f;
+        if (k < 3 * p * p) {
+            const int c = k / (p * p);
+            const int rem = k - c * p * p;
+            const int ky = rem / p, kx = rem - (rem / p) * p;
+            const int im = static_cast<int>(row / (hg * wg));
+            const int t = static_cast<int>(row - static_cast<long long>(im) * hg * wg);
+            const int gy = t / wg, gx = t - (t / wg) * wg;
+            const uint8_t u = img[((static_cast<long long>(im) * H + gy * p + ky) * W + gx * p + kx) * 3 + c];
+            v = (static_cast<float>(u) / 255.0f - mean[c]) / stdv[c];
+        }
+        out[e] = __float2bfloat16_rn(v);
+    }
+}
+
+// One warp per row; two-pass mean / variance in fp32 (vit_encoder.py:98-108).
+__global__ void layernorm_kernel(const float* __restrict__ x, int rows, int D, const float* __restrict__ g,
+                                 const float* __restrict__ b, __nv_bfloat16* __restrict__ y) {
+    const int warps = blockDim.x >> 5;
+    const int lane = threadIdx.x & 31;
+    for (long long r = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5); r < rows;
+         r += static_cast<long long>(gridDim.x) * warps) {
+        const float4* xr = reinterpret_cast<const float4*>(x + r * D);
+        const int n4 = D >> 2;
+        float4 v[8];  // D <= 1024
+        float s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int idx = lane + 32 * i;
+            if (idx < n4) {
+                v[i] = xr[idx];
+                s += v[i].x + v[i].y + v[i].z + v[i].w;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        const float mean = s / D;
+        float q = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int idx = lane + 32 * i;
+            if (idx < n4) {
+                const float a = v[i].x - mean, bb = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+                q += a * a + bb * bb + c * c + d * d;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+        const float rstd = rsqrtf(q / D + 1e-6f);
+        uint2* yr = reinterpret_cast<uint2*>(y + r * D);
+        const float4* g4 = reinterpret_cast<const float4*>(g);
+        const float4* b4 = reinterpret_cast<const float4*>(b);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int idx = lane + 32 * i;
+            if (idx < n4) {
+                const float4 gg = __ldg(g4 + idx), bb = __ldg(b4 + idx);
+                __nv_bfloat162 lo = __floats2bfloat162_rn((v[i].x - mean) * rstd * gg.x + bb.x,
+                                                          (v[i].y - mean) * rstd * gg.y + bb.y);
+                __nv_bfloat162 hi = __floats2bfloat162_rn((v[i].z - mean) * rstd * gg.z + bb.z,
+                                                          (v[i].w - mean) * rstd * gg.w + bb.w);
+                uint2 u;
+                u.x = *reinterpret_cast<uint32_t*>(&lo);
+                u.y = *reinterpret_cast<uint32_t*>(&hi);
+                yr[idx] = u;
+            }
+        }
+    }
+}
+
+__global__ void cast_bf16_kernel(const float* __restrict__ x, long long n, __nv_bfloat16* __restrict__ y) {
+    const long long n4 = n >> 2;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const float4 v = reinterpret_cast<const float4*>(x)[i];
+        __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&lo);
+        u.y = *reinterpret_cast<uint32_t*>(&hi);
+        reinterpret_cast<uint2*>(y)[i] = u;
+    }
+}
+
+// half-pixel source coordinate, clamped like PyTorch / MPSGraph (align_corners=False)
+__device__ __forceinline__ void src_coord(int o, int n_in, int n_out, int& i0, int& i1, float& f) {
+    float s = (o + 0.5f) * (static_cast<float>(n_in) / n_out) - 0.5f;
+    s = fmaxf(s, 0.0f);
+    i0 = min(static_cast<int>(s), n_in - 1);
+    i1 = min(i0 + 1, n_in - 1);
+    f = s - i0;
+}
+
+struct F8 {
+    float v[8];
+};
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, F8& o) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        o.v[2 * i] = f.x;
+        o.v[2 * i + 1] = f.y;
+    }
+}
+
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const F8& o) {
+    uint4 u;
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(o.v[2 * i], o.v[2 * i + 1]);
+        w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(p) = u;
+}
+
+__device__ __forceinline__ void bilerp_acc(const __nv_bfloat16* base, int hi, int wi, int C, int Ho, int Wo, int y,
+                                           int x, int c8, F8& acc) {
+    int y0, y1, x0, x1;
+    float fy, fx;
+    src_coord(y, hi, Ho, y0, y1, fy);
+    src_coord(x, wi, Wo, x0, x1, fx);
+    F8 a, b, c, d;
+    load8(base + (static_cast<long long>(y0) * wi + x0) * C + c8, a);
+    load8(base + (static_cast<long long>(y0) * wi + x1) * C + c8, b);
+    load8(base + (static_cast<long long>(y1) * wi + x0) * C + c8, c);
+    load8(base + (static_cast<long long>(y1) * wi + x1) * C + c8, d);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float top = a.v[i] * (1.0f - fx) + b.v[i] * fx;
+        const float bot = c.v[i] * (1.0f - fx) + d.v[i] * fx;
+        acc.v[i] += top * (1.0f - fy) + bot * fy;
+    }
+}
+
+__global__ void dpt_fuse_kernel(const __nv_bfloat16* __restrict__ f0, const __nv_bfloat16* __restrict__ f1, int h1,
+                                int w1, const __nv_bfloat16* __restrict__ f2, int h2, int w2,
+                                const __nv_bfloat16* __restrict__ f3, int h3, int w3, int n, int H0, int W0, int C,
+                                __nv_bfloat16* __restrict__ out) {
+    const int c8n = C / 8;
+    const long long total = static_cast<long long>(n) * H0 * W0 * c8n;
+    for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
+         e += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int c8 = static_cast<int>(e % c8n) * 8;
+        long long pix = e / c8n;
+        const int x = static_cast<int>(pix % W0);
+        pix /= W0;
+        const int y = static_cast<int>(pix % H0);
+        const int im = static_cast<int>(pix / H0);
+        F8 acc;
+        load8(f0 + ((static_cast<long long>(im) * H0 + y) * W0 + x) * C + c8, acc);
+        bilerp_acc(f1 + static_cast<long long>(im) * h1 * w1 * C, h1, w1, C, H0, W0, y, x, c8, acc);
+        bilerp_acc(f2 + static_cast<long long>(im) * h2 * w2 * C, h2, w2, C, H0, W0, y, x, c8, acc);
+        bilerp_acc(f3 + static_cast<long long>(im) * h3 * w3 * C, h3, w3, C, H0, W0, y, x, c8, acc);
+        store8(out + ((static_cast<long long>(im) * H0 + y) * W0 + x) * C + c8, acc);
+    }
+}
+
+__global__ void resize_bf16_kernel(const __nv_bfloat16* __restrict__ x, int n, int hi, int wi, int C, int ho, int wo,
+                                   __nv_bfloat16* __restrict__ y) {
+    const int c8n = C / 8;
+    const long long total = static_cast<long long>(n) * ho * wo * c8n;
+    for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
+         e += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int c8 = static_cast<int>(e % c8n) * 8;
+        long long pix = e / c8n;
+        const int xx = static_cast<int>(pix % wo);
+        pix /= wo;
+        const int yy = static_cast<int>(pix % ho);
+        const int im = static_cast<int>(pix / ho);
+        F8 acc;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc.v[i] = 0.0f;
+        bilerp_acc(x + static_cast<long long>(im) * hi * wi * C, hi, wi, C, ho, wo, yy, xx, c8, acc);
+        store8(y + ((static_cast<long long>(im) * ho + yy) * wo + xx) * C + c8, acc);
+    }
+}
+
+__global__ void im2col_s2_kernel(const __nv_bfloat16* __restrict__ x, int n, int h, int w, int C,
+                                 __nv_bfloat16* __restrict__ out) {
+    const int ho = (h - 1) / 2 + 1, wo = (w - 1) / 2 + 1;
+    const int c8n = C / 8;
+    const long long total = static_cast<long long>(n) * ho * wo * 9 * c8n;
+    for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
+         e += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int c8 = static_cast<int>(e % c8n) * 8;
+        long long r = e / c8n;
+        const int tap = static_cast<int>(r % 9);
+        r /= 9;
+        const int xo = static_cast<int>(r % wo);
+        r /= wo;
+        const int yo = static_cast<int>(r % ho);
+        const int im = static_cast<int>(r / ho);
+        const int yi = 2 * yo + tap / 3 - 1, xi = 2 * xo + tap % 3 - 1;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (yi >= 0 && yi < h && xi >= 0 && xi < w)
+            v = *reinterpret_cast<const uint4*>(x + ((static_cast<long long>(im) * h + yi) * w + xi) * C + c8);
+        *reinterpret_cast<uint4*>(out + e * 8) = v;
+    }
+}
+
+__global__ void head_split_kernel(const float* __restrict__ o4, int n, int h4, int w4, int H, int W,
+                                  float* __restrict__ pts, float* __restrict__ conf) {
+    const long long total = static_cast<long long>(n) * H * W;
+    for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
+         e += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int x = static_cast<int>(e % W);
+        const int y = static_cast<int>((e / W) % H);
+        const int im = static_cast<int>(e / (static_cast<long long>(W) * H));
+        const float4* base = reinterpret_cast<const float4*>(o4) + static_cast<long long>(im) * h4 * w4;
+        float4 v;
+        if (h4 == H && w4 == W) {
+            v = base[static_cast<long long>(y) * w4 + x];
+        } else {
+            int y0, y1, x0, x1;
+            float fy, fx;
+            src_coord(y, h4, H, y0, y1, fy);
+            src_coord(x, w4, W, x0, x1, fx);
+            const float4 a = base[y0 * w4 + x0], b = base[y0 * w4 + x1], c = base[y1 * w4 + x0],
+                         d = base[y1 * w4 + x1];
+            auto lerp2 = [&](float pa, float pb, float pc, float pd) {
+                return (pa * (1.0f - fx) + pb * fx) * (1.0f - fy) + (pc * (1.0f - fx) + pd * fx) * fy;
+            };
+            v = make_float4(lerp2(a.x, b.x, c.x, d.x), lerp2(a.y, b.y, c.y, d.y), lerp2(a.z, b.z, c.z, d.z),
+                            lerp2(a.w, b.w, c.w, d.w));
+        }
+        pts[e * 3 + 0] = v.x;
+        pts[e * 3 + 1] = v.y;
+        pts[e * 3 + 2] = v.z;
+        conf[e] = v.w;
+    }
+}
+
+}  // namespace
+
+void patch_im2col(cudaStream_t s, const uint8_t* img, int n, int H, int W, int p, int kpad, __nv_bfloat16* out) {
+    const long long total = static_cast<long long>(n) * (H / p) * (W / p) * kpad;
+    patch_im2col_kernel<<<grid_for(total, 256), 256, 0, s>>>(img, n, H, W, p, kpad, out);
+    M3R_CUDA(cudaGetLastError());
+}
+
+void layernorm(cudaStream_t s, const float* x, int rows, int D, const float* gamma, const float* beta,
+               __nv_bfloat16* y) {
+    M3R_REQUIRE(D % 4 == 0 && D <= 1024, "layernorm: D must be a multiple of 4 and <= 1024");
+    if (rows == 0) return;
+    const int warps = 8;
+    long long blocks = (rows + warps - 1) / warps;
+    if (blocks > 148LL * 16) blocks = 148LL * 16;
+    layernorm_kernel<<<static_cast<int>(blocks), warps * 32, 0, s>>>(x, rows, D, gamma, beta, y);
+    M3R_CUDA(cudaGetLastError());
+}
+
+void cast_bf16(cudaStream_t s, const float* x, long long n, __nv_bfloat16* y) {
+    M3R_REQUIRE(n % 4 == 0, "cast_bf16: size must be a multiple of 4");
+    cast_bf16_kernel<<<grid_for(n / 4, 256), 256, 0, s>>>(x, n, y);
+    M3R_CUDA(cudaGetLastError());
+}
+
+void dpt_fuse(cudaStream_t s, const __nv_bfloat16* f0, const __nv_bfloat16* f1, int h1, int w1,
+              const __nv_bfloat16* f2, int h2, int w2, const __nv_bfloat16* f3, int h3, int w3, int n, int H0,
+              int W0, int C, __nv_bfloat16* out) {
+    M3R_REQUIRE(C % 8 == 0, "dpt_fuse: C % 8");
+    const long long total = static_cast<long long>(n) * H0 * W0 * (C / 8);
+    dpt_fuse_kernel<<<grid_for(total, 256), 256, 0, s>>>(f0, f1, h1, w1, f2, h2, w2, f3, h3, w3, n, H0, W0, C, out);
+    M3R_CUDA(cudaGetLastError());
+}
+
+void resize_bf16(cudaStream_t s, const __nv_bfloat16* x, int n, int hi, int wi, int C, int ho, int wo,
+                 __nv_bfloat16* y) {
+    M3R_REQUIRE(C % 8 == 0, "resize_bf16: C % 8");
+    const long long total = static_cast<long long>(n) * ho * wo * (C / 8);
+    resize_bf16_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, n, hi, wi, C, ho, wo, y);
+    M3R_CUDA(cudaGetLastError());
+}
+
+void im2col_s2(cudaStream_t s, const __nv_bfloat16* x, int n, int h, int w, int C, __nv_bfloat16* out) {
+    M3R_REQUIRE(C % 8 == 0, "im2col_s2: C % 8");
+    const int ho = (h - 1) / 2 + 1, wo = (w - 1) / 2 + 1;
+    const long long total = static_cast<long long>(n) * ho * wo * 9 * (C / 8);
+    im2col_s2_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, n, h, w, C, out);
+    M3R_CUDA(cudaGetLastError());
+}
+
+void head_split(cudaStream_t s, const float* out4, int n, int h4, int w4, int H, int W, float* pts3d, float* conf) {
+    const long long total = static_cast<long long>(n) * H * W;
+    head_split_kernel<<<grid_for(total, 256), 256, 0, s>>>(out4, n, h4, w4, H, W, pts3d, conf);
+    M3R_CUDA(cudaGetLastError());
+}
+
+}  // namespace m3r

@@ -1,0 +1,558 @@
+// Reciprocal top-k descriptor matcher, bit-exact with the reference CPU matcher
+// (csrc/cpu/matching.cpp:85-237 of the reference).
+//
+// Arithmetic is restated exactly as the reference computes it (its build has no
+// FMA): normalisation s = s + x*x sequentially, n = sqrtf(s), x * (1.0f / n) when
+// n > 1e-8; similarity d = d + a[k]*b[k] for k = 0..D-1, every multiply and add
+// separately rounded (mul.rn / add.rn, never contracted).  On Blackwell the
+// packed mul.rn.f32x2 / add.rn.f32x2 forms do two such operations per
+// instruction without changing a single rounding.
+//
+// Pipeline (one device, rows [row0, row1) of set A against all of set B):
+//   normalize      one thread per row
+//   argmax         128 x 128 tiles, 8 x 8 per thread; row and column maxima of
+//                  every similarity, fused -- the N x N matrix never exists.
+//                  Partial maxima are merged with 64-bit atomicMax on keys
+//                  (orderable(value) << 32) | (0xFFFFFFFF - index): the maximum
+//                  key is the maximum value with the lowest index, which is the
+//                  reference's strict-> first-wins rule.
+//   candidates     reciprocal test nn_21[nn_12[i]] == i and sim >= threshold,
+//                  compacted in ascending i (the reference's push_back order)
+//   top-k          when more than top_k survive: radix select (16-bit digits) of
+//                  the top_k largest (conf, -i) keys, then a bitonic sort of
+//                  those, i.e. confidence descending, idx_1 ascending on ties.
+#include <algorithm>
+#include <vector>
+
+#include "matcher.h"
+#include "tmap.h"
+
+namespace m3r {
+
+namespace {
+
+__device__ __forceinline__ uint32_t orderable(float f) {
+    f = f + 0.0f;  // -0.0 -> +0.0: the reference's > comparison treats them as equal
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ float from_orderable(uint32_t k) {
+    const uint32_t u = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
+    return __uint_as_float(u);
+}
+
+__device__ __forceinline__ unsigned long long make_key(float v, uint32_t idx) {
+    return (static_cast<unsigned long long>(orderable(v)) << 32) | (0xFFFFFFFFu - idx);
+}
+
+// ------------------------------------------------------------------ normalize
+__global__ void normalize_kernel(const float* __restrict__ in, float* __restrict__ out, long long n, int d) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const float* r = in + i * d;
+        float* o = out + i * d;
+        float s = 0.0f;
+        for (int k = 0; k < d; ++k) s = __fadd_rn(s, __fmul_rn(r[k], r[k]));
+        s = sqrtf(s);
+        if (s > 1e-8f) {
+            const float inv = 1.0f / s;
+            for (int k = 0; k < d; ++k) o[k] = __fmul_rn(r[k], inv);
+        } else {
+            for (int k = 0; k < d; ++k) o[k] = r[k];
+        }
+    }
+}
+
+// ------------------------------------------------------------------ argmax
+constexpr int kTI = 128;  // rows per CTA tile
+constexpr int kTJ = 128;  // columns per j-tile
+constexpr int kKC = 32;   // k chunk held in shared memory
+constexpr int kPitch = 128 + 4;
+
+__device__ __forceinline__ unsigned long long dup2(float a) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(a));
+    return r;
+}
+__device__ __forceinline__ unsigned long long pack2(float a, float b) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void unpack2(unsigned long long v, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+// acc = acc + a * b, elementwise on float pairs, each operation rounded separately.
+__device__ __forceinline__ void mul_add2(unsigned long long& acc, unsigned long long a, unsigned long long b) {
+    unsigned long long t;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(t) : "l"(a), "l"(b));
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(acc) : "l"(acc), "l"(t));
+}
+
+// Thread (tr, tc) of a 16 x 16 grid owns rows tr*8 .. +8 and columns
+// {tc*4 .. +4} U {64 + tc*4 .. +4} of the 128 x 128 tile.  Warp w holds
+// tr in [4*(w/2), +4), tc in [8*(w%2), +8): lane = tr_l * 8 + tc_l.
+template <int DFIX>
+__global__ void __launch_bounds__(256, 2)
+    argmax_kernel(const float* __restrict__ A, const float* __restrict__ B, long long row0, long long row1, long long n2,
+                  int dyn_d, int n_seg, unsigned long long* __restrict__ rowkey, unsigned long long* __restrict__ colkey) {
+    const int D = DFIX > 0 ? DFIX : dyn_d;
+    __shared__ __align__(16) float sA[kKC][kPitch];
+    __shared__ __align__(16) float sB[kKC][kPitch];
+    __shared__ unsigned long long sCol[4][kTJ];
+    __shared__ unsigned long long sRow[2][kTI];
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int tr = 4 * (warp >> 1) + (lane >> 3);
+    const int tc = 8 * (warp & 1) + (lane & 7);
+    const long long i0 = row0 + static_cast<long long>(blockIdx.x) * kTI;
+    const int seg = blockIdx.y;
+    const long long jt_per_seg = ((n2 + kTJ - 1) / kTJ + n_seg - 1) / n_seg;
+    const long long jt_begin = seg * jt_per_seg;
+    long long jt_end = jt_begin + jt_per_seg;
+    const long long jt_total = (n2 + kTJ - 1) / kTJ;
+    if (jt_end > jt_total) jt_end = jt_total;
+
+    float rbest[8];
+    uint32_t ridx[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+        rbest[r] = -INFINITY;
+        ridx[r] = 0xFFFFFFFFu;
+    }
+
+    const bool a_resident = D <= kKC;
+    for (long long jt = jt_begin; jt < jt_end; ++jt) {
+        const long long j0 = jt * kTJ;
+        unsigned long long acc[8][4];
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[r][c] = 0ull;
+
+        for (int kc = 0; kc < D; kc += kKC) {
+            const int kn = D - kc < kKC ? D - kc : kKC;
+            __syncthreads();
+            // stage transposed chunks: thread t writes column (row t&127) for k in its half
+            if (!a_resident || jt == jt_begin) {
+                for (int e = tid; e < kTI * kn; e += 256) {
+                    const int rr = e % kTI, k = e / kTI;
+                    const long long gi = i0 + rr;
+                    sA[k][rr] = gi < row1 ? A[gi * D + kc + k] : 0.0f;
+                }
+            }
+            for (int e = tid; e < kTJ * kn; e += 256) {
+                const int cc = e % kTJ, k = e / kTJ;
+                const long long gj = j0 + cc;
+                sB[k][cc] = gj < n2 ? B[gj * D + kc + k] : 0.0f;
+            }
+            __syncthreads();
+            const int KN = DFIX > 0 ? (DFIX < kKC ? DFIX : kKC) : kKC;
+#pragma unroll
+            for (int k = 0; k < KN; ++k) {
+                if (DFIX == 0 && k >= kn) break;
+                const float4 a0 = *reinterpret_cast<const float4*>(&sA[k][tr * 8]);
+                const float4 a1 = *reinterpret_cast<const float4*>(&sA[k][tr * 8 + 4]);
+                const float4 b0 = *reinterpret_cast<const float4*>(&sB[k][tc * 4]);
+                const float4 b1 = *reinterpret_cast<const float4*>(&sB[k][64 + tc * 4]);
+                const unsigned long long bp[4] = {pack2(b0.x, b0.y), pack2(b0.z, b0.w), pack2(b1.x, b1.y),
+                                                  pack2(b1.z, b1.w)};
+                const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+                for (int r = 0; r < 8; ++r) {
+                    const unsigned long long ad = dup2(av[r]);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) mul_add2(acc[r][c], ad, bp[c]);
+                }
+            }
+        }
+
+        // unpack: s[r][c], c in 0..7 -> column j0 + (c < 4 ? tc*4 + c : 64 + tc*4 + c - 4)
+        float s[8][8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) unpack2(acc[r][c], s[r][2 * c], s[r][2 * c + 1]);
+
+        // ---- rows: first (lowest j) maximum over this thread's columns, in increasing j
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            float m = -INFINITY;
+            int mc = -1;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const long long j = j0 + (c < 4 ? tc * 4 + c : 64 + tc * 4 + c - 4);
+                if (j < n2 && s[r][c] > m) {
+                    m = s[r][c];
+                    mc = c;
+                }
+            }
+            if (mc >= 0 && m > rbest[r]) {
+                rbest[r] = m;
+                ridx[r] = static_cast<uint32_t>(j0 + (mc < 4 ? tc * 4 + mc : 64 + tc * 4 + mc - 4));
+            }
+        }
+
+        // ---- columns: first (lowest i) maximum over this thread's rows, keyed
+        unsigned long long ck[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            float m = -INFINITY;
+            int mr = -1;
+#pragma unroll
+            for (int r = 0; r < 8; ++r)
+                if (i0 + tr * 8 + r < row1 && s[r][c] > m) {
+                    m = s[r][c];
+                    mr = r;
+                }
+            ck[c] = mr >= 0 ? make_key(m, static_cast<uint32_t>(i0 + tr * 8 + mr)) : 0ull;
+            // reduce over the 4 row groups of this warp (lanes differing in bits 3, 4)
+#pragma unroll
+            for (int o = 8; o <= 16; o <<= 1) {
+                const unsigned long long other = __shfl_xor_sync(0xffffffffu, ck[c], o);
+                ck[c] = other > ck[c] ? other : ck[c];
+            }
+        }
+        if ((lane >> 3) == 0) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) sCol[warp >> 1][c < 4 ? tc * 4 + c : 64 + tc * 4 + c - 4] = ck[c];
+        }
+        __syncthreads();
+        if (tid < kTJ) {
+            unsigned long long k = sCol[0][tid];
+#pragma unroll
+            for (int w = 1; w < 4; ++w) k = sCol[w][tid] > k ? sCol[w][tid] : k;
+            if (j0 + tid < n2 && k != 0ull) atomicMax(colkey + j0 + tid, k);
+        }
+    }
+
+    // ---- row keys: reduce over the 8 column groups of the warp (lane bits 0..2), then the 2 warps
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+        unsigned long long k = ridx[r] != 0xFFFFFFFFu ? make_key(rbest[r], ridx[r]) : 0ull;
+#pragma unroll
+        for (int o = 1; o <= 4; o <<= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, k, o);
+            k = other > k ? other : k;
+        }
+        if ((lane & 7) == 0) sRow[warp & 1][tr * 8 + r] = k;
+    }
+    __syncthreads();
+    if (tid < kTI) {
+        const unsigned long long k = sRow[0][tid] > sRow[1][tid] ? sRow[0][tid] : sRow[1][tid];
+        if (i0 + tid < row1 && k != 0ull) atomicMax(rowkey + (i0 + tid - row0), k);
+    }
+}
+
+// ------------------------------------------------------------------ candidates
+// flag(i) = reciprocal test and threshold; per-block counts, then ordered scatter.
+__device__ __forceinline__ bool cand_flag(const unsigned long long* rowkey, const unsigned long long* colkey,
+                                          long long i_local, long long row0, int reciprocal, float thr,
+                                          uint32_t& j_out, float& v_out) {
+    const unsigned long long rk = rowkey[i_local];
+    if (rk == 0ull) return false;
+    const uint32_t j = 0xFFFFFFFFu - static_cast<uint32_t>(rk & 0xFFFFFFFFu);
+    const float v = from_orderable(static_cast<uint32_t>(rk >> 32));
+    j_out = j;
+    v_out = v;
+    if (reciprocal) {
+        const unsigned long long ck = colkey[j];
+        const long long i21 = 0xFFFFFFFFu - static_cast<uint32_t>(ck & 0xFFFFFFFFu);
+        if (i21 != row0 + i_local) return false;
+    }
+    return v >= thr;
+}
+
+constexpr int kCandBlock = 1024;
+
+__global__ void cand_count_kernel(const unsigned long long* __restrict__ rowkey,
+                                  const unsigned long long* __restrict__ colkey, long long nrows, long long row0,
+                                  int reciprocal, float thr, int* __restrict__ block_counts) {
+    __shared__ int s_cnt;
+    if (threadIdx.x == 0) s_cnt = 0;
+    __syncthreads();
+    const long long i = static_cast<long long>(blockIdx.x) * kCandBlock + threadIdx.x;
+    uint32_t j;
+    float v;
+    const bool f = i < nrows && cand_flag(rowkey, colkey, i, row0, reciprocal, thr, j, v);
+    const unsigned bal = __ballot_sync(0xffffffffu, f);
+    if ((threadIdx.x & 31) == 0 && bal) atomicAdd(&s_cnt, __popc(bal));
+    __syncthreads();
+    if (threadIdx.x == 0) block_counts[blockIdx.x] = s_cnt;
+}
+
+__global__ void scan_counts_kernel(int* __restrict__ counts, int n, int* __restrict__ total) {
+    // single block: exclusive scan in place
+    __shared__ int s_carry;
+    if (threadIdx.x == 0) s_carry = 0;
+    __syncthreads();
+    for (int base = 0; base < n; base += blockDim.x) {
+        const int i = base + threadIdx.x;
+        const int v = i < n ? counts[i] : 0;
+        // inclusive scan within the block
+        __shared__ int tmp[1024];
+        tmp[threadIdx.x] = v;
+        __syncthreads();
+        for (int o = 1; o < blockDim.x; o <<= 1) {
+            const int t = threadIdx.x >= o ? tmp[threadIdx.x - o] : 0;
+            __syncthreads();
+            tmp[threadIdx.x] += t;
+            __syncthreads();
+        }
+        if (i < n) counts[i] = s_carry + tmp[threadIdx.x] - v;
+        __syncthreads();
+        if (threadIdx.x == blockDim.x - 1) s_carry += tmp[threadIdx.x];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) *total = s_carry;
+}
+
+__global__ void cand_scatter_kernel(const unsigned long long* __restrict__ rowkey,
+                                    const unsigned long long* __restrict__ colkey, long long nrows, long long row0,
+                                    int reciprocal, float thr, const int* __restrict__ block_offsets,
+                                    unsigned long long* __restrict__ ckey, uint32_t* __restrict__ cj) {
+    __shared__ int s_warp[kCandBlock / 32];
+    const long long i = static_cast<long long>(blockIdx.x) * kCandBlock + threadIdx.x;
+    uint32_t j = 0;
+    float v = 0.0f;
+    const bool f = i < nrows && cand_flag(rowkey, colkey, i, row0, reciprocal, thr, j, v);
+    const unsigned bal = __ballot_sync(0xffffffffu, f);
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    if (lane == 0) s_warp[w] = __popc(bal);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int acc = 0;
+        for (int k = 0; k < kCandBlock / 32; ++k) {
+            const int t = s_warp[k];
+            s_warp[k] = acc;
+            acc += t;
+        }
+    }
+    __syncthreads();
+    if (f) {
+        const int pos = block_offsets[blockIdx.x] + s_warp[w] + __popc(bal & ((1u << lane) - 1u));
+        ckey[pos] = make_key(v, static_cast<uint32_t>(row0 + i));
+        cj[pos] = j;
+    }
+}
+
+// ------------------------------------------------------------------ top-k (radix select + sort)
+__global__ void radix_hist_kernel(const unsigned long long* __restrict__ keys, int n, int shift,
+                                  const unsigned long long* __restrict__ state, int prefix_bits,
+                                  unsigned* __restrict__ hist) {
+    const unsigned long long prefix = state[0];
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const unsigned long long k = keys[i];
+        if (prefix_bits > 0 && (k >> (64 - prefix_bits)) != prefix) continue;
+        atomicAdd(hist + ((k >> shift) & 0xFFFFull), 1u);
+    }
+}
+
+// single thread: pick the digit bucket that holds the remaining-th largest key
+__global__ void radix_pick_kernel(unsigned* __restrict__ hist, unsigned long long* __restrict__ state) {
+    // state[0] = prefix, state[1] = remaining
+    unsigned long long remaining = state[1];
+    unsigned long long cum = 0;
+    int b = 65535;
+    for (; b >= 0; --b) {
+        if (cum + hist[b] >= remaining) break;
+        cum += hist[b];
+    }
+    if (b < 0) b = 0;
+    state[0] = (state[0] << 16) | static_cast<unsigned long long>(b);
+    state[1] = remaining - cum;
+    for (int i = 0; i < 65536; ++i) hist[i] = 0;
+}
+
+__global__ void select_ge_kernel(const unsigned long long* __restrict__ keys, const uint32_t* __restrict__ cj,
+                                 int n, const unsigned long long* __restrict__ kth,
+                                 unsigned long long* __restrict__ out_key, uint32_t* __restrict__ out_j,
+                                 int* __restrict__ counter) {
+    const unsigned long long t = kth[0];
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        if (keys[i] >= t) {
+            const int pos = atomicAdd(counter, 1);
+            out_key[pos] = keys[i];
+            out_j[pos] = cj[i];
+        }
+    }
+}
+
+// single block bitonic sort, descending by key, n <= 4096 (padded to a power of two)
+__global__ void sort_desc_kernel(unsigned long long* __restrict__ key, uint32_t* __restrict__ val, int n) {
+    __shared__ unsigned long long sk[4096];
+    __shared__ uint32_t sv[4096];
+    int m = 1;
+    while (m < n) m <<= 1;
+    for (int i = threadIdx.x; i < m; i += blockDim.x) {
+        sk[i] = i < n ? key[i] : 0ull;
+        sv[i] = i < n ? val[i] : 0u;
+    }
+    __syncthreads();
+    for (int size = 2; size <= m; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = threadIdx.x; i < m; i += blockDim.x) {
+                const int partner = i ^ stride;
+                if (partner > i) {
+                    const bool desc = (i & size) == 0;
+                    const bool swap = desc ? (sk[i] < sk[partner]) : (sk[i] > sk[partner]);
+                    if (swap) {
+                        const unsigned long long tk = sk[i];
+                        sk[i] = sk[partner];
+                        sk[partner] = tk;
+                        const uint32_t tv = sv[i];
+                        sv[i] = sv[partner];
+                        sv[partner] = tv;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        key[i] = sk[i];
+        val[i] = sv[i];
+    }
+}
+
+__global__ void finalize_kernel(const unsigned long long* __restrict__ key, const uint32_t* __restrict__ cj, int n,
+                                long long* __restrict__ idx1, long long* __restrict__ idx2,
+                                float* __restrict__ conf) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const unsigned long long k = key[i];
+        idx1[i] = static_cast<long long>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFu));
+        idx2[i] = static_cast<long long>(cj[i]);
+        conf[i] = from_orderable(static_cast<uint32_t>(k >> 32));
+    }
+}
+
+__global__ void decode_keys_kernel(const unsigned long long* __restrict__ key, long long n, int32_t* __restrict__ idx) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+        idx[i] = static_cast<int32_t>(0xFFFFFFFFu - static_cast<uint32_t>(key[i] & 0xFFFFFFFFu));
+}
+
+int blocks_for(long long n, int b) {
+    long long g = (n + b - 1) / b;
+    if (g > 148LL * 16) g = 148LL * 16;
+    return static_cast<int>(g < 1 ? 1 : g);
+}
+
+}  // namespace
+
+MatchWorkspace::~MatchWorkspace() { release(); }
+
+void MatchWorkspace::release() {
+    for (void** p : {reinterpret_cast<void**>(&a), reinterpret_cast<void**>(&b), reinterpret_cast<void**>(&rowkey),
+                     reinterpret_cast<void**>(&colkey), reinterpret_cast<void**>(&counts),
+                     reinterpret_cast<void**>(&ckey), reinterpret_cast<void**>(&cj),
+                     reinterpret_cast<void**>(&hist), reinterpret_cast<void**>(&state),
+                     reinterpret_cast<void**>(&skey), reinterpret_cast<void**>(&sj), reinterpret_cast<void**>(&misc),
+                     reinterpret_cast<void**>(&idx1), reinterpret_cast<void**>(&idx2),
+                     reinterpret_cast<void**>(&conf)}) {
+        if (*p) cudaFree(*p);
+        *p = nullptr;
+    }
+    cap_n = 0;
+    cap_d = 0;
+}
+
+void MatchWorkspace::reserve(long long n, int d) {
+    if (n <= cap_n && d <= cap_d) return;
+    release();
+    const long long nn = n > 0 ? n : 1;
+    const int dd = d > 0 ? d : 1;
+    M3R_CUDA(cudaMalloc(&a, sizeof(float) * nn * dd));
+    M3R_CUDA(cudaMalloc(&b, sizeof(float) * nn * dd));
+    M3R_CUDA(cudaMalloc(&rowkey, sizeof(unsigned long long) * nn));
+    M3R_CUDA(cudaMalloc(&colkey, sizeof(unsigned long long) * nn));
+    M3R_CUDA(cudaMalloc(&counts, sizeof(int) * ((nn + kCandBlock - 1) / kCandBlock + 1)));
+    M3R_CUDA(cudaMalloc(&ckey, sizeof(unsigned long long) * nn));
+    M3R_CUDA(cudaMalloc(&cj, sizeof(uint32_t) * nn));
+    M3R_CUDA(cudaMalloc(&hist, sizeof(unsigned) * 65536));
+    M3R_CUDA(cudaMalloc(&state, sizeof(unsigned long long) * 2));
+    M3R_CUDA(cudaMalloc(&skey, sizeof(unsigned long long) * 4096));
+    M3R_CUDA(cudaMalloc(&sj, sizeof(uint32_t) * 4096));
+    M3R_CUDA(cudaMalloc(&misc, sizeof(int) * 4));
+    M3R_CUDA(cudaMalloc(&idx1, sizeof(long long) * nn));
+    M3R_CUDA(cudaMalloc(&idx2, sizeof(long long) * nn));
+    M3R_CUDA(cudaMalloc(&conf, sizeof(float) * nn));
+    M3R_CUDA(cudaMemset(hist, 0, sizeof(unsigned) * 65536));
+    cap_n = n;
+    cap_d = d;
+}
+
+void match_normalize(cudaStream_t s, const float* in, float* out, long long n, int d) {
+    if (n == 0) return;
+    normalize_kernel<<<blocks_for(n, 256), 256, 0, s>>>(in, out, n, d);
+    M3R_CUDA(cudaGetLastError());
+}
+
+void match_argmax(cudaStream_t s, const float* a_norm, const float* b_norm, long long row0, long long row1,
+                  long long n2, int d, unsigned long long* rowkey, unsigned long long* colkey, bool clear_colkey) {
+    const long long nrows = row1 - row0;
+    if (nrows > 0) M3R_CUDA(cudaMemsetAsync(rowkey, 0, sizeof(unsigned long long) * nrows, s));
+    if (clear_colkey && n2 > 0) M3R_CUDA(cudaMemsetAsync(colkey, 0, sizeof(unsigned long long) * n2, s));
+    if (nrows <= 0 || n2 <= 0) return;
+    const long long row_blocks = (nrows + kTI - 1) / kTI;
+    const long long jt_total = (n2 + kTJ - 1) / kTJ;
+    // column segments: enough CTAs for ~8 waves of 2 CTAs per SM
+    long long seg = (148LL * 2 * 8 + row_blocks - 1) / row_blocks;
+    if (seg > jt_total) seg = jt_total;
+    if (seg < 1) seg = 1;
+    if (seg > 65535) seg = 65535;
+    M3R_REQUIRE(row_blocks <= 0x7FFFFFFFLL, "match: too many rows");
+    dim3 grid(static_cast<unsigned>(row_blocks), static_cast<unsigned>(seg));
+    if (d == 24)
+        argmax_kernel<24><<<grid, 256, 0, s>>>(a_norm, b_norm, row0, row1, n2, d, static_cast<int>(seg), rowkey,
+                                               colkey);
+    else
+        argmax_kernel<0><<<grid, 256, 0, s>>>(a_norm, b_norm, row0, row1, n2, d, static_cast<int>(seg), rowkey, colkey);
+    M3R_CUDA(cudaGetLastError());
+}
+
+int match_select(cudaStream_t s, MatchWorkspace& ws, long long nrows, long long row0, int reciprocal, float thr,
+                 int top_k) {
+    if (nrows <= 0) return 0;
+    const int nblk = static_cast<int>((nrows + kCandBlock - 1) / kCandBlock);
+    int* total_d = ws.misc;
+    cand_count_kernel<<<nblk, kCandBlock, 0, s>>>(ws.rowkey, ws.colkey, nrows, row0, reciprocal, thr, ws.counts);
+    scan_counts_kernel<<<1, 1024, 0, s>>>(ws.counts, nblk, total_d);
+    cand_scatter_kernel<<<nblk, kCandBlock, 0, s>>>(ws.rowkey, ws.colkey, nrows, row0, reciprocal, thr, ws.counts,
+                                                    ws.ckey, ws.cj);
+    M3R_CUDA(cudaGetLastError());
+    int total = 0;
+    M3R_CUDA(cudaMemcpyAsync(&total, total_d, sizeof(int), cudaMemcpyDeviceToHost, s));
+    M3R_CUDA(cudaStreamSynchronize(s));
+    int m = total;
+    if (total > top_k) {
+        M3R_REQUIRE(top_k <= 4096, "match: top_k must be <= 4096");
+        unsigned long long st[2] = {0ull, static_cast<unsigned long long>(top_k)};
+        M3R_CUDA(cudaMemcpyAsync(ws.state, st, sizeof(st), cudaMemcpyHostToDevice, s));
+        for (int pass = 0; pass < 4; ++pass) {
+            radix_hist_kernel<<<blocks_for(total, 256), 256, 0, s>>>(ws.ckey, total, 48 - 16 * pass, ws.state,
+                                                                      16 * pass, ws.hist);
+            radix_pick_kernel<<<1, 1, 0, s>>>(ws.hist, ws.state);
+        }
+        M3R_CUDA(cudaMemsetAsync(ws.misc + 1, 0, sizeof(int), s));
+        select_ge_kernel<<<blocks_for(total, 256), 256, 0, s>>>(ws.ckey, ws.cj, total, ws.state, ws.skey, ws.sj,
+                                                                 ws.misc + 1);
+        sort_desc_kernel<<<1, 1024, 0, s>>>(ws.skey, ws.sj, top_k);
+        finalize_kernel<<<blocks_for(top_k, 256), 256, 0, s>>>(ws.skey, ws.sj, top_k, ws.idx1, ws.idx2, ws.conf);
+        m = top_k;
+    } else if (total > 0) {
+        finalize_kernel<<<blocks_for(total, 256), 256, 0, s>>>(ws.ckey, ws.cj, total, ws.idx1, ws.idx2, ws.conf);
+    }
+    M3R_CUDA(cudaGetLastError());
+    return m;
+}
+
+void match_decode(cudaStream_t s, const unsigned long long* keys, long long n, int32_t* idx) {
+    if (n <= 0) return;
+    decode_keys_kernel<<<blocks_for(n, 256), 256, 0, s>>>(keys, n, idx);
+    M3R_CUDA(cudaGetLastError());
+}
+
+}  // namespace m3r

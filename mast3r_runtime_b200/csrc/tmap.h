@@ -1,0 +1,55 @@
+// Host-side TMA tensor-map encoding (cuTensorMapEncodeTiled through the runtime's
+// driver entry point, so the library does not link libcuda directly).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <stdexcept>
+#include <string>
+
+namespace m3r {
+
+struct Error : std::runtime_error {
+    int code;
+    Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+// Status codes of the C ABI (include/m3r_cuda.h)
+constexpr int kOk = 0;
+constexpr int kErrArg = -1;
+constexpr int kErrIo = -2;
+constexpr int kErrCuda = -3;
+constexpr int kErrNccl = -4;
+constexpr int kErrTimeout = -5;
+constexpr int kErrState = -6;
+constexpr int kErrNoMem = -7;
+
+#define M3R_CUDA(call)                                                                                 \
+    do {                                                                                               \
+        cudaError_t e_ = (call);                                                                       \
+        if (e_ != cudaSuccess)                                                                         \
+            throw ::m3r::Error(e_ == cudaErrorMemoryAllocation ? ::m3r::kErrNoMem : ::m3r::kErrCuda,   \
+                               std::string(#call) + ": " + cudaGetErrorString(e_) + " (" + __FILE__ + \
+                                   ":" + std::to_string(__LINE__) + ")");                              \
+    } while (0)
+
+#define M3R_REQUIRE(cond, msg)                                            \
+    do {                                                                  \
+        if (!(cond)) throw ::m3r::Error(::m3r::kErrArg, std::string(msg)); \
+    } while (0)
+
+// bf16 row-major matrix [rows, cols] with row stride ld (elements); box
+// [box_rows, 64] with 128-byte swizzle.  Out-of-bounds boxes read zero.
+CUtensorMap tmap_bf16_2d(const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows);
+
+// bf16 tensor [d2, d1, 64] (innermost 64 = head dim), box [box_d1, 64].
+CUtensorMap tmap_bf16_3d_rows64(const void* ptr, uint64_t d1, uint64_t d2, uint32_t box_d1);
+
+// bf16 NHWC tensor [n, h, w, c] (row stride of a pixel = cstride elements), box
+// [1, hbox, wbox, 64].
+CUtensorMap tmap_bf16_nhwc(const void* ptr, uint64_t n, uint64_t h, uint64_t w, uint64_t c, uint64_t cstride,
+                           uint32_t hbox, uint32_t wbox);
+
+}  // namespace m3r

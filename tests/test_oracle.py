@@ -1,0 +1,162 @@
+"""The oracle is pinned before it is trusted: its restatements are checked against the
+golden fixtures that tests/golden/make_golden.py produced by running the reference's own
+code, and against the reference's known-answer tests (tests/unit/test_matching.py)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, matcher_inputs, rel_l2
+
+
+# ---------------------------------------------------------------------------- model restatement
+@pytest.fixture(scope="module")
+def tiny_model():
+    from make_golden import seeded_images
+    from mast3r_runtime_b200.weights import make_weights, tiny_dims
+    from oracle import model as om
+
+    g = np.load(GOLDEN / "model_tiny.npz")
+    d = tiny_dims()
+    w = make_weights(d, seed=int(g["model_seed"]), randomize_affine=True)
+    m = om.Model(w, d)
+    img1, img2 = seeded_images()
+    return g, m, img1, img2
+
+
+def test_encoder_matches_reference(tiny_model):
+    from oracle import model as om
+
+    g, m, img1, img2 = tiny_model
+    e1, _ = m.encode(om.preprocess(img1))
+    e2, _ = m.encode(om.preprocess(img2))
+    assert rel_l2(e1, g["enc_1"]) < 1e-5
+    assert rel_l2(e2, g["enc_2"]) < 1e-5
+
+
+def test_decoder_matches_reference(tiny_model):
+    from oracle import model as om
+
+    g, m, img1, img2 = tiny_model
+    e1, grid = m.encode(om.preprocess(img1))
+    e2, _ = m.encode(om.preprocess(img2))
+    (d1, _), (d2, _) = m.decode(e1, e2, grid)
+    assert rel_l2(d1, g["dec_1"]) < 1e-5
+    assert rel_l2(d2, g["dec_2"]) < 1e-5
+
+
+def test_ref_simple_head_matches_reference(tiny_model):
+    from oracle import model as om
+
+    g, m, img1, img2 = tiny_model
+    e1, grid = m.encode(om.preprocess(img1))
+    e2, _ = m.encode(om.preprocess(img2))
+    (d1, _), _ = m.decode(e1, e2, grid)
+    pts, desc, conf = m.ref_simple_head("downstream_head1", e1, d1, grid, tuple(g["image_hw"]))
+    assert rel_l2(pts, g["ref_simple_pts3d_1"]) < 1e-5
+    assert rel_l2(conf, g["ref_simple_conf_1"]) < 1e-5
+    assert rel_l2(desc[..., :32], g["ref_simple_desc_1"]) < 1e-5
+
+
+def test_rope_matches_reference():
+    from oracle import model as om
+
+    g = np.load(GOLDEN / "model_tiny.npz")
+    cos, sin = om.rope_tables(g["positions"], 64)
+    out = om.rope(g["rope_in"][0].astype(np.float64), cos, sin)
+    assert rel_l2(out, g["rope_out"][0]) < 1e-6
+
+
+def test_full_forward_outputs_are_sane(tiny_model):
+    g, m, img1, img2 = tiny_model
+    out = m.forward(img1, img2)
+    H, W = g["image_hw"]
+    for v in (1, 2):
+        assert out[f"pts3d_{v}"].shape == (H, W, 3)
+        assert out[f"conf_{v}"].shape == (H, W)
+        assert out[f"desc_{v}"].shape == (H, W, 24)
+        np.testing.assert_allclose(np.linalg.norm(out[f"desc_{v}"], axis=-1), 1.0, rtol=1e-6)
+        assert np.isfinite(out[f"pts3d_{v}"]).all()
+
+
+def test_bilinear_half_pixel_matches_closed_form():
+    from oracle import model as om
+
+    x = np.arange(4, dtype=np.float64).reshape(1, 4, 1)
+    y = om.resize_bilinear(x, 1, 8)[0, :, 0]
+    # PyTorch / MPSGraph align_corners=False: src = (i + 0.5) / 2 - 0.5, clamped at 0
+    np.testing.assert_allclose(y, [0, 0.25, 0.75, 1.25, 1.75, 2.25, 2.75, 3.0])
+
+
+# ---------------------------------------------------------------------------- matcher restatement
+def test_matcher_golden_cpp_and_numpy(oracle_lib):
+    z = np.load(GOLDEN / "matcher.npz")
+    for ci, (h, w, d, seed, top_k, recip, thr_m) in enumerate(z["cases"]):
+        a, b = matcher_inputs(int(h), int(w), int(d), int(seed))
+        o = oracle_lib.match(a, b, top_k=int(top_k), reciprocal=bool(recip), confidence_threshold=thr_m / 1000.0)
+        ref1, ref2, refc = z[f"c{ci}_cpp_idx_1"], z[f"c{ci}_cpp_idx_2"], z[f"c{ci}_cpp_confidence"]
+        assert len(o["idx_1"]) == len(ref1)
+        # same matches with bit-identical confidences (ordering of equal confidences is unspecified
+        # in the reference's partial_sort, so compare as sets keyed by the pair)
+        got = {(int(i), int(j)): c for i, j, c in zip(o["idx_1"], o["idx_2"], o["confidence"])}
+        want = {(int(i), int(j)): c for i, j, c in zip(ref1, ref2, refc)}
+        assert got.keys() == want.keys()
+        assert all(np.float32(got[k]).tobytes() == np.float32(want[k]).tobytes() for k in got)
+        # numpy reference: same match set (its confidences differ in the last bits: BLAS dot order)
+        np_set = set(zip(z[f"c{ci}_np_idx_1"].tolist(), z[f"c{ci}_np_idx_2"].tolist()))
+        assert len(np_set ^ set(got.keys())) <= max(2, len(got) // 50)
+        # pts2d = (idx % W, idx // W)
+        np.testing.assert_array_equal(o["pts2d_1"][:, 0], o["idx_1"] % w)
+        np.testing.assert_array_equal(o["pts2d_1"][:, 1], o["idx_1"] // w)
+
+
+def test_matcher_against_reference_cpp_live(oracle_lib):
+    if oracle_lib.ref_lib() is None:
+        pytest.skip("oracle/_ref not built (reference tree absent)")
+    for seed, (h, w, d) in enumerate([(24, 32, 24), (8, 8, 64), (3, 5, 24)]):
+        a, b = matcher_inputs(h, w, d, 100 + seed)
+        for recip in (True, False):
+            o = oracle_lib.match(a, b, top_k=64, reciprocal=recip, confidence_threshold=0.0)
+            r = oracle_lib.ref_match(a, b, top_k=64, reciprocal=recip, confidence_threshold=0.0)
+            assert set(zip(o["idx_1"], o["idx_2"])) == set(zip(r["idx_1"], r["idx_2"]))
+
+
+def test_matcher_kats(oracle_lib):
+    # tests/unit/test_matching.py:27-35: [3, 4] -> [0.6, 0.8]
+    n = oracle_lib.normalize(np.array([[3.0, 4.0], [1.0, 0.0]], np.float32))
+    np.testing.assert_allclose(n, [[0.6, 0.8], [1.0, 0.0]], rtol=1e-7)
+    # zero vectors stay finite (matching.cpp:38 skips the division)
+    assert np.isfinite(oracle_lib.normalize(np.zeros((1, 3), np.float32))).all()
+    # identical descriptors -> identity matches (test_matching.py:234-240)
+    rng = np.random.default_rng(0)
+    desc = rng.random((8, 8, 64)).astype(np.float32)
+    r = oracle_lib.match(desc, desc, reciprocal=True, confidence_threshold=0.0)
+    np.testing.assert_array_equal(r["idx_1"], r["idx_2"])
+    # top_k cap (test_matching.py:190-195)
+    a, b = matcher_inputs(24, 24, 24, 3)
+    assert len(oracle_lib.match(a, b, top_k=10)["idx_1"]) <= 10
+    # reciprocal <= non-reciprocal; threshold monotone (test_matching.py:197-212)
+    assert len(oracle_lib.match(a, b, reciprocal=True, top_k=4096)["idx_1"]) <= len(
+        oracle_lib.match(a, b, reciprocal=False, top_k=4096)["idx_1"])
+    assert len(oracle_lib.match(a, b, confidence_threshold=0.9)["idx_1"]) <= len(
+        oracle_lib.match(a, b, confidence_threshold=0.0)["idx_1"])
+    # orthogonal sets: nothing passes 0.5 (test_matching.py:341-355)
+    d1 = np.zeros((4, 4, 64), np.float32)
+    d1[..., :32] = 1.0
+    d2 = np.zeros((4, 4, 64), np.float32)
+    d2[..., 32:] = 1.0
+    assert len(oracle_lib.match(d1, d2, confidence_threshold=0.5)["idx_1"]) == 0
+
+
+def test_matcher_ties_lowest_index(oracle_lib):
+    # all-equal descriptors: every similarity ties; nn_12 = 0 for every row, nn_21 = 0 for every column
+    d = np.ones((4, 4, 24), np.float32)
+    r = oracle_lib.match(d, d, top_k=16, confidence_threshold=0.0, with_nn=True)
+    assert (r["nn_12"] == 0).all() and (r["nn_21"] == 0).all()
+    assert r["idx_1"].tolist() == [0] and r["idx_2"].tolist() == [0]
+
+
+def test_matcher_empty(oracle_lib):
+    d = np.zeros((0, 0, 64), np.float32)
+    assert len(oracle_lib.match(d, d)["idx_1"]) == 0
