@@ -41,6 +41,12 @@ extern "C" {
 
 #define M3R_MAX_DEVICES 16
 
+/* 16-bit tensor-core operand type (fp32 accumulation and fp32 residual stream in
+ * both).  The reference's precision names map as: "fp16" (its default) and "fp32"
+ * -> M3R_DTYPE_F16, "bf16" -> M3R_DTYPE_BF16. */
+#define M3R_DTYPE_BF16 0
+#define M3R_DTYPE_F16 1
+
 /* Model architecture + runtime shape.  Dimensions follow the reference's model
  * table (csrc/common/types.hpp:51-69, csrc/mps/graph_builder.hpp:67-77). */
 typedef struct m3r_config {
@@ -53,6 +59,7 @@ typedef struct m3r_config {
     int n_devices;      /* 0 = device 0 only */
     int devices[M3R_MAX_DEVICES];
     int max_pairs;      /* image pairs per device per launch (activation buffers) */
+    int dtype;          /* M3R_DTYPE_F16 or M3R_DTYPE_BF16 */
 } m3r_config;
 
 /* Slots of the timing_ms array written by m3r_infer / m3r_match. */
@@ -130,21 +137,22 @@ void m3r_host_free(void* p);
 /* ---- test / measurement entry points (no reference counterpart; they expose
  * single kernels of this backend for parity tests and kernel timing). ---- */
 
-/* Isolated attention (bf16 bits as uint16): O[s, t, h*64] = softmax(Q K^T * scale) V,
- * Q [s, h, nq, 64], K/V [s, h, nk, 64].  *kernel_ms gets the mean device time over
- * `iters` launches (>= 1) when not NULL. */
-int m3r_attention_fwd(int device, const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out,
+/* 16-bit operands below are bit patterns of the type `dtype` (M3R_DTYPE_*). */
+
+/* Isolated attention: O[s, t, h*64] = softmax(Q K^T * scale) V, Q [s, h, nq, 64],
+ * K/V [s, h, nk, 64].  *kernel_ms gets the mean device time over `iters` launches
+ * (>= 1) when not NULL. */
+int m3r_attention_fwd(int device, int dtype, const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out,
                       int n_seq, int heads, int nq, int nk, float scale, int iters, float* kernel_ms);
 
-/* GEMM C[M, N] = A[M, K] * W[N, K]^T + bias (bf16 bits in, fp32 out). */
-int m3r_gemm_test(int device, const uint16_t* a, const uint16_t* w, const float* bias, float* c, int M, int N,
-                  int K, int bn, int iters, float* kernel_ms);
+/* GEMM C[M, N] = A[M, K] * W[N, K]^T + bias (16-bit in, fp32 out). */
+int m3r_gemm_test(int device, int dtype, const uint16_t* a, const uint16_t* w, const float* bias, float* c, int M,
+                  int N, int K, int bn, int iters, float* kernel_ms);
 
-/* 3x3 conv, stride 1, pad 1, NHWC: x [n, h, w, c] bf16 bits, w [cout, 9 * cpad]
- * (tap-major, channel padded to cpad = ceil(c / 64) * 64) -> y [n, h, w, cout] fp32
- * (bias added). */
-int m3r_conv3_test(int device, const uint16_t* x, const uint16_t* w, const float* bias, float* y, int n, int h,
-                   int wd, int c, int cout, int bn);
+/* 3x3 conv, stride 1, pad 1, NHWC: x [n, h, w, c], w [cout, 9 * cpad] (tap-major,
+ * channel padded to cpad = ceil(c / 64) * 64) -> y [n, h, w, cout] fp32 (bias added). */
+int m3r_conv3_test(int device, int dtype, const uint16_t* x, const uint16_t* w, const float* bias, float* y, int n,
+                   int h, int wd, int c, int cout, int bn);
 
 /* Matcher arg-max only: nn_12 [n1] and nn_21 [n2] (lowest index on ties) of the
  * normalised descriptors, and the row maxima best_12 [n1]. */

@@ -22,8 +22,9 @@ Errors follow the reference bindings: bad shapes raise ValueError / RuntimeError
 (pybind11 maps std::runtime_error to RuntimeError, csrc/cpu/bindings.cpp:18-20).
 There is no CPU fallback: without the built library or a GPU every compute call raises.
 
-Precision: the reference's Precision.FP32 / FP16 (core/config.py:42-48) both run the
-bf16 tensor-core path (fp32 accumulation, fp32 residual stream and outputs).
+Precision: the reference's Precision.FP16 (its default) and FP32 (core/config.py:42-48)
+run fp16 tensor-core operands, "bf16" runs bf16 operands; both accumulate in fp32 and
+keep the residual stream and every output in fp32.
 """
 
 from __future__ import annotations
@@ -72,7 +73,8 @@ def get_compute_capability(device: int = 0) -> tuple[int, int]:
     return (ma.value, mi.value)
 
 
-def make_config(dims: ModelDims, image_hw: tuple[int, int], devices=(0,), max_pairs: int = 1) -> _lib.M3RConfig:
+def make_config(dims: ModelDims, image_hw: tuple[int, int], devices=(0,), max_pairs: int = 1,
+                dtype: int = _lib.DTYPE_F16) -> _lib.M3RConfig:
     c = _lib.M3RConfig()
     c.patch = dims.patch
     c.enc_dim, c.enc_depth, c.enc_heads, c.enc_mlp = dims.enc_dim, dims.enc_depth, dims.enc_heads, dims.enc_mlp
@@ -86,6 +88,7 @@ def make_config(dims: ModelDims, image_hw: tuple[int, int], devices=(0,), max_pa
     for i, d in enumerate(devices):
         c.devices[i] = int(d)
     c.max_pairs = int(max_pairs)
+    c.dtype = int(dtype)
     return c
 
 
@@ -99,13 +102,15 @@ def _env_devices() -> list[int]:
 class NativeEngine:
     """One libm3r_cuda engine: fixed model dims, image size, device list and launch size."""
 
-    def __init__(self, dims: ModelDims, image_hw, devices=(0,), max_pairs: int = 1):
+    def __init__(self, dims: ModelDims, image_hw, devices=(0,), max_pairs: int = 1, dtype: int = _lib.DTYPE_F16):
         self.lib = _lib.load()
         self.dims = dims
         self.image_hw = (int(image_hw[0]), int(image_hw[1]))
         self.devices = list(devices)
         self.max_pairs = int(max_pairs)
-        cfg = make_config(dims, self.image_hw, self.devices, self.max_pairs)
+        self.dtype = int(dtype)
+        self.dtype_name = _lib.DTYPE_NAMES[self.dtype]
+        cfg = make_config(dims, self.image_hw, self.devices, self.max_pairs, self.dtype)
         h = ctypes.c_void_p()
         _lib.check(self.lib.m3r_create(ctypes.byref(cfg), ctypes.byref(h)))
         self.h = h
@@ -238,7 +243,8 @@ class CUDAEngine:
             raise RuntimeError(f"Unknown model variant: {variant}")
         self.variant = variant
         self.dims = VARIANTS[variant]
-        self.precision = str(precision)
+        self.precision = str(getattr(precision, "value", precision))
+        self.dtype = _lib.dtype_for_precision(self.precision)
         self.num_threads = int(num_threads)
         self.image_hw = tuple(image_size) if image_size is not None else (int(resolution), int(resolution))
         self.devices = list(devices) if devices is not None else _env_devices()
@@ -297,7 +303,7 @@ class CUDAEngine:
         if self._matcher is None:
             # matching needs no weights: a minimal engine provides the device context
             self._matcher = next(iter(self._engines.values()), None) or NativeEngine(
-                self.dims, (self.dims.patch * 2, self.dims.patch * 2), self.devices[:1], 1)
+                self.dims, (self.dims.patch * 2, self.dims.patch * 2), self.devices[:1], 1, self.dtype)
         t0 = time.perf_counter()
         r = self._matcher.match(desc_1, desc_2, top_k=top_k, reciprocal=reciprocal,
                                 confidence_threshold=confidence_threshold)
@@ -314,7 +320,7 @@ class CUDAEngine:
             # drop engines of the same size but another launch size, to bound memory
             for k in [k for k in self._engines if k[0] == tuple(hw)]:
                 self._engines.pop(k).close()
-            eng = NativeEngine(self.dims, hw, self.devices, max_pairs)
+            eng = NativeEngine(self.dims, hw, self.devices, max_pairs, self.dtype)
             eng.load(self._path)
             self._engines[key] = eng
         return eng

@@ -37,8 +37,24 @@ class M3RConfig(ctypes.Structure):
         ("dec_mlp", ctypes.c_int), ("lf_hidden", ctypes.c_int), ("desc_dim", ctypes.c_int),
         ("img_h", ctypes.c_int), ("img_w", ctypes.c_int),
         ("n_devices", ctypes.c_int), ("devices", ctypes.c_int * M3R_MAX_DEVICES),
-        ("max_pairs", ctypes.c_int),
+        ("max_pairs", ctypes.c_int), ("dtype", ctypes.c_int),
     ]
+
+
+DTYPE_BF16 = 0
+DTYPE_F16 = 1
+DTYPE_NAMES = {DTYPE_BF16: "bf16", DTYPE_F16: "fp16"}
+
+
+def dtype_for_precision(precision: str) -> int:
+    """Map the reference's precision names (core/config.py:42-48) to the operand type:
+    "fp16" (its default) and "fp32" run fp16 tensor cores, "bf16" runs bf16."""
+    p = str(getattr(precision, "value", precision)).lower()
+    if p == "bf16":
+        return DTYPE_BF16
+    if p in ("fp16", "fp32", "f16", "f32", "float16", "float32"):
+        return DTYPE_F16
+    raise ValueError(f"unsupported precision {precision!r} (fp32, fp16 or bf16)")
 
 
 # exported symbol -> (restype, argtypes)
@@ -65,9 +81,9 @@ SIGNATURES = {
     "m3r_get_profile": (_I, [_P, _P]),
     "m3r_host_alloc": (_P, [ctypes.c_size_t]),
     "m3r_host_free": (None, [_P]),
-    "m3r_attention_fwd": (_I, [_I, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I, ctypes.POINTER(_F)]),
-    "m3r_gemm_test": (_I, [_I, _P, _P, _P, _P, _I, _I, _I, _I, _I, ctypes.POINTER(_F)]),
-    "m3r_conv3_test": (_I, [_I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I]),
+    "m3r_attention_fwd": (_I, [_I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I, ctypes.POINTER(_F)]),
+    "m3r_gemm_test": (_I, [_I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, ctypes.POINTER(_F)]),
+    "m3r_conv3_test": (_I, [_I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I]),
     "m3r_match_nn": (_I, [_I, _P, _P, _I64, _I64, _I, _P, _P, _P, ctypes.POINTER(_F)]),
 }
 

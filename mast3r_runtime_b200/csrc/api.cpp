@@ -219,8 +219,8 @@ void m3r_host_free(void* p) {
     if (p) cudaFreeHost(p);
 }
 
-int m3r_attention_fwd(int device, const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int n_seq,
-                      int heads, int nq, int nk, float scale, int iters, float* kernel_ms) {
+int m3r_attention_fwd(int device, int dtype, const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out,
+                      int n_seq, int heads, int nq, int nk, float scale, int iters, float* kernel_ms) {
     return guarded(nullptr, [&] {
         M3R_REQUIRE(q && k && v && out && n_seq > 0 && heads > 0 && nq > 0 && nk > 0, "attention: bad arguments");
         m3r::DeviceGuard g(device);
@@ -232,12 +232,10 @@ int m3r_attention_fwd(int device, const uint16_t* q, const uint16_t* k, const ui
         M3R_CUDA(cudaMemset(derr.p, 0, sizeof(int)));
         const int it = iters < 1 ? 1 : iters;
         Events ev;
-        m3r::attention_fwd(nullptr, dq.as<__nv_bfloat16>(), dk.as<__nv_bfloat16>(), dv.as<__nv_bfloat16>(),
-                           dout.as<__nv_bfloat16>(), n_seq, heads, nq, nk, scale, derr.as<int>());
+        m3r::attention_fwd(nullptr, dtype, dq.p, dk.p, dv.p, dout.p, n_seq, heads, nq, nk, scale, derr.as<int>());
         M3R_CUDA(cudaEventRecord(ev.a, nullptr));
         for (int i = 0; i < it; ++i)
-            m3r::attention_fwd(nullptr, dq.as<__nv_bfloat16>(), dk.as<__nv_bfloat16>(), dv.as<__nv_bfloat16>(),
-                               dout.as<__nv_bfloat16>(), n_seq, heads, nq, nk, scale, derr.as<int>());
+            m3r::attention_fwd(nullptr, dtype, dq.p, dk.p, dv.p, dout.p, n_seq, heads, nq, nk, scale, derr.as<int>());
         M3R_CUDA(cudaEventRecord(ev.b, nullptr));
         M3R_CUDA(cudaDeviceSynchronize());
         check_dev_err(derr.as<int>());
@@ -246,8 +244,8 @@ int m3r_attention_fwd(int device, const uint16_t* q, const uint16_t* k, const ui
     });
 }
 
-int m3r_gemm_test(int device, const uint16_t* a, const uint16_t* w, const float* bias, float* c, int M, int N, int K,
-                  int bn, int iters, float* kernel_ms) {
+int m3r_gemm_test(int device, int dtype, const uint16_t* a, const uint16_t* w, const float* bias, float* c, int M,
+                  int N, int K, int bn, int iters, float* kernel_ms) {
     return guarded(nullptr, [&] {
         M3R_REQUIRE(a && w && c && M > 0 && N > 0 && K > 0 && K % 8 == 0 && N % 4 == 0, "gemm_test: bad arguments");
         m3r::DeviceGuard g(device);
@@ -264,10 +262,9 @@ int m3r_gemm_test(int device, const uint16_t* a, const uint16_t* w, const float*
         p.err = derr.as<int>();
         const int it = iters < 1 ? 1 : iters;
         Events ev;
-        m3r::gemm_rows(nullptr, bn, m3r::EPI_F32, da.as<__nv_bfloat16>(), K, M, K, dw.as<__nv_bfloat16>(), K, N, p);
+        m3r::gemm_rows(nullptr, dtype, bn, m3r::EPI_F32, da.p, K, M, K, dw.p, K, N, p);
         M3R_CUDA(cudaEventRecord(ev.a, nullptr));
-        for (int i = 0; i < it; ++i)
-            m3r::gemm_rows(nullptr, bn, m3r::EPI_F32, da.as<__nv_bfloat16>(), K, M, K, dw.as<__nv_bfloat16>(), K, N, p);
+        for (int i = 0; i < it; ++i) m3r::gemm_rows(nullptr, dtype, bn, m3r::EPI_F32, da.p, K, M, K, dw.p, K, N, p);
         M3R_CUDA(cudaEventRecord(ev.b, nullptr));
         M3R_CUDA(cudaDeviceSynchronize());
         check_dev_err(derr.as<int>());
@@ -276,8 +273,8 @@ int m3r_gemm_test(int device, const uint16_t* a, const uint16_t* w, const float*
     });
 }
 
-int m3r_conv3_test(int device, const uint16_t* x, const uint16_t* w, const float* bias, float* y, int n, int h, int wd,
-                   int c, int cout, int bn) {
+int m3r_conv3_test(int device, int dtype, const uint16_t* x, const uint16_t* w, const float* bias, float* y, int n,
+                   int h, int wd, int c, int cout, int bn) {
     return guarded(nullptr, [&] {
         M3R_REQUIRE(x && w && y && n > 0 && h > 0 && wd > 0 && c > 0 && c % 8 == 0 && cout > 0 && cout % 4 == 0,
                     "conv3_test: bad arguments");
@@ -295,8 +292,7 @@ int m3r_conv3_test(int device, const uint16_t* x, const uint16_t* w, const float
         p.out = dy.p;
         p.ldo = cout;
         p.err = derr.as<int>();
-        m3r::gemm_conv3(nullptr, bn, m3r::EPI_F32, dx.as<__nv_bfloat16>(), n, h, wd, c, c, dw.as<__nv_bfloat16>(),
-                        cout, p);
+        m3r::gemm_conv3(nullptr, dtype, bn, m3r::EPI_F32, dx.p, n, h, wd, c, c, dw.p, cout, p);
         M3R_CUDA(cudaDeviceSynchronize());
         check_dev_err(derr.as<int>());
         M3R_CUDA(cudaMemcpy(y, dy.p, yn * 4, cudaMemcpyDeviceToHost));

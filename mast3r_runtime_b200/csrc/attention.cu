@@ -1,16 +1,16 @@
-// Non-causal flash attention on tcgen05 (sm_100a), head dim 64, bf16 in/out,
-// fp32 softmax statistics and accumulation.
+// Non-causal flash attention on tcgen05 (sm_100a), head dim 64, 16-bit (fp16 or
+// bf16) in/out, fp32 softmax statistics and accumulation.
 //
-//   Q, K, V : head-major [seq, head, tok, 64] bf16 (written by the QKV GEMM epilogue)
-//   O       : token-major [seq, tok, head * 64] bf16 (the A operand of the output projection)
+//   Q, K, V : head-major [seq, head, tok, 64] (written by the QKV GEMM epilogue)
+//   O       : token-major [seq, tok, head * 64] (the A operand of the output projection)
 //
 // One CTA = 128 query rows of one (seq, head).  192 threads: warps 0-3 softmax
 // (thread = query row = TMEM lane), warp 4 TMA producer, warp 5 MMA issuer.
-// TMEM (256 columns, so two CTAs fit on an SM): S = Q K^T in [0,128), P (bf16,
-// two per column) in [128,192), O in [192,256).  S uses an SS MMA; O += P V uses
-// a TS MMA with P from TMEM and V read MN-major straight from its TMA tile.
-// K/V tiles of 128 keys are double-buffered; keys beyond Nk are masked to -inf
-// (their V rows are zero-filled by TMA).  Scores never touch HBM.
+// TMEM (256 columns, so two CTAs fit on an SM): S = Q K^T in [0,128), P (two
+// 16-bit values per column) in [128,192), O in [192,256).  S uses an SS MMA;
+// O += P V uses a TS MMA with P from TMEM and V read MN-major straight from its
+// TMA tile.  K/V tiles of 128 keys are double-buffered; keys beyond Nk are masked
+// to -inf (their V rows are zero-filled by TMA).  Scores never touch HBM.
 //
 // Semantics: softmax(Q K^T * scale) V per head, as
 // backends/python/croco_encoder.py:80-85 and croco_decoder.py:76-82, 171-177.
@@ -32,10 +32,11 @@ constexpr uint32_t kColS = 0, kColP = 128, kColO = 192, kTmemCols = 256;
 struct AttnParams {
     int nq, nk, heads, n_kv_tiles;
     float scale_log2;  // scale * log2(e)
-    __nv_bfloat16* out;
+    void* out;
     int* err;          // device status word (bounded-wait timeouts)
 };
 
+template <class T>
 __global__ void __launch_bounds__(192, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
                     const __grid_constant__ CUtensorMap mapV, const __grid_constant__ AttnParams p) {
@@ -112,8 +113,8 @@ __global__ void __launch_bounds__(192, 1)
     } else if (warp == 5) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc_s = idesc_bf16(128, 128, false, false);
-            constexpr uint32_t idesc_o = idesc_bf16(128, 64, false, true);
+            constexpr uint32_t idesc_s = idesc_f16kind<T>(128, 128, false, false);
+            constexpr uint32_t idesc_o = idesc_f16kind<T>(128, 64, false, true);
             const uint32_t q_addr = smem_u32(sQ);
             bool ok = mbar_wait(q_full, 0, abort_flag, kDevTimeoutMma, p.err);
             for (int j = 0; j < nkv && ok; ++j) {
@@ -125,16 +126,16 @@ __global__ void __launch_bounds__(192, 1)
                 const uint32_t k_addr = smem_u32(sK + st * kTileBytes);
 #pragma unroll
                 for (int k = 0; k < 4; ++k)
-                    mma_bf16_ss(tmem + kColS, umma_desc_sw128(q_addr + k * 32, 16, 1024),
-                                umma_desc_sw128(k_addr + k * 32, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
+                    mma_f16_ss(tmem + kColS, umma_desc_sw128(q_addr + k * 32, 16, 1024),
+                               umma_desc_sw128(k_addr + k * 32, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
                 mma_commit(s_full);
                 if (!mbar_wait(p_full, j & 1, abort_flag, kDevTimeoutMma, p.err)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t v_addr = smem_u32(sV + st * kTileBytes);
 #pragma unroll
                 for (int k = 0; k < 8; ++k)
-                    mma_bf16_ts(tmem + kColO, tmem + kColP + k * 8, umma_desc_sw128(v_addr + k * 2048, 16384, 1024),
-                                idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+                    mma_f16_ts(tmem + kColO, tmem + kColP + k * 8, umma_desc_sw128(v_addr + k * 2048, 16384, 1024),
+                               idesc_o, (j > 0 || k > 0) ? 1u : 0u);
                 mma_commit(&kv_empty[st]);
                 mma_commit(o_done);
             }
@@ -185,7 +186,7 @@ __global__ void __launch_bounds__(192, 1)
                     const float p0 = c0 < valid ? ex2_approx(__uint_as_float(v[2 * i]) * p.scale_log2 - m_new) : 0.0f;
                     const float p1 = c0 + 1 < valid ? ex2_approx(__uint_as_float(v[2 * i + 1]) * p.scale_log2 - m_new) : 0.0f;
                     rowsum += p0 + p1;
-                    pk[i] = pack_bf16x2(p0, p1);
+                    pk[i] = Elem<T>::pack(p0, p1);
                 }
                 asm volatile(
                     "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
@@ -222,17 +223,17 @@ __global__ void __launch_bounds__(192, 1)
             const int q = q0 + r;
             if (q < p.nq) {
                 const float inv = 1.0f / l_run;
-                __nv_bfloat16* dst = p.out + (static_cast<long long>(seq) * p.nq + q) * (p.heads * 64) + head * 64;
+                T* dst = reinterpret_cast<T*>(p.out) + (static_cast<long long>(seq) * p.nq + q) * (p.heads * 64) + head * 64;
                 uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
                 for (int h = 0; h < 2; ++h)
 #pragma unroll
                     for (int qq = 0; qq < 4; ++qq) {
                         uint4 u;
-                        u.x = pack_bf16x2(__uint_as_float(o[h][qq * 8 + 0]) * inv, __uint_as_float(o[h][qq * 8 + 1]) * inv);
-                        u.y = pack_bf16x2(__uint_as_float(o[h][qq * 8 + 2]) * inv, __uint_as_float(o[h][qq * 8 + 3]) * inv);
-                        u.z = pack_bf16x2(__uint_as_float(o[h][qq * 8 + 4]) * inv, __uint_as_float(o[h][qq * 8 + 5]) * inv);
-                        u.w = pack_bf16x2(__uint_as_float(o[h][qq * 8 + 6]) * inv, __uint_as_float(o[h][qq * 8 + 7]) * inv);
+                        u.x = Elem<T>::pack(__uint_as_float(o[h][qq * 8 + 0]) * inv, __uint_as_float(o[h][qq * 8 + 1]) * inv);
+                        u.y = Elem<T>::pack(__uint_as_float(o[h][qq * 8 + 2]) * inv, __uint_as_float(o[h][qq * 8 + 3]) * inv);
+                        u.z = Elem<T>::pack(__uint_as_float(o[h][qq * 8 + 4]) * inv, __uint_as_float(o[h][qq * 8 + 5]) * inv);
+                        u.w = Elem<T>::pack(__uint_as_float(o[h][qq * 8 + 6]) * inv, __uint_as_float(o[h][qq * 8 + 7]) * inv);
                         d4[h * 4 + qq] = u;
                     }
             }
@@ -245,11 +246,9 @@ __global__ void __launch_bounds__(192, 1)
     }
 }
 
-}  // namespace
-
-void attention_fwd(cudaStream_t s, const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v,
-                   __nv_bfloat16* out, int n_seq, int heads, int nq, int nk, float scale, int* err) {
-    M3R_REQUIRE(n_seq > 0 && heads > 0 && nq > 0 && nk > 0, "attention: bad shape");
+template <class T>
+void launch(cudaStream_t s, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnParams& p,
+            dim3 grid) {
     static std::once_flag once;
     std::call_once(once, [] {
         int ndev = 0, cur = 0;
@@ -257,13 +256,23 @@ void attention_fwd(cudaStream_t s, const __nv_bfloat16* q, const __nv_bfloat16* 
         M3R_CUDA(cudaGetDevice(&cur));
         for (int d = 0; d < ndev; ++d) {
             M3R_CUDA(cudaSetDevice(d));
-            M3R_CUDA(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+            M3R_CUDA(cudaFuncSetAttribute(attn_fwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
         }
         M3R_CUDA(cudaSetDevice(cur));
     });
-    const CUtensorMap mq = tmap_bf16_3d_rows64(q, nq, static_cast<uint64_t>(n_seq) * heads, kTile);
-    const CUtensorMap mk = tmap_bf16_3d_rows64(k, nk, static_cast<uint64_t>(n_seq) * heads, kTile);
-    const CUtensorMap mv = tmap_bf16_3d_rows64(v, nk, static_cast<uint64_t>(n_seq) * heads, kTile);
+    attn_fwd_kernel<T><<<grid, 192, kSmemBytes, s>>>(mq, mk, mv, p);
+    M3R_CUDA(cudaGetLastError());
+}
+
+}  // namespace
+
+void attention_fwd(cudaStream_t s, int dt, const void* q, const void* k, const void* v, void* out, int n_seq,
+                   int heads, int nq, int nk, float scale, int* err) {
+    M3R_REQUIRE(n_seq > 0 && heads > 0 && nq > 0 && nk > 0, "attention: bad shape");
+    M3R_REQUIRE(n_seq <= 65535 && heads <= 65535, "attention: grid too large");
+    const CUtensorMap mq = tmap_3d_rows64(dt, q, nq, static_cast<uint64_t>(n_seq) * heads, kTile);
+    const CUtensorMap mk = tmap_3d_rows64(dt, k, nk, static_cast<uint64_t>(n_seq) * heads, kTile);
+    const CUtensorMap mv = tmap_3d_rows64(dt, v, nk, static_cast<uint64_t>(n_seq) * heads, kTile);
     AttnParams p;
     p.nq = nq;
     p.nk = nk;
@@ -272,10 +281,13 @@ void attention_fwd(cudaStream_t s, const __nv_bfloat16* q, const __nv_bfloat16* 
     p.scale_log2 = scale * 1.4426950408889634f;
     p.out = out;
     p.err = err;
-    dim3 grid((nq + kTile - 1) / kTile, heads, n_seq);
-    M3R_REQUIRE(n_seq <= 65535 && heads <= 65535, "attention: grid too large");
-    attn_fwd_kernel<<<grid, 192, kSmemBytes, s>>>(mq, mk, mv, p);
-    M3R_CUDA(cudaGetLastError());
+    const dim3 grid((nq + kTile - 1) / kTile, heads, n_seq);
+    if (dt == DT_F16)
+        launch<__half>(s, mq, mk, mv, p, grid);
+    else if (dt == DT_BF16)
+        launch<__nv_bfloat16>(s, mq, mk, mv, p, grid);
+    else
+        throw Error(kErrArg, "attention: unknown operand type");
 }
 
 }  // namespace m3r

@@ -5,6 +5,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -151,16 +152,47 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo
     return d;
 }
 
-// Instruction descriptor, kind::f16 with BF16 A/B, F32 accumulate.
-//   c_format [4,6) = 1 (F32), a_format [7,10) = 1 (BF16), b_format [10,13) = 1,
+// 16-bit operand types of kind::f16 MMAs.  Operands live in memory as 16-bit
+// patterns; Elem<T> converts to / from fp32 and gives the MMA format code.
+enum Dt : int { DT_BF16 = 0, DT_F16 = 1 };
+
+template <class T>
+struct Elem;
+template <>
+struct Elem<__nv_bfloat16> {
+    static constexpr uint32_t kFmt = 1;  // a_format / b_format BF16
+    __device__ static __forceinline__ uint32_t pack(float lo, float hi) {
+        __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+        return *reinterpret_cast<uint32_t*>(&v);
+    }
+    __device__ static __forceinline__ float2 unpack(uint32_t u) {
+        return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u));
+    }
+    __device__ static __forceinline__ __nv_bfloat16 from(float f) { return __float2bfloat16_rn(f); }
+};
+template <>
+struct Elem<__half> {
+    static constexpr uint32_t kFmt = 0;  // a_format / b_format F16
+    __device__ static __forceinline__ uint32_t pack(float lo, float hi) {
+        __half2 v = __floats2half2_rn(lo, hi);
+        return *reinterpret_cast<uint32_t*>(&v);
+    }
+    __device__ static __forceinline__ float2 unpack(uint32_t u) { return __half22float2(*reinterpret_cast<__half2*>(&u)); }
+    __device__ static __forceinline__ __half from(float f) { return __float2half_rn(f); }
+};
+
+// Instruction descriptor, kind::f16 (A/B both F16 or both BF16), F32 accumulate.
+//   c_format [4,6) = 1 (F32), a_format [7,10), b_format [10,13) (0 F16, 1 BF16),
 //   a_major bit 15, b_major bit 16 (1 = MN-major), N >> 3 in [17,23), M >> 4 in [24,29).
-__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n, bool a_mn_major, bool b_mn_major) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | (a_mn_major ? (1u << 15) : 0u) | (b_mn_major ? (1u << 16) : 0u) |
-           (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+template <class T>
+__host__ __device__ constexpr uint32_t idesc_f16kind(int m, int n, bool a_mn_major, bool b_mn_major) {
+    return (1u << 4) | (Elem<T>::kFmt << 7) | (Elem<T>::kFmt << 10) | (a_mn_major ? (1u << 15) : 0u) |
+           (b_mn_major ? (1u << 16) : 0u) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(m >> 4) << 24);
 }
 
 // D[tmem] (+)= A[smem] * B[smem]^T
-__device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+__device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                             uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -170,7 +202,7 @@ __device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, ui
 }
 
 // D[tmem] (+)= A[tmem] * B[smem]
-__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                             uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -225,10 +257,6 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------- numerics
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&v);
-}
 
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;

@@ -4,7 +4,8 @@
 // pairs 0..n-1) are rows of one [2n * N, D] activation matrix, so the shared-
 // weight encoder runs as single GEMMs over every token.  The decoder runs per
 // view (different weights, dec_blocks / dec_blocks2), each view's rows being a
-// contiguous half.  Residual streams stay fp32; GEMM operands are bf16.
+// contiguous half.  Residual streams stay fp32; GEMM operands are 16-bit (fp16 or
+// bf16, Dims::dt) with fp32 accumulation.
 //
 // Reference semantics: encoder croco_encoder.py:245-283, decoder
 // croco_decoder.py:395-434, heads mpsgraph_engine.mm:383-437 (see oracle/model.py
@@ -19,6 +20,7 @@
 #include <thread>
 
 #include "attention.h"
+#include "common.cuh"
 #include "gemm.h"
 #include "kernels.h"
 #include "safetensors.h"
@@ -49,6 +51,8 @@ Dims Dims::from(const m3r_config& c) {
     d.kpad = (3 * d.patch * d.patch + 63) / 64 * 64;
     d.hook1 = d.dec_depth / 2 - 1;
     d.hook2 = d.dec_depth * 3 / 4 - 1;
+    d.dt = c.dtype;
+    M3R_REQUIRE(d.dt == DT_F16 || d.dt == DT_BF16, "dtype must be M3R_DTYPE_F16 or M3R_DTYPE_BF16");
     d.dpt_h = 16 * d.hg;
     d.dpt_w = 16 * d.wg;
     M3R_REQUIRE(d.enc_heads > 0 && d.enc_dim == 64 * d.enc_heads, "encoder head dim must be 64");
@@ -72,43 +76,48 @@ DeviceGuard::~DeviceGuard() { cudaSetDevice(prev); }
 // ---------------------------------------------------------------------------- host weight prep
 namespace {
 
-uint16_t f2bf(float f) {
-    uint32_t u;
-    std::memcpy(&u, &f, 4);
-    if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x7FFFFFu)) return 0x7FC0;
-    u += 0x7FFFu + ((u >> 16) & 1u);
-    return static_cast<uint16_t>(u >> 16);
+// float -> 16-bit operand bits, round to nearest even (CUDA's host-side conversions)
+uint16_t to16bits(float f, int dt) {
+    uint16_t r;
+    if (dt == DT_F16) {
+        const __half h = __float2half_rn(f);
+        std::memcpy(&r, &h, 2);
+    } else {
+        const __nv_bfloat16 h = __float2bfloat16_rn(f);
+        std::memcpy(&r, &h, 2);
+    }
+    return r;
 }
 
 struct HostLin {
-    std::vector<uint16_t> w;  // bf16 bits [out, in]
+    std::vector<uint16_t> w;  // 16-bit operand bits [out, in]
     std::vector<float> b;     // may be empty
     int out = 0, in = 0;
 };
 
-HostLin to_bf16(const std::vector<float>& w, int out, int in, std::vector<float> b = {}) {
+HostLin to16(int dt, const std::vector<float>& w, int out, int in, std::vector<float> b = {}) {
     HostLin h;
     h.out = out;
     h.in = in;
     h.w.resize(static_cast<size_t>(out) * in);
-    for (size_t i = 0; i < h.w.size(); ++i) h.w[i] = f2bf(w[i]);
+    for (size_t i = 0; i < h.w.size(); ++i) h.w[i] = to16bits(w[i], dt);
     h.b = std::move(b);
     return h;
 }
 
 // conv weight [co, ci, 3, 3] -> [co, 9, cpad] tap-major, zero channel padding
-HostLin conv3_weights(const std::vector<float>& w, int co, int ci, std::vector<float> b = {}) {
+HostLin conv3_weights(int dt, const std::vector<float>& w, int co, int ci, std::vector<float> b = {}) {
     const int cpad = (ci + 63) / 64 * 64;
     std::vector<float> t(static_cast<size_t>(co) * 9 * cpad, 0.0f);
     for (int o = 0; o < co; ++o)
         for (int c = 0; c < ci; ++c)
             for (int tap = 0; tap < 9; ++tap)
                 t[(static_cast<size_t>(o) * 9 + tap) * cpad + c] = w[(static_cast<size_t>(o) * ci + c) * 9 + tap];
-    return to_bf16(t, co, 9 * cpad, std::move(b));
+    return to16(dt, t, co, 9 * cpad, std::move(b));
 }
 
 // ConvTranspose2d weight [ci, co, s, s] -> B [(dy*s+dx)*co + o, ci]
-HostLin convt_weights(const std::vector<float>& w, int ci, int co, int s, std::vector<float> b) {
+HostLin convt_weights(int dt, const std::vector<float>& w, int ci, int co, int s, std::vector<float> b) {
     std::vector<float> t(static_cast<size_t>(s) * s * co * ci);
     for (int c = 0; c < ci; ++c)
         for (int o = 0; o < co; ++o)
@@ -116,7 +125,7 @@ HostLin convt_weights(const std::vector<float>& w, int ci, int co, int s, std::v
                 for (int dx = 0; dx < s; ++dx)
                     t[(static_cast<size_t>((dy * s + dx) * co + o)) * ci + c] =
                         w[((static_cast<size_t>(c) * co + o) * s + dy) * s + dx];
-    return to_bf16(t, s * s * co, ci, std::move(b));
+    return to16(dt, t, s * s * co, ci, std::move(b));
 }
 
 }  // namespace
@@ -161,7 +170,7 @@ public:
         Lin l;
         l.out = h.out;
         l.in = h.in;
-        l.w = reinterpret_cast<__nv_bfloat16*>(upload(h.w));
+        l.w = upload(h.w);
         l.b = upload(h.b);
         return l;
     }
@@ -180,11 +189,11 @@ public:
 
     // ------------------------------------------------------------ activations
     uint8_t* img = nullptr;
-    __nv_bfloat16 *patches = nullptr, *xn = nullptr, *yn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr,
+    uint16_t *patches = nullptr, *xn = nullptr, *yn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr,
                   *ao = nullptr, *h = nullptr, *enc_out = nullptr, *hook1 = nullptr, *hook2 = nullptr,
                   *dec_out = nullptr;
     float *xenc = nullptr, *xdec = nullptr, *encp = nullptr;
-    __nv_bfloat16 *f0a = nullptr, *f0 = nullptr, *rn0 = nullptr, *f1a = nullptr, *f1 = nullptr, *rn1 = nullptr,
+    uint16_t *f0a = nullptr, *f0 = nullptr, *rn0 = nullptr, *f1a = nullptr, *f1 = nullptr, *rn1 = nullptr,
                   *f2 = nullptr, *rn2 = nullptr, *f3a = nullptr, *col3 = nullptr, *f3 = nullptr, *rn3 = nullptr,
                   *fused = nullptr, *up1 = nullptr, *hd0 = nullptr, *up2 = nullptr, *lf1 = nullptr;
     float* out4 = nullptr;
@@ -199,7 +208,7 @@ public:
         const long long Dm = std::max(d_.enc_dim, d_.dec_dim);
         const long long Hm = std::max(d_.enc_mlp, d_.dec_mlp);
         const long long hg = d_.hg, wg = d_.wg;
-        auto bf = [&](long long n) { return static_cast<__nv_bfloat16*>(alloc(n * 2)); };
+        auto bf = [&](long long n) { return static_cast<uint16_t*>(alloc(n * 2)); };
         auto f32 = [&](long long n) { return static_cast<float*>(alloc(n * 4)); };
         img = static_cast<uint8_t*>(alloc(2 * P * d_.H * d_.W * 3));
         patches = bf(T * d_.kpad);
@@ -292,7 +301,7 @@ public:
         return p;
     }
 
-    void linear(const __nv_bfloat16* A, long long M, const Lin& L, int epi, void* out, long long ldo, int act = ACT_NONE,
+    void linear(const uint16_t* A, long long M, const Lin& L, int epi, void* out, long long ldo, int act = ACT_NONE,
                 const float* resid = nullptr, int bn = 0) {
         GemmParams p = gp();
         p.bias = L.b;
@@ -302,12 +311,12 @@ public:
         p.resid = resid;
         p.ldr = ldo;
         const int b = bn ? bn : bn_for(L.out);
-        launch(kGemm, 2.0 * M * L.out * L.in, [&] { gemm_rows(stream_, b, epi, A, L.in, static_cast<int>(M), L.in, L.w, L.in, L.out, p); });
+        launch(kGemm, 2.0 * M * L.out * L.in, [&] { gemm_rows(stream_, d_.dt, b, epi, A, L.in, static_cast<int>(M), L.in, L.w, L.in, L.out, p); });
     }
 
     // head-major scatter of [M, nsec * D] into up to three [seqs, heads, ntok, 64] buffers
-    void linear_heads(const __nv_bfloat16* A, long long M, const Lin& L, int D, __nv_bfloat16* o0, int r0,
-                      __nv_bfloat16* o1, int r1, __nv_bfloat16* o2, int r2) {
+    void linear_heads(const uint16_t* A, long long M, const Lin& L, int D, uint16_t* o0, int r0,
+                      uint16_t* o1, int r1, uint16_t* o2, int r2) {
         GemmParams p = gp();
         p.bias = L.b;
         p.sec_len = D;
@@ -323,20 +332,20 @@ public:
         p.rope_sin = rope_sin;
         const int b = (D % 256 == 0) ? 256 : 128;
         launch(kGemm, 2.0 * M * L.out * L.in,
-               [&] { gemm_rows(stream_, b, EPI_HEADS, A, L.in, static_cast<int>(M), L.in, L.w, L.in, L.out, p); });
+               [&] { gemm_rows(stream_, d_.dt, b, EPI_HEADS, A, L.in, static_cast<int>(M), L.in, L.w, L.in, L.out, p); });
     }
 
-    void attn(const __nv_bfloat16* qq, const __nv_bfloat16* kk, const __nv_bfloat16* vv, __nv_bfloat16* out, int seqs,
+    void attn(const uint16_t* qq, const uint16_t* kk, const uint16_t* vv, uint16_t* out, int seqs,
               int heads) {
         const double fl = 4.0 * seqs * heads * static_cast<double>(d_.ntok) * d_.ntok * 64;
-        launch(kAttn, fl, [&] { attention_fwd(stream_, qq, kk, vv, out, seqs, heads, d_.ntok, d_.ntok, 0.125f, err_); });
+        launch(kAttn, fl, [&] { attention_fwd(stream_, d_.dt, qq, kk, vv, out, seqs, heads, d_.ntok, d_.ntok, 0.125f, err_); });
     }
 
-    void ln(const float* x, long long rows, int D, const Norm& n, __nv_bfloat16* y) {
-        launch(kOther, 0, [&] { layernorm(stream_, x, static_cast<int>(rows), D, n.g, n.b, y); });
+    void ln(const float* x, long long rows, int D, const Norm& n, uint16_t* y) {
+        launch(kOther, 0, [&] { layernorm(stream_, d_.dt, x, static_cast<int>(rows), D, n.g, n.b, y); });
     }
 
-    void conv3(const __nv_bfloat16* X, int n, int hh, int ww, int c, const Lin& L, int epi, void* out, int act,
+    void conv3(const uint16_t* X, int n, int hh, int ww, int c, const Lin& L, int epi, void* out, int act,
                int bn, const float* w4 = nullptr, const float* b4 = nullptr) {
         GemmParams p = gp();
         p.bias = L.b;
@@ -346,7 +355,7 @@ public:
         p.w4 = w4;
         p.b4 = b4;
         const double fl = 2.0 * n * hh * ww * static_cast<double>(L.out) * 9 * c;
-        launch(kGemm, fl, [&] { gemm_conv3(stream_, bn, epi, X, n, hh, ww, c, c, L.w, L.out, p); });
+        launch(kGemm, fl, [&] { gemm_conv3(stream_, d_.dt, bn, epi, X, n, hh, ww, c, c, L.w, L.out, p); });
     }
 
     // ------------------------------------------------------------ forward
@@ -360,14 +369,14 @@ public:
         M3R_CUDA(cudaEventRecord(stage_ev_[0], stream_));
 
         // patch embedding (+ ImageNet normalisation fused into the im2col)
-        launch(kOther, 0, [&] { patch_im2col(stream_, img, 2 * n, d.H, d.W, d.patch, d.kpad, patches); });
+        launch(kOther, 0, [&] { patch_im2col(stream_, d_.dt, img, 2 * n, d.H, d.W, d.patch, d.kpad, patches); });
         {
             GemmParams p = gp();
             p.bias = patch.b;
             p.out = xenc;
             p.ldo = d.enc_dim;
             launch(kGemm, 2.0 * T * d.enc_dim * 3 * d.patch * d.patch,
-                   [&] { gemm_rows(stream_, bn_for(d.enc_dim), EPI_F32, patches, d.kpad, static_cast<int>(T), d.kpad, patch.w, d.kpad, d.enc_dim, p); });
+                   [&] { gemm_rows(stream_, d_.dt, bn_for(d.enc_dim), EPI_F32, patches, d.kpad, static_cast<int>(T), d.kpad, patch.w, d.kpad, d.enc_dim, p); });
         }
         M3R_CUDA(cudaEventRecord(stage_ev_[1], stream_));
 
@@ -395,8 +404,8 @@ public:
                 const DecBlock& B = dec[view][i];
                 float* xv = xdec + view * Tv * Dd;
                 const float* yo = encp + (1 - view) * Tv * Dd;
-                __nv_bfloat16* xnv = xn + view * Tv * Dd;
-                __nv_bfloat16* aov = ao + view * Tv * Dd;
+                uint16_t* xnv = xn + view * Tv * Dd;
+                uint16_t* aov = ao + view * Tv * Dd;
                 // self attention
                 ln(xv, Tv, Dd, B.n1, xnv);
                 linear_heads(xnv, Tv, B.qkv, Dd, q, 1, k, 1, v, 0);
@@ -414,8 +423,8 @@ public:
                 linear(xnv, Tv, B.fc1, EPI_BF16, h, d.dec_mlp, ACT_GELU);
                 linear(h, Tv, B.fc2, EPI_F32_RESID, xv, Dd, ACT_NONE, xv);
             }
-            if (i == d.hook1) launch(kOther, 0, [&] { cast_bf16(stream_, xdec, T * Dd, hook1); });
-            if (i == d.hook2) launch(kOther, 0, [&] { cast_bf16(stream_, xdec, T * Dd, hook2); });
+            if (i == d.hook1) launch(kOther, 0, [&] { cast16(stream_, d_.dt, xdec, T * Dd, hook1); });
+            if (i == d.hook2) launch(kOther, 0, [&] { cast16(stream_, d_.dt, xdec, T * Dd, hook2); });
         }
         ln(xdec, T, Dd, dec_norm, dec_out);
         M3R_CUDA(cudaEventRecord(stage_ev_[3], stream_));
@@ -442,10 +451,10 @@ public:
         const Head& Hh = head[view];
         const long long N = d.ntok, Tv = static_cast<long long>(n) * N;
         const int hg = d.hg, wg = d.wg;
-        const __nv_bfloat16* h0 = enc_out + view * Tv * d.enc_dim;
-        const __nv_bfloat16* h1 = hook1 + view * Tv * d.dec_dim;
-        const __nv_bfloat16* h2 = hook2 + view * Tv * d.dec_dim;
-        const __nv_bfloat16* h3 = dec_out + view * Tv * d.dec_dim;
+        const uint16_t* h0 = enc_out + view * Tv * d.enc_dim;
+        const uint16_t* h1 = hook1 + view * Tv * d.dec_dim;
+        const uint16_t* h2 = hook2 + view * Tv * d.dec_dim;
+        const uint16_t* h3 = dec_out + view * Tv * d.dec_dim;
 
         // act_postprocess (mpsgraph_engine.mm:391-395)
         linear(h0, Tv, Hh.ap0_0, EPI_BF16, f0a, 96, ACT_NONE, nullptr, 128);
@@ -459,7 +468,7 @@ public:
             p.ct_h = hg;
             p.ct_w = wg;
             launch(kGemm, 2.0 * Tv * Hh.ap0_1t.out * Hh.ap0_1t.in,
-                   [&] { gemm_rows(stream_, 256, EPI_CONVT, f0a, 96, static_cast<int>(Tv), 96, Hh.ap0_1t.w, 96, Hh.ap0_1t.out, p); });
+                   [&] { gemm_rows(stream_, d_.dt, 256, EPI_CONVT, f0a, 96, static_cast<int>(Tv), 96, Hh.ap0_1t.w, 96, Hh.ap0_1t.out, p); });
         }
         linear(h1, Tv, Hh.ap1_0, EPI_BF16, f1a, 192, ACT_NONE, nullptr, 128);
         {
@@ -472,7 +481,7 @@ public:
             p.ct_h = hg;
             p.ct_w = wg;
             launch(kGemm, 2.0 * Tv * Hh.ap1_1t.out * Hh.ap1_1t.in,
-                   [&] { gemm_rows(stream_, 256, EPI_CONVT, f1a, 192, static_cast<int>(Tv), 192, Hh.ap1_1t.w, 192, Hh.ap1_1t.out, p); });
+                   [&] { gemm_rows(stream_, d_.dt, 256, EPI_CONVT, f1a, 192, static_cast<int>(Tv), 192, Hh.ap1_1t.w, 192, Hh.ap1_1t.out, p); });
         }
         linear(h2, Tv, Hh.ap2_0, EPI_BF16, f2, 384, ACT_NONE, nullptr, 128);
         linear(h3, Tv, Hh.ap3_0, EPI_BF16, f3a, 768, ACT_NONE, nullptr, 256);
@@ -487,10 +496,10 @@ public:
 
         // fusion and head (graph_builder.hpp:285-299, mpsgraph_engine.mm:402-422)
         const int H0 = 4 * hg, W0 = 4 * wg;
-        launch(kOther, 0, [&] { dpt_fuse(stream_, rn0, rn1, 2 * hg, 2 * wg, rn2, hg, wg, rn3, hg / 2, wg / 2, n, H0, W0, 256, fused); });
-        launch(kOther, 0, [&] { resize_bf16(stream_, fused, n, H0, W0, 256, 2 * H0, 2 * W0, up1); });
+        launch(kOther, 0, [&] { dpt_fuse(stream_, d_.dt, rn0, rn1, 2 * hg, 2 * wg, rn2, hg, wg, rn3, hg / 2, wg / 2, n, H0, W0, 256, fused); });
+        launch(kOther, 0, [&] { resize16(stream_, d_.dt, fused, n, H0, W0, 256, 2 * H0, 2 * W0, up1); });
         conv3(up1, n, 2 * H0, 2 * W0, 256, Hh.hd0, EPI_BF16, hd0, ACT_RELU, 128);
-        launch(kOther, 0, [&] { resize_bf16(stream_, hd0, n, 2 * H0, 2 * W0, 128, 4 * H0, 4 * W0, up2); });
+        launch(kOther, 0, [&] { resize16(stream_, d_.dt, hd0, n, 2 * H0, 2 * W0, 128, 4 * H0, 4 * W0, up2); });
         conv3(up2, n, 4 * H0, 4 * W0, 128, Hh.hd2, EPI_HEAD4, out4, ACT_RELU, 128, Hh.w4, Hh.b4);
         float* pts = o_pts + static_cast<long long>(view) * n * d.H * d.W * 3;
         float* conf = o_conf + static_cast<long long>(view) * n * d.H * d.W;
@@ -504,7 +513,7 @@ public:
             p.out = lf1;
             p.ldo = d.lf_hidden;
             launch(kGemm, 2.0 * Tv * Hh.lf1.out * Hh.lf1.in, [&] {
-                gemm_concat(stream_, 256, EPI_BF16, h0, d.enc_dim, d.enc_dim, h3, d.dec_dim, d.dec_dim, static_cast<int>(Tv),
+                gemm_concat(stream_, d_.dt, 256, EPI_BF16, h0, d.enc_dim, d.enc_dim, h3, d.dec_dim, d.dec_dim, static_cast<int>(Tv),
                             Hh.lf1.w, Hh.lf1.in, Hh.lf1.out, p);
             });
         }
@@ -518,7 +527,7 @@ public:
             p.patch = d.patch;
             const int bn = (d.patch * d.patch) % 8 == 0 ? 192 : 96;
             launch(kGemm, 2.0 * Tv * Hh.lf2.out * Hh.lf2.in, [&] {
-                gemm_rows(stream_, bn, EPI_DESC, lf1, d.lf_hidden, static_cast<int>(Tv), d.lf_hidden, Hh.lf2.w, d.lf_hidden, Hh.lf2.out, p);
+                gemm_rows(stream_, d_.dt, bn, EPI_DESC, lf1, d.lf_hidden, static_cast<int>(Tv), d.lf_hidden, Hh.lf2.w, d.lf_hidden, Hh.lf2.out, p);
             });
         }
     }
@@ -568,12 +577,13 @@ Engine::~Engine() = default;
 
 void Engine::load(const std::string& path) {
     SafetensorsFile f(path);
+    const int dt = d_.dt;
     const Dims& d = d_;
     auto L = [&](const std::string& name, int out, int in, bool bias = true) {
         auto w = f.load_f32(name + ".weight", {out, in});
         std::vector<float> b;
         if (bias) b = f.load_f32(name + ".bias", {out});
-        return to_bf16(w, out, in, std::move(b));
+        return to16(dt, w, out, in, std::move(b));
     };
     auto V = [&](const std::string& name, int n) { return f.load_f32(name, {n}); };
 
@@ -585,7 +595,7 @@ void Engine::load(const std::string& path) {
         std::vector<float> t(static_cast<size_t>(d.enc_dim) * d.kpad, 0.0f);
         for (int o = 0; o < d.enc_dim; ++o)
             for (int kk = 0; kk < kp; ++kk) t[static_cast<size_t>(o) * d.kpad + kk] = w[static_cast<size_t>(o) * kp + kk];
-        patch = to_bf16(t, d.enc_dim, d.kpad, V("patch_embed.proj.bias", d.enc_dim));
+        patch = to16(dt, t, d.enc_dim, d.kpad, V("patch_embed.proj.bias", d.enc_dim));
     }
     struct HostEnc {
         std::vector<float> n1g, n1b, n2g, n2b;
@@ -632,7 +642,7 @@ void Engine::load(const std::string& path) {
                 auto bv = V(b + "cross_attn.projv.bias", Dd);
                 wk.insert(wk.end(), wv.begin(), wv.end());
                 bk.insert(bk.end(), bv.begin(), bv.end());
-                e.kv = to_bf16(wk, 2 * Dd, Dd, bk);
+                e.kv = to16(dt, wk, 2 * Dd, Dd, bk);
             }
             e.cproj = L(b + "cross_attn.proj", Dd, Dd);
             e.fc1 = L(b + "mlp.fc1", d.dec_mlp, Dd);
@@ -651,23 +661,23 @@ void Engine::load(const std::string& path) {
         HostHead& H = hh[view];
         auto conv1 = [&](const std::string& name, int out, int in) {
             auto w = f.load_f32(name + ".weight", {out, in, 1, 1});
-            return to_bf16(w, out, in, V(name + ".bias", out));
+            return to16(dt, w, out, in, V(name + ".bias", out));
         };
         H.ap0_0 = conv1(t + "act_postprocess.0.0", 96, d.enc_dim);
-        H.ap0_1t = convt_weights(f.load_f32(t + "act_postprocess.0.1.weight", {96, 96, 4, 4}), 96, 96, 4,
+        H.ap0_1t = convt_weights(dt, f.load_f32(t + "act_postprocess.0.1.weight", {96, 96, 4, 4}), 96, 96, 4,
                                  V(t + "act_postprocess.0.1.bias", 96));
         H.ap1_0 = conv1(t + "act_postprocess.1.0", 192, Dd);
-        H.ap1_1t = convt_weights(f.load_f32(t + "act_postprocess.1.1.weight", {192, 192, 2, 2}), 192, 192, 2,
+        H.ap1_1t = convt_weights(dt, f.load_f32(t + "act_postprocess.1.1.weight", {192, 192, 2, 2}), 192, 192, 2,
                                  V(t + "act_postprocess.1.1.bias", 192));
         H.ap2_0 = conv1(t + "act_postprocess.2.0", 384, Dd);
         H.ap3_0 = conv1(t + "act_postprocess.3.0", 768, Dd);
-        H.ap3_1 = conv3_weights(f.load_f32(t + "act_postprocess.3.1.weight", {768, 768, 3, 3}), 768, 768,
+        H.ap3_1 = conv3_weights(dt, f.load_f32(t + "act_postprocess.3.1.weight", {768, 768, 3, 3}), 768, 768,
                                 V(t + "act_postprocess.3.1.bias", 768));
         for (int k = 0; k < 4; ++k)
-            H.rn[k] = conv3_weights(f.load_f32(t + "scratch.layer_rn." + std::to_string(k) + ".weight", {256, dpt[k], 3, 3}),
+            H.rn[k] = conv3_weights(dt, f.load_f32(t + "scratch.layer_rn." + std::to_string(k) + ".weight", {256, dpt[k], 3, 3}),
                                     256, dpt[k]);
-        H.hd0 = conv3_weights(f.load_f32(t + "head.0.weight", {128, 256, 3, 3}), 128, 256, V(t + "head.0.bias", 128));
-        H.hd2 = conv3_weights(f.load_f32(t + "head.2.weight", {128, 128, 3, 3}), 128, 128, V(t + "head.2.bias", 128));
+        H.hd0 = conv3_weights(dt, f.load_f32(t + "head.0.weight", {128, 256, 3, 3}), 128, 256, V(t + "head.0.bias", 128));
+        H.hd2 = conv3_weights(dt, f.load_f32(t + "head.2.weight", {128, 128, 3, 3}), 128, 128, V(t + "head.2.bias", 128));
         H.w4 = f.load_f32(t + "head.4.weight", {4, 128, 1, 1});
         H.b4 = V(t + "head.4.bias", 4);
         const std::string lf = std::string(view == 0 ? "downstream_head1" : "downstream_head2") + ".head_local_features.";
@@ -685,7 +695,7 @@ void Engine::load(const std::string& path) {
                     std::memcpy(&w2[dst * d.lf_hidden], &w[src * d.lf_hidden], sizeof(float) * d.lf_hidden);
                     b2[dst] = b[src];
                 }
-            H.lf2 = to_bf16(w2, groups * d.desc_dim, d.lf_hidden, b2);
+            H.lf2 = to16(dt, w2, groups * d.desc_dim, d.lf_hidden, b2);
         }
     }
     // RoPE tables (rope2d.py:77-92): freq_i = 1 / 100^(i/16), angle = pos * freq_i in float32

@@ -2,7 +2,6 @@
 // activation arena per device, pairs sharded across devices by host threads.
 #pragma once
 
-#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <memory>
@@ -21,12 +20,13 @@ struct Dims {
     int H, W, hg, wg, ntok;
     int kpad;  // patch-embed K (3 p^2) rounded up to 64
     int hook1, hook2;
+    int dt;    // operand type (Dt)
     int dpt_h, dpt_w;  // 16 * grid
     static Dims from(const m3r_config& c);
 };
 
 struct Lin {
-    __nv_bfloat16* w = nullptr;  // [out, in]
+    uint16_t* w = nullptr;  // [out, in], 16-bit operand type of the engine
     float* b = nullptr;          // [out] or null
     int out = 0, in = 0;
 };

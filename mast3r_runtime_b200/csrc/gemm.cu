@@ -1,4 +1,5 @@
-// Launchers and the instantiated (BN, A mode, epilogue) variants of the tcgen05 GEMM.
+// Launchers and the instantiated (operand type, BN, A mode, epilogue) variants of the
+// tcgen05 GEMM.
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -24,11 +25,11 @@ GemmParams gemm_params() {
 
 namespace {
 
-template <int BN, int AMODE, int EPI>
+template <class T, int BN, int AMODE, int EPI>
 void launch(cudaStream_t s, const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b,
             const GemmParams& p) {
     using C = GemmCfg<BN>;
-    auto kern = gemm_tc_kernel<BN, AMODE, EPI>;
+    auto kern = gemm_tc_kernel<T, BN, AMODE, EPI>;
     static std::once_flag once;  // per instantiation; the attribute is set on every device
     std::call_once(once, [&] {
         int ndev = 0;
@@ -50,12 +51,13 @@ void launch(cudaStream_t s, const CUtensorMap& a0, const CUtensorMap& a1, const 
 
 #define M3R_GEMM_CASE(BN_, AM_, EPI_)                   \
     if (bn == BN_ && amode == AM_ && epi == EPI_) {     \
-        launch<BN_, AM_, EPI_>(s, a0, a1, b, p);        \
+        launch<T, BN_, AM_, EPI_>(s, a0, a1, b, p);     \
         return;                                         \
     }
 
-void dispatch(cudaStream_t s, int bn, int amode, int epi, const CUtensorMap& a0, const CUtensorMap& a1,
-              const CUtensorMap& b, const GemmParams& p) {
+template <class T>
+void dispatch_t(cudaStream_t s, int bn, int amode, int epi, const CUtensorMap& a0, const CUtensorMap& a1,
+                const CUtensorMap& b, const GemmParams& p) {
     M3R_GEMM_CASE(256, A_PLAIN, EPI_BF16)
     M3R_GEMM_CASE(128, A_PLAIN, EPI_BF16)
     M3R_GEMM_CASE(256, A_PLAIN, EPI_F32)
@@ -71,55 +73,66 @@ void dispatch(cudaStream_t s, int bn, int amode, int epi, const CUtensorMap& a0,
     M3R_GEMM_CASE(256, A_CONV3, EPI_BF16)
     M3R_GEMM_CASE(128, A_CONV3, EPI_BF16)
     M3R_GEMM_CASE(128, A_CONV3, EPI_HEAD4)
+    M3R_GEMM_CASE(128, A_CONV3, EPI_F32)  // conv parity test entry
+    M3R_GEMM_CASE(256, A_CONV3, EPI_F32)
     throw Error(kErrArg, "no GEMM variant for bn=" + std::to_string(bn) + " amode=" + std::to_string(amode) +
                              " epi=" + std::to_string(epi));
+}
+
+void dispatch(cudaStream_t s, int dt, int bn, int amode, int epi, const CUtensorMap& a0, const CUtensorMap& a1,
+              const CUtensorMap& b, const GemmParams& p) {
+    if (dt == DT_F16)
+        dispatch_t<__half>(s, bn, amode, epi, a0, a1, b, p);
+    else if (dt == DT_BF16)
+        dispatch_t<__nv_bfloat16>(s, bn, amode, epi, a0, a1, b, p);
+    else
+        throw Error(kErrArg, "unknown operand type " + std::to_string(dt));
 }
 
 int cdiv(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
 
 }  // namespace
 
-void gemm_rows(cudaStream_t s, int bn, int epi, const __nv_bfloat16* A, long long lda, int M, int K,
-               const __nv_bfloat16* W, long long ldw, int N, GemmParams p) {
+void gemm_rows(cudaStream_t s, int dt, int bn, int epi, const void* A, long long lda, int M, int K, const void* W,
+               long long ldw, int N, GemmParams p) {
     M3R_REQUIRE(M >= 0 && N > 0 && K > 0, "gemm: bad shape");
     if (M == 0) return;
-    const CUtensorMap a = tmap_bf16_2d(A, M, K, lda, 128);
-    const CUtensorMap b = tmap_bf16_2d(W, N, K, ldw, bn);
+    const CUtensorMap a = tmap_2d(dt, A, M, K, lda, 128);
+    const CUtensorMap b = tmap_2d(dt, W, N, K, ldw, bn);
     p.M = M;
     p.N = N;
     p.num_kb = cdiv(K, 64);
     p.tiles_m = cdiv(M, 128);
     p.tiles_n = cdiv(N, bn);
-    dispatch(s, bn, A_PLAIN, epi, a, a, b, p);
+    dispatch(s, dt, bn, A_PLAIN, epi, a, a, b, p);
 }
 
-void gemm_concat(cudaStream_t s, int bn, int epi, const __nv_bfloat16* A0, long long lda0, int K0,
-                 const __nv_bfloat16* A1, long long lda1, int K1, int M, const __nv_bfloat16* W, long long ldw,
-                 int N, GemmParams p) {
+void gemm_concat(cudaStream_t s, int dt, int bn, int epi, const void* A0, long long lda0, int K0, const void* A1,
+                 long long lda1, int K1, int M, const void* W, long long ldw, int N, GemmParams p) {
     M3R_REQUIRE(K0 % 64 == 0, "gemm_concat: K0 must be a multiple of 64");
     if (M == 0) return;
-    const CUtensorMap a0 = tmap_bf16_2d(A0, M, K0, lda0, 128);
-    const CUtensorMap a1 = tmap_bf16_2d(A1, M, K1, lda1, 128);
-    const CUtensorMap b = tmap_bf16_2d(W, N, K0 + K1, ldw, bn);
+    const CUtensorMap a0 = tmap_2d(dt, A0, M, K0, lda0, 128);
+    const CUtensorMap a1 = tmap_2d(dt, A1, M, K1, lda1, 128);
+    const CUtensorMap b = tmap_2d(dt, W, N, K0 + K1, ldw, bn);
     p.M = M;
     p.N = N;
     p.a_split_kb = K0 / 64;
     p.num_kb = K0 / 64 + cdiv(K1, 64);
     p.tiles_m = cdiv(M, 128);
     p.tiles_n = cdiv(N, bn);
-    dispatch(s, bn, A_CONCAT, epi, a0, a1, b, p);
+    dispatch(s, dt, bn, A_CONCAT, epi, a0, a1, b, p);
 }
 
-void gemm_conv3(cudaStream_t s, int bn, int epi, const __nv_bfloat16* X, int n, int h, int w, int c, int cstride,
-                const __nv_bfloat16* W, int N, GemmParams p) {
+void gemm_conv3(cudaStream_t s, int dt, int bn, int epi, const void* X, int n, int h, int w, int c, int cstride,
+                const void* W, int N, GemmParams p) {
     M3R_REQUIRE(n > 0 && h > 0 && w > 0 && c > 0 && cstride >= c, "gemm_conv3: bad shape");
     int wbox = 1;
     while (wbox * 2 <= 128 && w % (wbox * 2) == 0) wbox *= 2;
     const int hbox = 128 / wbox;
     M3R_REQUIRE(hbox <= 256, "gemm_conv3: box too tall");
     const int cblocks = cdiv(c, 64);
-    const CUtensorMap a = tmap_bf16_nhwc(X, n, h, w, c, cstride, hbox, wbox);
-    const CUtensorMap b = tmap_bf16_2d(W, N, 9LL * cblocks * 64, 9LL * cblocks * 64, bn);
+    const CUtensorMap a = tmap_nhwc(dt, X, n, h, w, c, cstride, hbox, wbox);
+    const CUtensorMap b = tmap_2d(dt, W, N, 9LL * cblocks * 64, 9LL * cblocks * 64, bn);
     p.M = n * h * w;
     p.N = N;
     p.cv_H = h;
@@ -132,7 +145,7 @@ void gemm_conv3(cudaStream_t s, int bn, int epi, const __nv_bfloat16* X, int n, 
     p.num_kb = 9 * cblocks;
     p.tiles_m = n * p.cv_tx * p.cv_ty;
     p.tiles_n = cdiv(N, bn);
-    dispatch(s, bn, A_CONV3, epi, a, a, b, p);
+    dispatch(s, dt, bn, A_CONV3, epi, a, a, b, p);
 }
 
 }  // namespace m3r

@@ -1,5 +1,6 @@
-// Persistent tcgen05 GEMM for sm_100a:  C[M, N] = A[M, K] * B[N, K]^T  (bf16 in,
-// fp32 accumulate in TMEM), with the fused epilogues of the two-view model.
+// Persistent tcgen05 GEMM for sm_100a:  C[M, N] = A[M, K] * B[N, K]^T  (fp16 or
+// bf16 operands, fp32 accumulate in TMEM), with the fused epilogues of the
+// two-view model.  T is the 16-bit operand type; 16-bit outputs are written as T.
 //
 // Roles (192 threads):  warps 0-3 epilogue (TMEM lanes 0-127 = tile rows),
 // warp 4 TMA producer, warp 5 TMEM allocator + single-thread MMA issuer.
@@ -24,13 +25,13 @@ namespace m3r {
 enum AMode : int { A_PLAIN = 0, A_CONCAT = 1, A_CONV3 = 2 };
 
 enum Epi : int {
-    EPI_BF16 = 0,       // out_bf16 = act(acc + bias)
+    EPI_BF16 = 0,       // out_T = act(acc + bias)   (16-bit output of the operand type T)
     EPI_F32 = 1,        // out_f32 = acc + bias
     EPI_F32_RESID = 2,  // out_f32 = resid_f32 + acc + bias   (resid may alias out)
-    EPI_HEADS = 3,      // + bias, optional 2-D RoPE, scatter to head-major [seq, head, tok, 64] bf16
+    EPI_HEADS = 3,      // + bias, optional 2-D RoPE, scatter to head-major [seq, head, tok, 64] T
     EPI_DESC = 4,       // + bias, pixel shuffle, L2-normalise groups of 24 -> fp32 descriptors
     EPI_HEAD4 = 5,      // + bias, ReLU, fused 1x1 conv 128 -> 4 (+ bias4) -> fp32 [pixel, 4]
-    EPI_CONVT = 6,      // + bias, transposed conv (kernel == stride) scatter -> bf16 NHWC
+    EPI_CONVT = 6,      // + bias, transposed conv (kernel == stride) scatter -> T NHWC
 };
 
 enum Act : int { ACT_NONE = 0, ACT_GELU = 1, ACT_RELU = 2 };
@@ -108,20 +109,21 @@ __device__ __forceinline__ float apply_act(float v, int act) {
     return v;
 }
 
-__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32]) {
+template <class T>
+__device__ __forceinline__ void store16x32(T* dst, const float (&v)[32]) {
     uint4* d = reinterpret_cast<uint4*>(dst);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
         uint4 u;
-        u.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
-        u.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
-        u.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
-        u.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+        u.x = Elem<T>::pack(v[q * 8 + 0], v[q * 8 + 1]);
+        u.y = Elem<T>::pack(v[q * 8 + 2], v[q * 8 + 3]);
+        u.z = Elem<T>::pack(v[q * 8 + 4], v[q * 8 + 5]);
+        u.w = Elem<T>::pack(v[q * 8 + 6], v[q * 8 + 7]);
         d[q] = u;
     }
 }
 
-template <int BN, int AMODE, int EPI>
+template <class T, int BN, int AMODE, int EPI>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeom& g, uint32_t tacc, int r) {
     // tile row r -> global output row
     long long grow;
@@ -156,11 +158,11 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
             if constexpr (EPI == EPI_BF16) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] = apply_act(v[i], p.act);
-                __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + grow * p.ldo + col0;
+                T* dst = reinterpret_cast<T*>(p.out) + grow * p.ldo + col0;
                 if (full) {
-                    store_bf16x32(dst, v);
+                    store16x32<T>(dst, v);
                 } else {
-                    for (int i = 0; i < 32 && col0 + i < p.N; ++i) dst[i] = __float2bfloat16_rn(v[i]);
+                    for (int i = 0; i < 32 && col0 + i < p.N; ++i) dst[i] = Elem<T>::from(v[i]);
                 }
             } else if constexpr (EPI == EPI_CONVT) {
                 // column = (dy * s + dx) * cout + co ; row = token (img, y, x) of the input grid
@@ -173,8 +175,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
                 const int yy = rem / p.ct_w, xx = rem - (rem / p.ct_w) * p.ct_w;
                 const int OH = p.ct_h * p.ct_s, OW = p.ct_w * p.ct_s;
                 const long long opix = (static_cast<long long>(img) * OH + (yy * p.ct_s + dy)) * OW + (xx * p.ct_s + dx);
-                __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + opix * p.ldo + co;
-                store_bf16x32(dst, v);
+                T* dst = reinterpret_cast<T*>(p.out) + opix * p.ldo + co;
+                store16x32<T>(dst, v);
             } else {
                 float* dst = reinterpret_cast<float*>(p.out) + grow * p.ldo + col0;
                 if constexpr (EPI == EPI_F32_RESID) {
@@ -206,7 +208,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
         const int tok = static_cast<int>(grow - static_cast<long long>(seq) * p.n_tok);
         const int py = tok / p.grid_w, px = tok - (tok / p.grid_w) * p.grid_w;
         const bool rope = p.sec_rope[sec] != 0;
-        __nv_bfloat16* base = reinterpret_cast<__nv_bfloat16*>(p.sec_out[sec]);
+        T* base = reinterpret_cast<T*>(p.sec_out[sec]);
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 64) {
             uint32_t ra[32], rb[32];
@@ -234,9 +236,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
                     hi[i] = t1 * s + t2 * c;
                 }
             }
-            __nv_bfloat16* dst = base + ((static_cast<long long>(seq) * nh + head) * p.n_tok + tok) * 64;
-            store_bf16x32(dst, lo);
-            store_bf16x32(dst + 32, hi);
+            T* dst = base + ((static_cast<long long>(seq) * nh + head) * p.n_tok + tok) * 64;
+            store16x32<T>(dst, lo);
+            store16x32<T>(dst + 32, hi);
         }
     } else if constexpr (EPI == EPI_DESC) {
         // Columns are groups of desc_dim (=24) channels, one group per (dy, dx) of the
@@ -305,7 +307,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
 }
 
 // ------------------------------------------------------------------------- kernel
-template <int BN, int AMODE, int EPI>
+template <class T, int BN, int AMODE, int EPI>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_constant__ CUtensorMap mapA1,
                    const __grid_constant__ CUtensorMap mapB, const __grid_constant__ GemmParams p) {
@@ -390,7 +392,7 @@ __global__ void __launch_bounds__(192, 1)
     } else if (warp == 5) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_bf16(128, BN, false, false);
+            constexpr uint32_t idesc = idesc_f16kind<T>(128, BN, false, false);
             uint32_t it = 0, tcount = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++tcount) {
@@ -410,7 +412,7 @@ __global__ void __launch_bounds__(192, 1)
                     for (int k = 0; k < 4; ++k) {
                         const uint64_t ad = umma_desc_sw128(a_addr + k * 32, 16, 1024);
                         const uint64_t bd = umma_desc_sw128(b_addr + k * 32, 16, 1024);
-                        mma_bf16_ss(dacc, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                        mma_f16_ss(dacc, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
                     }
                     mma_commit(&empty[s]);
                 }
@@ -432,7 +434,7 @@ __global__ void __launch_bounds__(192, 1)
             tc_fence_after();
             const TileGeom g = tile_geom<AMODE>(p, t);
             const uint32_t tacc = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + buf * C::ACC_COLS;
-            epilogue_tile<BN, AMODE, EPI>(p, g, tacc, r);
+            epilogue_tile<T, BN, AMODE, EPI>(p, g, tacc, r);
             tc_fence_before();
             mbar_arrive(&tempty[buf]);
         }

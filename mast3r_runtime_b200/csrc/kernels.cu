@@ -1,5 +1,6 @@
-// Bandwidth-bound helper kernels: vectorised (16-byte) loads and stores, grids
-// sized in multiples of the SM count by the launch helpers.
+// Bandwidth-bound helper kernels: vectorised (16-byte) loads and stores,
+// grid-stride loops with grids capped at a multiple of the SM count.
+#include "common.cuh"
 #include "kernels.h"
 #include "tmap.h"
 
@@ -13,8 +14,9 @@ inline int grid_for(long long n, int block) {
     return static_cast<int>(g > 0 ? g : 1);
 }
 
+template <class T>
 __global__ void patch_im2col_kernel(const uint8_t* __restrict__ img, int n, int H, int W, int p, int kpad,
-                                    __nv_bfloat16* __restrict__ out) {
+                                    T* __restrict__ out) {
     const int hg = H / p, wg = W / p;
     const long long total = static_cast<long long>(n) * hg * wg * kpad;
     const float mean[3] = {0.485f, 0.456f, 0.406f};
@@ -34,13 +36,14 @@ __global__ void patch_im2col_kernel(const uint8_t* __restrict__ img, int n, int 
             const uint8_t u = img[((static_cast<long long>(im) * H + gy * p + ky) * W + gx * p + kx) * 3 + c];
             v = (static_cast<float>(u) / 255.0f - mean[c]) / stdv[c];
         }
-        out[e] = __float2bfloat16_rn(v);
+        out[e] = Elem<T>::from(v);
     }
 }
 
 // One warp per row; two-pass mean / variance in fp32 (vit_encoder.py:98-108).
+template <class T>
 __global__ void layernorm_kernel(const float* __restrict__ x, int rows, int D, const float* __restrict__ g,
-                                 const float* __restrict__ b, __nv_bfloat16* __restrict__ y) {
+                                 const float* __restrict__ b, T* __restrict__ y) {
     const int warps = blockDim.x >> 5;
     const int lane = threadIdx.x & 31;
     for (long long r = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5); r < rows;
@@ -80,28 +83,24 @@ __global__ void layernorm_kernel(const float* __restrict__ x, int rows, int D, c
             const int idx = lane + 32 * i;
             if (idx < n4) {
                 const float4 gg = __ldg(g4 + idx), bb = __ldg(b4 + idx);
-                __nv_bfloat162 lo = __floats2bfloat162_rn((v[i].x - mean) * rstd * gg.x + bb.x,
-                                                          (v[i].y - mean) * rstd * gg.y + bb.y);
-                __nv_bfloat162 hi = __floats2bfloat162_rn((v[i].z - mean) * rstd * gg.z + bb.z,
-                                                          (v[i].w - mean) * rstd * gg.w + bb.w);
                 uint2 u;
-                u.x = *reinterpret_cast<uint32_t*>(&lo);
-                u.y = *reinterpret_cast<uint32_t*>(&hi);
+                u.x = Elem<T>::pack((v[i].x - mean) * rstd * gg.x + bb.x, (v[i].y - mean) * rstd * gg.y + bb.y);
+                u.y = Elem<T>::pack((v[i].z - mean) * rstd * gg.z + bb.z, (v[i].w - mean) * rstd * gg.w + bb.w);
                 yr[idx] = u;
             }
         }
     }
 }
 
-__global__ void cast_bf16_kernel(const float* __restrict__ x, long long n, __nv_bfloat16* __restrict__ y) {
+template <class T>
+__global__ void cast16_kernel(const float* __restrict__ x, long long n, T* __restrict__ y) {
     const long long n4 = n >> 2;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
         const float4 v = reinterpret_cast<const float4*>(x)[i];
-        __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
         uint2 u;
-        u.x = *reinterpret_cast<uint32_t*>(&lo);
-        u.y = *reinterpret_cast<uint32_t*>(&hi);
+        u.x = Elem<T>::pack(v.x, v.y);
+        u.y = Elem<T>::pack(v.z, v.w);
         reinterpret_cast<uint2*>(y)[i] = u;
     }
 }
@@ -119,30 +118,30 @@ struct F8 {
     float v[8];
 };
 
-__device__ __forceinline__ void load8(const __nv_bfloat16* p, F8& o) {
+template <class T>
+__device__ __forceinline__ void load8(const T* p, F8& o) {
     const uint4 u = *reinterpret_cast<const uint4*>(p);
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(&u);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(h[i]);
+        const float2 f = Elem<T>::unpack(w[i]);
         o.v[2 * i] = f.x;
         o.v[2 * i + 1] = f.y;
     }
 }
 
-__device__ __forceinline__ void store8(__nv_bfloat16* p, const F8& o) {
+template <class T>
+__device__ __forceinline__ void store8(T* p, const F8& o) {
     uint4 u;
     uint32_t* w = reinterpret_cast<uint32_t*>(&u);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        __nv_bfloat162 h = __floats2bfloat162_rn(o.v[2 * i], o.v[2 * i + 1]);
-        w[i] = *reinterpret_cast<uint32_t*>(&h);
-    }
+    for (int i = 0; i < 4; ++i) w[i] = Elem<T>::pack(o.v[2 * i], o.v[2 * i + 1]);
     *reinterpret_cast<uint4*>(p) = u;
 }
 
-__device__ __forceinline__ void bilerp_acc(const __nv_bfloat16* base, int hi, int wi, int C, int Ho, int Wo, int y,
-                                           int x, int c8, F8& acc) {
+template <class T>
+__device__ __forceinline__ void bilerp_acc(const T* base, int hi, int wi, int C, int Ho, int Wo, int y, int x, int c8,
+                                           F8& acc) {
     int y0, y1, x0, x1;
     float fy, fx;
     src_coord(y, hi, Ho, y0, y1, fy);
@@ -160,10 +159,10 @@ __device__ __forceinline__ void bilerp_acc(const __nv_bfloat16* base, int hi, in
     }
 }
 
-__global__ void dpt_fuse_kernel(const __nv_bfloat16* __restrict__ f0, const __nv_bfloat16* __restrict__ f1, int h1,
-                                int w1, const __nv_bfloat16* __restrict__ f2, int h2, int w2,
-                                const __nv_bfloat16* __restrict__ f3, int h3, int w3, int n, int H0, int W0, int C,
-                                __nv_bfloat16* __restrict__ out) {
+template <class T>
+__global__ void dpt_fuse_kernel(const T* __restrict__ f0, const T* __restrict__ f1, int h1, int w1,
+                                const T* __restrict__ f2, int h2, int w2, const T* __restrict__ f3, int h3, int w3,
+                                int n, int H0, int W0, int C, T* __restrict__ out) {
     const int c8n = C / 8;
     const long long total = static_cast<long long>(n) * H0 * W0 * c8n;
     for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
@@ -183,8 +182,9 @@ __global__ void dpt_fuse_kernel(const __nv_bfloat16* __restrict__ f0, const __nv
     }
 }
 
-__global__ void resize_bf16_kernel(const __nv_bfloat16* __restrict__ x, int n, int hi, int wi, int C, int ho, int wo,
-                                   __nv_bfloat16* __restrict__ y) {
+template <class T>
+__global__ void resize_kernel(const T* __restrict__ x, int n, int hi, int wi, int C, int ho, int wo,
+                              T* __restrict__ y) {
     const int c8n = C / 8;
     const long long total = static_cast<long long>(n) * ho * wo * c8n;
     for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
@@ -203,8 +203,9 @@ __global__ void resize_bf16_kernel(const __nv_bfloat16* __restrict__ x, int n, i
     }
 }
 
-__global__ void im2col_s2_kernel(const __nv_bfloat16* __restrict__ x, int n, int h, int w, int C,
-                                 __nv_bfloat16* __restrict__ out) {
+// 16-bit agnostic: moves 8-element (16-byte) chunks
+__global__ void im2col_s2_kernel(const uint16_t* __restrict__ x, int n, int h, int w, int C,
+                                 uint16_t* __restrict__ out) {
     const int ho = (h - 1) / 2 + 1, wo = (w - 1) / 2 + 1;
     const int c8n = C / 8;
     const long long total = static_cast<long long>(n) * ho * wo * 9 * c8n;
@@ -258,53 +259,67 @@ __global__ void head_split_kernel(const float* __restrict__ o4, int n, int h4, i
     }
 }
 
+#define M3R_BY_DT(dt, ...)                                                  \
+    do {                                                                    \
+        if ((dt) == DT_F16) {                                               \
+            using T = __half;                                               \
+            __VA_ARGS__;                                                    \
+        } else if ((dt) == DT_BF16) {                                       \
+            using T = __nv_bfloat16;                                        \
+            __VA_ARGS__;                                                    \
+        } else {                                                            \
+            throw Error(kErrArg, "unknown operand type");                   \
+        }                                                                   \
+    } while (0)
+
 }  // namespace
 
-void patch_im2col(cudaStream_t s, const uint8_t* img, int n, int H, int W, int p, int kpad, __nv_bfloat16* out) {
+void patch_im2col(cudaStream_t s, int dt, const uint8_t* img, int n, int H, int W, int p, int kpad, void* out) {
     const long long total = static_cast<long long>(n) * (H / p) * (W / p) * kpad;
-    patch_im2col_kernel<<<grid_for(total, 256), 256, 0, s>>>(img, n, H, W, p, kpad, out);
+    M3R_BY_DT(dt, patch_im2col_kernel<T><<<grid_for(total, 256), 256, 0, s>>>(img, n, H, W, p, kpad, static_cast<T*>(out)));
     M3R_CUDA(cudaGetLastError());
 }
 
-void layernorm(cudaStream_t s, const float* x, int rows, int D, const float* gamma, const float* beta,
-               __nv_bfloat16* y) {
+void layernorm(cudaStream_t s, int dt, const float* x, int rows, int D, const float* gamma, const float* beta, void* y) {
     M3R_REQUIRE(D % 4 == 0 && D <= 1024, "layernorm: D must be a multiple of 4 and <= 1024");
     if (rows == 0) return;
     const int warps = 8;
     long long blocks = (rows + warps - 1) / warps;
     if (blocks > 148LL * 16) blocks = 148LL * 16;
-    layernorm_kernel<<<static_cast<int>(blocks), warps * 32, 0, s>>>(x, rows, D, gamma, beta, y);
+    M3R_BY_DT(dt, layernorm_kernel<T><<<static_cast<int>(blocks), warps * 32, 0, s>>>(x, rows, D, gamma, beta, static_cast<T*>(y)));
     M3R_CUDA(cudaGetLastError());
 }
 
-void cast_bf16(cudaStream_t s, const float* x, long long n, __nv_bfloat16* y) {
-    M3R_REQUIRE(n % 4 == 0, "cast_bf16: size must be a multiple of 4");
-    cast_bf16_kernel<<<grid_for(n / 4, 256), 256, 0, s>>>(x, n, y);
+void cast16(cudaStream_t s, int dt, const float* x, long long n, void* y) {
+    M3R_REQUIRE(n % 4 == 0, "cast16: size must be a multiple of 4");
+    M3R_BY_DT(dt, cast16_kernel<T><<<grid_for(n / 4, 256), 256, 0, s>>>(x, n, static_cast<T*>(y)));
     M3R_CUDA(cudaGetLastError());
 }
 
-void dpt_fuse(cudaStream_t s, const __nv_bfloat16* f0, const __nv_bfloat16* f1, int h1, int w1,
-              const __nv_bfloat16* f2, int h2, int w2, const __nv_bfloat16* f3, int h3, int w3, int n, int H0,
-              int W0, int C, __nv_bfloat16* out) {
+void dpt_fuse(cudaStream_t s, int dt, const void* f0, const void* f1, int h1, int w1, const void* f2, int h2, int w2,
+              const void* f3, int h3, int w3, int n, int H0, int W0, int C, void* out) {
     M3R_REQUIRE(C % 8 == 0, "dpt_fuse: C % 8");
     const long long total = static_cast<long long>(n) * H0 * W0 * (C / 8);
-    dpt_fuse_kernel<<<grid_for(total, 256), 256, 0, s>>>(f0, f1, h1, w1, f2, h2, w2, f3, h3, w3, n, H0, W0, C, out);
+    M3R_BY_DT(dt, dpt_fuse_kernel<T><<<grid_for(total, 256), 256, 0, s>>>(
+                      static_cast<const T*>(f0), static_cast<const T*>(f1), h1, w1, static_cast<const T*>(f2), h2, w2,
+                      static_cast<const T*>(f3), h3, w3, n, H0, W0, C, static_cast<T*>(out)));
     M3R_CUDA(cudaGetLastError());
 }
 
-void resize_bf16(cudaStream_t s, const __nv_bfloat16* x, int n, int hi, int wi, int C, int ho, int wo,
-                 __nv_bfloat16* y) {
-    M3R_REQUIRE(C % 8 == 0, "resize_bf16: C % 8");
+void resize16(cudaStream_t s, int dt, const void* x, int n, int hi, int wi, int C, int ho, int wo, void* y) {
+    M3R_REQUIRE(C % 8 == 0, "resize16: C % 8");
     const long long total = static_cast<long long>(n) * ho * wo * (C / 8);
-    resize_bf16_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, n, hi, wi, C, ho, wo, y);
+    M3R_BY_DT(dt, resize_kernel<T><<<grid_for(total, 256), 256, 0, s>>>(static_cast<const T*>(x), n, hi, wi, C, ho, wo,
+                                                                        static_cast<T*>(y)));
     M3R_CUDA(cudaGetLastError());
 }
 
-void im2col_s2(cudaStream_t s, const __nv_bfloat16* x, int n, int h, int w, int C, __nv_bfloat16* out) {
+void im2col_s2(cudaStream_t s, const void* x, int n, int h, int w, int C, void* out) {
     M3R_REQUIRE(C % 8 == 0, "im2col_s2: C % 8");
     const int ho = (h - 1) / 2 + 1, wo = (w - 1) / 2 + 1;
     const long long total = static_cast<long long>(n) * ho * wo * 9 * (C / 8);
-    im2col_s2_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, n, h, w, C, out);
+    im2col_s2_kernel<<<grid_for(total, 256), 256, 0, s>>>(static_cast<const uint16_t*>(x), n, h, w, C,
+                                                          static_cast<uint16_t*>(out));
     M3R_CUDA(cudaGetLastError());
 }
 

@@ -1,36 +1,32 @@
-// Bandwidth-bound helper kernels of the two-view model (kernels.cu).
+// Bandwidth-bound helper kernels of the two-view model (kernels.cu).  16-bit
+// tensors are of the operand type `dt` (DT_F16 or DT_BF16, common.cuh).
 #pragma once
 
-#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace m3r {
 
-// uint8 [n, H, W, 3] -> bf16 patch rows [n * (H/p) * (W/p), kpad]; column
-// c*p*p + ky*p + kx, value (x/255 - mean_c) / std_c (python_engine.py:176-188),
-// zero in [3*p*p, kpad).
-void patch_im2col(cudaStream_t s, const uint8_t* img, int n, int H, int W, int p, int kpad, __nv_bfloat16* out);
+// uint8 [n, H, W, 3] -> patch rows [n * (H/p) * (W/p), kpad]; column c*p*p + ky*p + kx,
+// value (x/255 - mean_c) / std_c (python_engine.py:176-188), zero in [3*p*p, kpad).
+void patch_im2col(cudaStream_t s, int dt, const uint8_t* img, int n, int H, int W, int p, int kpad, void* out);
 
-// y = LayerNorm(x) * gamma + beta (eps 1e-6), x fp32 [rows, D], y bf16 [rows, D].
-void layernorm(cudaStream_t s, const float* x, int rows, int D, const float* gamma, const float* beta,
-               __nv_bfloat16* y);
+// y = LayerNorm(x) * gamma + beta (eps 1e-6), x fp32 [rows, D], y 16-bit [rows, D].
+void layernorm(cudaStream_t s, int dt, const float* x, int rows, int D, const float* gamma, const float* beta, void* y);
 
-// fp32 -> bf16, [rows, D] contiguous.
-void cast_bf16(cudaStream_t s, const float* x, long long n, __nv_bfloat16* y);
+// fp32 -> 16-bit, n elements (n % 4 == 0).
+void cast16(cudaStream_t s, int dt, const float* x, long long n, void* y);
 
 // out[n, H0, W0, C] = f0 + up(f1) + up(f2) + up(f3), bilinear (half-pixel,
-// align_corners=False); f_k is [n, h_k, w_k, C] bf16, C % 8 == 0.
-void dpt_fuse(cudaStream_t s, const __nv_bfloat16* f0, const __nv_bfloat16* f1, int h1, int w1,
-              const __nv_bfloat16* f2, int h2, int w2, const __nv_bfloat16* f3, int h3, int w3, int n, int H0,
-              int W0, int C, __nv_bfloat16* out);
+// align_corners=False); f_k is [n, h_k, w_k, C], C % 8 == 0.
+void dpt_fuse(cudaStream_t s, int dt, const void* f0, const void* f1, int h1, int w1, const void* f2, int h2, int w2,
+              const void* f3, int h3, int w3, int n, int H0, int W0, int C, void* out);
 
-// Bilinear resize NHWC bf16 [n, hi, wi, C] -> [n, ho, wo, C] (half-pixel), C % 8 == 0.
-void resize_bf16(cudaStream_t s, const __nv_bfloat16* x, int n, int hi, int wi, int C, int ho, int wo,
-                 __nv_bfloat16* y);
+// Bilinear resize NHWC [n, hi, wi, C] -> [n, ho, wo, C] (half-pixel), C % 8 == 0.
+void resize16(cudaStream_t s, int dt, const void* x, int n, int hi, int wi, int C, int ho, int wo, void* y);
 
 // 3x3 / stride 2 / pad 1 im2col: x [n, h, w, C] -> [n * ho * wo, 9 * C], tap-major.
-void im2col_s2(cudaStream_t s, const __nv_bfloat16* x, int n, int h, int w, int C, __nv_bfloat16* out);
+void im2col_s2(cudaStream_t s, const void* x, int n, int h, int w, int C, void* out);
 
 // out4 fp32 [n, h4, w4, 4] -> pts3d [n, H, W, 3], conf [n, H, W]; bilinear
 // (half-pixel) when (h4, w4) != (H, W).

@@ -4,9 +4,10 @@
 // Arithmetic is restated exactly as the reference computes it (its build has no
 // FMA): normalisation s = s + x*x sequentially, n = sqrtf(s), x * (1.0f / n) when
 // n > 1e-8; similarity d = d + a[k]*b[k] for k = 0..D-1, every multiply and add
-// separately rounded (mul.rn / add.rn, never contracted).  On Blackwell the
-// packed mul.rn.f32x2 / add.rn.f32x2 forms do two such operations per
-// instruction without changing a single rounding.
+// separately rounded (__fmul_rn / __fadd_rn, never contracted into an FMA).
+// A packed mul.rn.f32x2 followed by add.rn.f32x2 is NOT safe for this: the
+// pair was measured to be fused (about 60% of 24-term dot products changed),
+// while packed/scalar mixes stay exact but are no faster than scalar here.
 //
 // Pipeline (one device, rows [row0, row1) of set A against all of set B):
 //   normalize      one thread per row
@@ -70,26 +71,6 @@ constexpr int kTJ = 128;  // columns per j-tile
 constexpr int kKC = 32;   // k chunk held in shared memory
 constexpr int kPitch = 128 + 4;
 
-__device__ __forceinline__ unsigned long long dup2(float a) {
-    unsigned long long r;
-    asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(a));
-    return r;
-}
-__device__ __forceinline__ unsigned long long pack2(float a, float b) {
-    unsigned long long r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-    return r;
-}
-__device__ __forceinline__ void unpack2(unsigned long long v, float& a, float& b) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
-}
-// acc = acc + a * b, elementwise on float pairs, each operation rounded separately.
-__device__ __forceinline__ void mul_add2(unsigned long long& acc, unsigned long long a, unsigned long long b) {
-    unsigned long long t;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(t) : "l"(a), "l"(b));
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(acc) : "l"(acc), "l"(t));
-}
-
 // Thread (tr, tc) of a 16 x 16 grid owns rows tr*8 .. +8 and columns
 // {tc*4 .. +4} U {64 + tc*4 .. +4} of the 128 x 128 tile.  Warp w holds
 // tr in [4*(w/2), +4), tc in [8*(w%2), +8): lane = tr_l * 8 + tc_l.
@@ -126,11 +107,12 @@ __global__ void __launch_bounds__(256, 2)
     const bool a_resident = D <= kKC;
     for (long long jt = jt_begin; jt < jt_end; ++jt) {
         const long long j0 = jt * kTJ;
-        unsigned long long acc[8][4];
+        // s[r][c]: similarity of row tr*8 + r and column (c < 4 ? tc*4 + c : 64 + tc*4 + c - 4)
+        float s[8][8];
 #pragma unroll
         for (int r = 0; r < 8; ++r)
 #pragma unroll
-            for (int c = 0; c < 4; ++c) acc[r][c] = 0ull;
+            for (int c = 0; c < 8; ++c) s[r][c] = 0.0f;
 
         for (int kc = 0; kc < D; kc += kKC) {
             const int kn = D - kc < kKC ? D - kc : kKC;
@@ -157,24 +139,14 @@ __global__ void __launch_bounds__(256, 2)
                 const float4 a1 = *reinterpret_cast<const float4*>(&sA[k][tr * 8 + 4]);
                 const float4 b0 = *reinterpret_cast<const float4*>(&sB[k][tc * 4]);
                 const float4 b1 = *reinterpret_cast<const float4*>(&sB[k][64 + tc * 4]);
-                const unsigned long long bp[4] = {pack2(b0.x, b0.y), pack2(b0.z, b0.w), pack2(b1.x, b1.y),
-                                                  pack2(b1.z, b1.w)};
+                const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
                 const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
-                for (int r = 0; r < 8; ++r) {
-                    const unsigned long long ad = dup2(av[r]);
+                for (int r = 0; r < 8; ++r)
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) mul_add2(acc[r][c], ad, bp[c]);
-                }
+                    for (int c = 0; c < 8; ++c) s[r][c] = __fadd_rn(s[r][c], __fmul_rn(av[r], bv[c]));
             }
         }
-
-        // unpack: s[r][c], c in 0..7 -> column j0 + (c < 4 ? tc*4 + c : 64 + tc*4 + c - 4)
-        float s[8][8];
-#pragma unroll
-        for (int r = 0; r < 8; ++r)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) unpack2(acc[r][c], s[r][2 * c], s[r][2 * c + 1]);
 
         // ---- rows: first (lowest j) maximum over this thread's columns, in increasing j
 #pragma unroll

@@ -1,5 +1,7 @@
 // Host-side TMA tensor-map encoding (cuTensorMapEncodeTiled through the runtime's
-// driver entry point, so the library does not link libcuda directly).
+// driver entry point, so the library does not link libcuda directly).  All maps
+// are of 16-bit elements (fp16 or bf16, `dt` = Dt), 128-byte swizzled boxes whose
+// inner extent is 64 elements; out-of-bounds box elements read as zero.
 #pragma once
 
 #include <cuda.h>
@@ -40,16 +42,14 @@ constexpr int kErrNoMem = -7;
         if (!(cond)) throw ::m3r::Error(::m3r::kErrArg, std::string(msg)); \
     } while (0)
 
-// bf16 row-major matrix [rows, cols] with row stride ld (elements); box
-// [box_rows, 64] with 128-byte swizzle.  Out-of-bounds boxes read zero.
-CUtensorMap tmap_bf16_2d(const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows);
+// row-major matrix [rows, cols] with row stride ld (elements); box [box_rows, 64].
+CUtensorMap tmap_2d(int dt, const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows);
 
-// bf16 tensor [d2, d1, 64] (innermost 64 = head dim), box [box_d1, 64].
-CUtensorMap tmap_bf16_3d_rows64(const void* ptr, uint64_t d1, uint64_t d2, uint32_t box_d1);
+// tensor [d2, d1, 64] (innermost 64 = head dim), box [box_d1, 64].
+CUtensorMap tmap_3d_rows64(int dt, const void* ptr, uint64_t d1, uint64_t d2, uint32_t box_d1);
 
-// bf16 NHWC tensor [n, h, w, c] (row stride of a pixel = cstride elements), box
-// [1, hbox, wbox, 64].
-CUtensorMap tmap_bf16_nhwc(const void* ptr, uint64_t n, uint64_t h, uint64_t w, uint64_t c, uint64_t cstride,
-                           uint32_t hbox, uint32_t wbox);
+// NHWC tensor [n, h, w, c] (pixel stride cstride elements), box [1, hbox, wbox, 64].
+CUtensorMap tmap_nhwc(int dt, const void* ptr, uint64_t n, uint64_t h, uint64_t w, uint64_t c, uint64_t cstride,
+                      uint32_t hbox, uint32_t wbox);
 
 }  // namespace m3r

@@ -57,7 +57,7 @@ def gelu(x):
 
 def linear(x, w, b=None):
     """vit_encoder.py:111-120: y = x W^T + b, W [out, in]."""
-    y = x @ np.asarray(w, np.float64).T
+    y = x @ np.asarray(w).T
     return y if b is None else y + b
 
 
@@ -115,8 +115,8 @@ def conv2d(x, w, b=None, stride=1, pad=0):
         x = np.pad(x, ((pad, pad), (pad, pad), (0, 0)))
     ho = (hh + 2 * pad - kh) // stride + 1
     wo = (ww + 2 * pad - kw) // stride + 1
-    wt = np.asarray(w, np.float64).transpose(2, 3, 1, 0)  # [kh, kw, ci, co]
-    out = np.zeros((ho, wo, co))
+    wt = np.asarray(w).transpose(2, 3, 1, 0)  # [kh, kw, ci, co]
+    out = np.zeros((ho, wo, co), np.result_type(x, wt))
     for dy in range(kh):
         for dx in range(kw):
             xs = x[dy: dy + stride * (ho - 1) + 1: stride, dx: dx + stride * (wo - 1) + 1: stride]
@@ -129,7 +129,7 @@ def conv_transpose_k_eq_s(x, w, b, s):
     out[s*y + dy, s*x + dx, co] = b[co] + sum_ci x[y, x, ci] w[ci, co, dy, dx]."""
     hh, ww, ci = x.shape
     co = w.shape[1]
-    y = np.einsum("yxc,codk->ydxko", x, np.asarray(w, np.float64))  # [H, s, W, s, co]
+    y = np.einsum("yxc,codk->ydxko", x, np.asarray(w))  # [H, s, W, s, co]
     return y.reshape(hh * s, ww * s, co) + b
 
 
@@ -172,10 +172,15 @@ def interpolate_bilinear_ref(x, ho, wo):
 # ----------------------------------------------------------------------------- model
 
 class Model:
-    """Float64 restatement of encoder + decoder + heads for one image pair."""
+    """Restatement of encoder + decoder + heads for one image pair.
 
-    def __init__(self, weights: dict, dims):
-        self.w = {k: np.asarray(v, np.float64) for k, v in weights.items()}
+    ``dtype`` float64 (default) is the parity reference; float32 is the arithmetic the
+    reference's numpy path starts from and is used to time the CPU baseline.
+    """
+
+    def __init__(self, weights: dict, dims, dtype=np.float64):
+        self.dt = np.dtype(dtype)
+        self.w = {k: np.asarray(v, self.dt) for k, v in weights.items()}
         self.d = dims
 
     # croco_encoder.py:245-283
@@ -184,10 +189,12 @@ class Model:
         p = d.patch
         _, hh, ww = img_chw.shape
         hg, wg = hh // p, ww // p
+        img_chw = img_chw.astype(self.dt)
         patches = img_chw[:, : hg * p, : wg * p].reshape(3, hg, p, wg, p).transpose(1, 3, 0, 2, 4)
         x = patches.reshape(hg * wg, 3 * p * p) @ W["patch_embed.proj.weight"].reshape(d.enc_dim, -1).T
         x = x + W["patch_embed.proj.bias"]
         cos, sin = rope_tables(positions(hg, wg), d.head_dim)
+        cos, sin = cos.astype(self.dt), sin.astype(self.dt)
         scale = d.head_dim ** -0.5
         for i in range(d.enc_depth):
             b = f"enc_blocks.{i}."
@@ -233,6 +240,7 @@ class Model:
     def decode(self, enc1, enc2, grid):
         d, W = self.d, self.w
         cos, sin = rope_tables(positions(*grid), d.head_dim)
+        cos, sin = cos.astype(self.dt), sin.astype(self.dt)
         p1 = linear(enc1, W["decoder_embed.weight"], W["decoder_embed.bias"])
         p2 = linear(enc2, W["decoder_embed.weight"], W["decoder_embed.bias"])
         outs = []

@@ -37,6 +37,26 @@ def bf16_round(x: np.ndarray) -> np.ndarray:
     return from_bf16_bits(to_bf16_bits(x))
 
 
+DTYPES = {"fp16": 1, "bf16": 0}  # M3R_DTYPE_F16 / M3R_DTYPE_BF16
+
+
+def to16(x: np.ndarray, dtype: str) -> np.ndarray:
+    """float32 -> 16-bit operand bits of `dtype` ("fp16" or "bf16"), round to nearest even."""
+    if dtype == "fp16":
+        return np.ascontiguousarray(x, np.float32).astype(np.float16).view(np.uint16)
+    return to_bf16_bits(x)
+
+
+def from16(b: np.ndarray, dtype: str) -> np.ndarray:
+    if dtype == "fp16":
+        return b.view(np.float16).astype(np.float32)
+    return from_bf16_bits(b)
+
+
+def round16(x: np.ndarray, dtype: str) -> np.ndarray:
+    return from16(to16(x, dtype), dtype)
+
+
 def rel_l2(a, b) -> float:
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)

@@ -1,0 +1,205 @@
+"""Kernel parity on the GPU, through the C ABI (include/m3r_cuda.h).
+
+GEMM / conv / attention are floating point: compared with float64 references computed
+from the same bf16-rounded operands, tolerances stated per test.  The matcher is
+compared with the oracle bit for bit (indices and confidences)."""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import DTYPES, from16, matcher_inputs, rel_l2, round16, to16
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from mast3r_runtime_b200 import _lib
+
+    L = _lib.load()
+    n = ctypes.c_int(0)
+    _lib.check(L.m3r_device_count(ctypes.byref(n)))
+    assert n.value > 0, "no CUDA device visible"
+    return L
+
+
+def P(a):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+# ---------------------------------------------------------------------------- GEMM
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+@pytest.mark.parametrize("M,N,K,bn", [
+    (128, 256, 64, 256),
+    (300, 200, 136, 128),   # ragged M, N, K (TMA zero fill, epilogue masks)
+    (389, 512, 1024, 256),
+    (1000, 96, 96, 128),
+    (2048, 768, 3072, 256),
+])
+def test_gemm_matches_fp64(lib, M, N, K, bn, dtype):
+    from mast3r_runtime_b200 import _lib
+
+    rng = np.random.default_rng(M + N + K)
+    a = round16(rng.standard_normal((M, K)).astype(np.float32), dtype)
+    w = round16(rng.standard_normal((N, K)).astype(np.float32) * 0.05, dtype)
+    bias = rng.standard_normal(N).astype(np.float32)
+    c = np.zeros((M, N), np.float32)
+    ms = ctypes.c_float(0)
+    _lib.check(lib.m3r_gemm_test(0, DTYPES[dtype], P(to16(a, dtype)), P(to16(w, dtype)), P(bias), P(c), M, N, K, bn,
+                                 2, ctypes.byref(ms)))
+    ref = a.astype(np.float64) @ w.astype(np.float64).T + bias
+    # fp32 accumulation of K exact 16-bit products: relative error ~ sqrt(K) * 2^-24
+    assert rel_l2(c, ref) < 1e-5, rel_l2(c, ref)
+    assert np.abs(c - ref).max() < 1e-4 * np.sqrt(K) * (np.abs(ref).max() + 1)
+
+
+def _conv3_ref(x, w, b):
+    n, h, wd, c = x.shape
+    co = w.shape[0]
+    xp = np.pad(x.astype(np.float64), ((0, 0), (1, 1), (1, 1), (0, 0)))
+    out = np.zeros((n, h, wd, co))
+    for t in range(9):
+        dy, dx = t // 3, t % 3
+        out += xp[:, dy:dy + h, dx:dx + wd, :] @ w[:, t, :c].T.astype(np.float64)
+    return out + b
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+@pytest.mark.parametrize("n,h,wd,c,cout,bn", [
+    (2, 8, 16, 64, 128, 128),
+    (1, 12, 12, 96, 256, 256),    # channels padded to 128; w = 12 -> 4-wide boxes
+    (2, 5, 32, 192, 128, 128),    # h not a multiple of the box height
+    (1, 16, 128, 128, 128, 128),
+])
+def test_conv3_matches_fp64(lib, n, h, wd, c, cout, bn, dtype):
+    from mast3r_runtime_b200 import _lib
+
+    rng = np.random.default_rng(n * 1000 + h + wd + c)
+    cpad = (c + 63) // 64 * 64
+    x = round16(rng.standard_normal((n, h, wd, c)).astype(np.float32), dtype)
+    w = np.zeros((cout, 9, cpad), np.float32)
+    w[:, :, :c] = round16(rng.standard_normal((cout, 9, c)).astype(np.float32) * 0.05, dtype)
+    b = rng.standard_normal(cout).astype(np.float32)
+    y = np.zeros((n, h, wd, cout), np.float32)
+    _lib.check(lib.m3r_conv3_test(0, DTYPES[dtype], P(to16(x, dtype)), P(to16(w, dtype)), P(b), P(y), n, h, wd, c,
+                                  cout, bn))
+    ref = _conv3_ref(x, w, b)
+    assert rel_l2(y, ref) < 1e-5, rel_l2(y, ref)
+
+
+# ---------------------------------------------------------------------------- attention
+def _attn_ref(q, k, v, scale):
+    s = np.einsum("shqd,shkd->shqk", q.astype(np.float64), k.astype(np.float64)) * scale
+    s -= s.max(-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(-1, keepdims=True)
+    o = np.einsum("shqk,shkd->shqd", p, v.astype(np.float64))
+    return o.transpose(0, 2, 1, 3).reshape(q.shape[0], q.shape[2], -1)  # [s, tok, h*64]
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+@pytest.mark.parametrize("s,h,nq,nk", [
+    (2, 3, 128, 128),
+    (3, 2, 576, 576),   # 4.5 tiles: masked key tail, partial query tile
+    (1, 1, 24, 24),     # tiny grid of the golden model
+    (2, 2, 200, 300),   # nq != nk (cross attention)
+    (2, 12, 768, 768),
+])
+def test_attention_matches_fp64(lib, s, h, nq, nk, dtype):
+    from mast3r_runtime_b200 import _lib
+
+    rng = np.random.default_rng(s * 100 + h + nq + nk)
+    q = round16(rng.standard_normal((s, h, nq, 64)).astype(np.float32), dtype)
+    k = round16(rng.standard_normal((s, h, nk, 64)).astype(np.float32), dtype)
+    v = round16(rng.standard_normal((s, h, nk, 64)).astype(np.float32), dtype)
+    out = np.zeros((s, nq, h * 64), np.uint16)
+    ms = ctypes.c_float(0)
+    _lib.check(lib.m3r_attention_fwd(0, DTYPES[dtype], P(to16(q, dtype)), P(to16(k, dtype)), P(to16(v, dtype)),
+                                     P(out), s, h, nq, nk, 0.125, 2, ctypes.byref(ms)))
+    got = from16(out, dtype)
+    ref = _attn_ref(q, k, v, 0.125)
+    # 16-bit probabilities and output: |err| ~ 2^-8 (bf16) / 2^-11 (fp16) of the output scale
+    tol = 1e-2 if dtype == "bf16" else 2e-3
+    err = rel_l2(got, ref)
+    assert err < tol, err
+    assert np.abs(got - ref).max() < 3 * tol * (np.abs(ref).max() + 1e-3)
+
+
+# ---------------------------------------------------------------------------- matcher
+def _nn_gpu(lib, a, b):
+    from mast3r_runtime_b200 import _lib
+
+    n1, d = a.shape
+    n2 = b.shape[0]
+    nn12 = np.zeros(n1, np.int32)
+    nn21 = np.zeros(n2, np.int32)
+    b12 = np.zeros(n1, np.float32)
+    ms = ctypes.c_float(0)
+    _lib.check(lib.m3r_match_nn(0, P(np.ascontiguousarray(a)), P(np.ascontiguousarray(b)), n1, n2, d, P(nn12),
+                                P(nn21), P(b12), ctypes.byref(ms)))
+    return nn12, nn21, b12
+
+
+@pytest.mark.parametrize("n1,n2,d", [(4096, 4096, 24), (1000, 3001, 24), (777, 555, 64), (300, 260, 256), (5, 7, 24)])
+def test_match_argmax_bit_exact(lib, oracle_lib, n1, n2, d):
+    rng = np.random.default_rng(n1 + n2 + d)
+    a = rng.standard_normal((n1, d)).astype(np.float32)
+    b = rng.standard_normal((n2, d)).astype(np.float32)
+    b[: n2 // 4] = a[rng.integers(0, n1, n2 // 4)]          # exact copies: ties between rows
+    a[n1 // 2: n1 // 2 + 3] = a[0]                          # duplicated rows: column ties
+    g12, g21, gb = _nn_gpu(lib, a, b)
+    an = oracle_lib.normalize(a)
+    bn = oracle_lib.normalize(b)
+    o12, ob12, o21, _ = oracle_lib.argmax(an, bn)
+    np.testing.assert_array_equal(g12, o12)
+    np.testing.assert_array_equal(g21, o21)
+    assert gb.tobytes() == ob12.tobytes()
+
+
+@pytest.fixture(scope="module")
+def matcher_engine(lib):
+    from mast3r_runtime_b200 import NativeEngine, tiny_dims
+
+    return NativeEngine(tiny_dims(), (32, 32), [0], 1)
+
+
+@pytest.mark.parametrize("h,w,d,top_k,recip,thr", [
+    (64, 64, 24, 512, True, 0.5),      # top-k selection path
+    (48, 64, 24, 4096, True, 0.0),     # all candidates, i order
+    (48, 64, 24, 100, False, 0.5),
+    (16, 16, 64, 512, True, 0.0),
+    (192, 256, 24, 512, True, 0.5),    # a quarter of the 512x384 map
+])
+def test_match_bit_exact_vs_oracle(matcher_engine, oracle_lib, h, w, d, top_k, recip, thr):
+    a, b = matcher_inputs(h, w, d, h * w + d)
+    r = matcher_engine.match(a, b, top_k=top_k, reciprocal=recip, confidence_threshold=thr)
+    o = oracle_lib.match(a, b, top_k=top_k, reciprocal=recip, confidence_threshold=thr)
+    np.testing.assert_array_equal(r.idx_1, o["idx_1"])
+    np.testing.assert_array_equal(r.idx_2, o["idx_2"])
+    assert r.confidence.tobytes() == o["confidence"].tobytes()
+    np.testing.assert_array_equal(r.pts2d_1, o["pts2d_1"])
+    np.testing.assert_array_equal(r.pts2d_2, o["pts2d_2"])
+
+
+def test_match_kats_gpu(matcher_engine):
+    rng = np.random.default_rng(0)
+    desc = rng.random((8, 8, 64)).astype(np.float32)
+    r = matcher_engine.match(desc, desc, reciprocal=True, confidence_threshold=0.0)
+    np.testing.assert_array_equal(r.idx_1, r.idx_2)
+    assert len(r.idx_1) == 64
+    same = np.ones((4, 4, 24), np.float32)
+    r = matcher_engine.match(same, same, top_k=16, confidence_threshold=0.0)
+    assert r.idx_1.tolist() == [0] and r.idx_2.tolist() == [0]
+    d1 = np.zeros((4, 4, 64), np.float32)
+    d1[..., :32] = 1.0
+    d2 = np.zeros((4, 4, 64), np.float32)
+    d2[..., 32:] = 1.0
+    assert len(matcher_engine.match(d1, d2, confidence_threshold=0.5).idx_1) == 0
+    empty = np.zeros((0, 0, 64), np.float32)
+    assert len(matcher_engine.match(empty, empty).idx_1) == 0
+    one = rng.random((1, 1, 64)).astype(np.float32)
+    assert len(matcher_engine.match(one, one).idx_1) <= 1

@@ -1,0 +1,133 @@
+"""End-to-end parity of the two-view forward pass on the GPU against the oracle
+(oracle/model.py, itself pinned to the reference's numpy model by tests/test_oracle.py).
+
+Tolerances (the stated bar): pts3d relative L2 <= 1e-2, descriptor cosine >= 0.999.
+The confidence map is held to the same relative-L2 bar as pts3d."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+def _compare(out, ref, hw):
+    H, W = hw
+    rep = {}
+    for v in (1, 2):
+        assert out[f"pts3d_{v}"].shape == (H, W, 3)
+        assert out[f"desc_{v}"].shape == (H, W, 24)
+        assert out[f"conf_{v}"].shape == (H, W)
+        rep[f"pts3d_{v}"] = rel_l2(out[f"pts3d_{v}"], ref[f"pts3d_{v}"])
+        rep[f"conf_{v}"] = rel_l2(out[f"conf_{v}"], ref[f"conf_{v}"])
+        g = out[f"desc_{v}"].astype(np.float64)
+        r = ref[f"desc_{v}"]
+        cos = (g * r).sum(-1) / np.maximum(np.linalg.norm(g, axis=-1) * np.linalg.norm(r, axis=-1), 1e-30)
+        rep[f"desc_cos_min_{v}"] = float(cos.min())
+        rep[f"desc_cos_mean_{v}"] = float(cos.mean())
+    return rep
+
+
+def _run(tmp_path, dims, hw, seed, randomize_affine, n_pairs=1, max_pairs=None, dtype=1):
+    from mast3r_runtime_b200 import NativeEngine, make_weights, save_safetensors
+
+    w = make_weights(dims, seed=seed, randomize_affine=randomize_affine)
+    path = save_safetensors(tmp_path / "unified.safetensors", w)
+    rng = np.random.default_rng(seed + 1)
+    img1 = rng.integers(0, 256, (n_pairs, *hw, 3), dtype=np.uint8)
+    img2 = rng.integers(0, 256, (n_pairs, *hw, 3), dtype=np.uint8)
+    eng = NativeEngine(dims, hw, [0], max_pairs or n_pairs, dtype)
+    eng.load(str(path))
+    out, timing = eng.infer_batch(img1, img2)
+    eng.close()
+    return w, img1, img2, out, timing
+
+
+@pytest.mark.parametrize("dtype", [1, 0], ids=["fp16", "bf16"])
+def test_tiny_model_matches_oracle(tmp_path, dtype):
+    from mast3r_runtime_b200.weights import tiny_dims
+    from oracle.model import Model
+
+    d = tiny_dims()
+    w, img1, img2, out, timing = _run(tmp_path, d, (64, 96), 11, True, n_pairs=2, dtype=dtype)
+    m = Model(w, d)
+    for p in range(2):
+        ref = m.forward(img1[p], img2[p])
+        rep = _compare({k: v[p] for k, v in out.items()}, ref, (64, 96))
+        print(rep)
+        for v in (1, 2):
+            assert rep[f"pts3d_{v}"] <= 1e-2, rep
+            assert rep[f"conf_{v}"] <= 1e-2, rep
+            assert rep[f"desc_cos_mean_{v}"] >= 0.999, rep
+    assert timing["inference_ms"] > 0
+
+
+def test_dune_small_336_matches_oracle(tmp_path):
+    """The CPU-runnable parity configuration: DUNE ViT-S/14 encoder + MASt3R decoder,
+    336x336, one pair, trunc-normal(0.02) weights, zero biases, unit LayerNorm; fp16
+    operands (precision "fp32"/"fp16").  bf16 operands miss the pts3d bar here
+    (measured rel-L2 0.011 on view 2), which is why fp16 is the default."""
+    from mast3r_runtime_b200.weights import VARIANTS
+    from oracle.model import Model
+
+    d = VARIANTS["dune_vit_small_336"]
+    w, img1, img2, out, _ = _run(tmp_path, d, (336, 336), 0, False)
+    ref = Model(w, d).forward(img1[0], img2[0])
+    rep = _compare({k: v[0] for k, v in out.items()}, ref, (336, 336))
+    print(rep)
+    for v in (1, 2):
+        assert rep[f"pts3d_{v}"] <= 1e-2, rep
+        assert rep[f"desc_cos_mean_{v}"] >= 0.999, rep
+
+
+def test_batch_equals_single(tmp_path):
+    """Pairs are independent: a batched launch reproduces single-pair launches exactly."""
+    from mast3r_runtime_b200 import NativeEngine, make_weights, save_safetensors
+    from mast3r_runtime_b200.weights import tiny_dims
+
+    d = tiny_dims()
+    path = save_safetensors(tmp_path / "u.safetensors", make_weights(d, seed=3, randomize_affine=True))
+    rng = np.random.default_rng(9)
+    img1 = rng.integers(0, 256, (3, 64, 96, 3), dtype=np.uint8)
+    img2 = rng.integers(0, 256, (3, 64, 96, 3), dtype=np.uint8)
+    eng = NativeEngine(d, (64, 96), [0], 3)
+    eng.load(str(path))
+    batch, _ = eng.infer_batch(img1, img2)
+    for p in range(3):
+        single, _ = eng.infer_batch(img1[p:p + 1], img2[p:p + 1])
+        for k in batch:
+            np.testing.assert_array_equal(batch[k][p], single[k][0])
+    eng.close()
+
+
+def test_drop_in_engine_contract(tmp_path):
+    """The object NativeEngineWrapper drives (native_wrapper.py:40-140): same calls, same fields."""
+    from mast3r_runtime_b200 import CUDAEngine, get_compute_capability, is_available, make_weights, save_safetensors
+    from mast3r_runtime_b200.weights import VARIANTS
+
+    assert is_available()
+    assert get_compute_capability() >= (10, 0)
+    d = VARIANTS["dune_vit_small_336"]
+    path = save_safetensors(tmp_path / "safetensors" / "dune_vit_small_336" / "decoder.safetensors", make_weights(d, seed=1))
+    eng = CUDAEngine(variant="dune_vit_small_336", resolution=336, precision="fp16", num_threads=4)
+    assert not eng.is_ready()
+    eng.load(str(path))
+    assert eng.is_ready()
+    assert "CUDA" in eng.name()
+    eng.warmup(1)
+    rng = np.random.default_rng(0)
+    img = rng.integers(0, 256, (336, 336, 3), dtype=np.uint8)
+    r = eng.infer(img, img[::-1].copy())
+    for k, shape in (("pts3d_1", (336, 336, 3)), ("desc_2", (336, 336, 24)), ("conf_1", (336, 336))):
+        a = np.asarray(getattr(r, k))
+        assert a.shape == shape and a.dtype == np.float32
+    t = dict(r.timing)
+    assert t["inference_ms"] > 0
+    m = eng.match(r.desc_1, r.desc_2, top_k=128, reciprocal=True, confidence_threshold=0.5)
+    assert m.idx_1.dtype == np.int64 and m.pts2d_1.shape == (len(m.idx_1), 2) and m.pts3d_1.shape == (len(m.idx_1), 3)
+    assert len(m.idx_1) <= 128 and "match_ms" in dict(m.timing)
+    with pytest.raises(RuntimeError):
+        eng.infer(np.zeros((10, 10), np.uint8), np.zeros((10, 10), np.uint8))
