@@ -145,7 +145,7 @@ def flops_per_pair(d, hw):
         + 2 * (hg // 2) * (wg // 2) * 768 * 9 * 768 \
         + 2 * 9 * 256 * (h0 * w0 * 96 + (h0 // 2) * (w0 // 2) * 192 + hg * wg * 384 + (hg // 2) * (wg // 2) * 768) \
         + 2 * 9 * (2 * h0) * (2 * w0) * 256 * 128 + 2 * 9 * (4 * h0) * (4 * w0) * 128 * 128 + 2 * (4 * h0) * (4 * w0) * 128 * 4
-    return 2 * enc + dec + 2 * (lf + dpt)
+    return 2 * (enc + dec + lf + dpt)  # per view, two views
 
 
 def cpu_baseline_port(dims, hw, n_pairs=1, budget_s=60.0):
