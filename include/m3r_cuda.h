@@ -159,6 +159,21 @@ int m3r_conv3_test(int device, int dtype, const uint16_t* x, const uint16_t* w, 
 int m3r_match_nn(int device, const float* desc_1, const float* desc_2, int64_t n1, int64_t n2, int desc_dim,
                  int32_t* nn_12, int32_t* nn_21, float* best_12, float* kernel_ms);
 
+/* m3r_match_nn without any device allocation (no counterpart in the reference).
+ * For callers that must not allocate GPU memory while running -- a real-time loop
+ * that cannot absorb the device synchronisation of cudaMalloc / cudaFree, or a host
+ * framework that owns all device memory in its own pool.  Same results as
+ * m3r_match_nn, but desc_* (raw, un-normalised) and nn_12 / nn_21 / best_12 are
+ * DEVICE buffers on `device`, and the work is queued on `stream` (a cudaStream_t,
+ * NULL = default stream) without waiting for it.  Temporaries live in one static
+ * 8.25 MiB device array that every GPU loading the library keeps until exit; limits:
+ * n1, n2 <= 16384 and desc_dim <= 64 (larger sizes return M3R_ERR_ARG).  The first
+ * call on a device looks up the array's address (make it before any stream capture).
+ * All calls share the array: calls that overlap on the GPU race.  best_12 may be NULL.
+ * Errors: m3r_global_error(). */
+int m3r_match_nn_static(int device, const float* desc_1, const float* desc_2, int64_t n1, int64_t n2, int desc_dim,
+                        int32_t* nn_12, int32_t* nn_21, float* best_12, void* stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

@@ -75,6 +75,11 @@ void check_dev_err(int* d_err) {
 
 }  // namespace
 
+namespace m3r {
+// Lets entry points defined outside this file report through m3r_global_error().
+void set_global_error(const std::string& msg) { g_err = msg; }
+}  // namespace m3r
+
 extern "C" {
 
 int m3r_version(void) { return M3R_ABI_VERSION; }
