@@ -37,7 +37,7 @@ struct AttnParams {
 };
 
 template <class T>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, 2)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
                     const __grid_constant__ CUtensorMap mapV, const __grid_constant__ AttnParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -112,31 +112,44 @@ __global__ void __launch_bounds__(192, 1)
         }
     } else if (warp == 5) {
         // ------------------------------------------------------------ MMA issuer
+        // S_{j+1} = Q K_{j+1}^T is issued as soon as the softmax warps have read S_j
+        // into registers, so it overlaps their exponentials; O += P_j V_j follows P_j.
         if (lane == 0) {
             constexpr uint32_t idesc_s = idesc_f16kind<T>(128, 128, false, false);
             constexpr uint32_t idesc_o = idesc_f16kind<T>(128, 64, false, true);
             const uint32_t q_addr = smem_u32(sQ);
-            bool ok = mbar_wait(q_full, 0, abort_flag, kDevTimeoutMma, p.err);
-            for (int j = 0; j < nkv && ok; ++j) {
-                const int st = j & 1;
-                const uint32_t ph = (j >> 1) & 1;
-                if (!mbar_wait(&kv_full[st], ph, abort_flag, kDevTimeoutMma, p.err)) { ok = false; break; }
-                if (j > 0 && !mbar_wait(s_empty, (j - 1) & 1, abort_flag, kDevTimeoutMma, p.err)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t k_addr = smem_u32(sK + st * kTileBytes);
+            auto issue_s = [&](int j) {
+                const uint32_t k_addr = smem_u32(sK + (j & 1) * kTileBytes);
 #pragma unroll
                 for (int k = 0; k < 4; ++k)
                     mma_f16_ss(tmem + kColS, umma_desc_sw128(q_addr + k * 32, 16, 1024),
                                umma_desc_sw128(k_addr + k * 32, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
                 mma_commit(s_full);
+            };
+            bool ok = mbar_wait(q_full, 0, abort_flag, kDevTimeoutMma, p.err) &&
+                      mbar_wait(&kv_full[0], 0, abort_flag, kDevTimeoutMma, p.err);
+            if (ok) {
+                tc_fence_after();
+                issue_s(0);
+            }
+            for (int j = 0; j < nkv && ok; ++j) {
+                if (j + 1 < nkv) {
+                    if (!mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, kDevTimeoutMma, p.err) ||
+                        !mbar_wait(s_empty, j & 1, abort_flag, kDevTimeoutMma, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    issue_s(j + 1);
+                }
                 if (!mbar_wait(p_full, j & 1, abort_flag, kDevTimeoutMma, p.err)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t v_addr = smem_u32(sV + st * kTileBytes);
+                const uint32_t v_addr = smem_u32(sV + (j & 1) * kTileBytes);
 #pragma unroll
                 for (int k = 0; k < 8; ++k)
                     mma_f16_ts(tmem + kColO, tmem + kColP + k * 8, umma_desc_sw128(v_addr + k * 2048, 16384, 1024),
                                idesc_o, (j > 0 || k > 0) ? 1u : 0u);
-                mma_commit(&kv_empty[st]);
+                mma_commit(&kv_empty[j & 1]);
                 mma_commit(o_done);
             }
             mma_commit(mma_done);
@@ -145,72 +158,86 @@ __global__ void __launch_bounds__(192, 1)
         }
     } else {
         // ------------------------------------------------------------ softmax (warps 0-3)
+        // Lazy rescaling: the exponent offset m_use only moves when the row maximum
+        // exceeds it by more than 8 (log2 units), so P <= 2^8 and O is rescaled rarely.
         const int r = warp * 32 + lane;
         const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
         const uint32_t tS = tmem + lane_base + kColS;
         const uint32_t tP = tmem + lane_base + kColP;
         const uint32_t tO = tmem + lane_base + kColO;
-        float m_run = -INFINITY, l_run = 0.0f;
+        const float sl2 = p.scale_log2;
+        float m_use = -INFINITY, l_run = 0.0f;
         bool ok = true;
         for (int j = 0; j < nkv; ++j) {
             if (!mbar_wait(s_full, j & 1, abort_flag, kDevTimeoutSoftmax, p.err)) { ok = false; break; }
             tc_fence_after();
+            uint32_t v[4][32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, v[c]);
+            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(s_empty);  // S is in registers: the next S may overwrite it
             const int valid = p.nk - j * kTile;  // keys valid in this tile (>= 1)
+            const bool full_tile = valid >= kTile;
             float mx = -INFINITY;
+            if (full_tile) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t v[32];
-                tmem_ld32(tS + c * 32, v);
-                tmem_wait_ld();
+                for (int c = 0; c < 4; ++c)
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    if (c * 32 + i < valid) mx = fmaxf(mx, __uint_as_float(v[i]));
+                    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(v[c][i]));
+            } else {
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (c * 32 + i < valid) mx = fmaxf(mx, __uint_as_float(v[c][i]));
             }
-            const float m_new = fmaxf(m_run, mx * p.scale_log2);
-            const float alpha = ex2_approx(m_run - m_new);
+            const float m_cand = mx * sl2;
+            const float m_new = (m_cand > m_use + 8.0f) ? m_cand : m_use;
+            const float alpha = ex2_approx(m_use - m_new);  // 1 when m_use is kept, 0 on the first tile
+            float rowsum = 0.0f;
+            uint32_t pk[4][16];
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int c0 = c * 32 + 2 * i;
+                    float p0 = ex2_approx(__uint_as_float(v[c][2 * i]) * sl2 - m_new);
+                    float p1 = ex2_approx(__uint_as_float(v[c][2 * i + 1]) * sl2 - m_new);
+                    if (!full_tile) {
+                        p0 = c0 < valid ? p0 : 0.0f;
+                        p1 = c0 + 1 < valid ? p1 : 0.0f;
+                    }
+                    rowsum += p0 + p1;
+                    pk[c][i] = Elem<T>::pack(p0, p1);
+                }
             if (j > 0) {
                 // P buffer free and O stable once PV of the previous tile is done
                 if (!mbar_wait(o_done, (j - 1) & 1, abort_flag, kDevTimeoutSoftmax, p.err)) { ok = false; break; }
                 tc_fence_after();
-            }
-            float rowsum = 0.0f;
+                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t v[32];
-                tmem_ld32(tS + c * 32, v);
-                tmem_wait_ld();
-                uint32_t pk[16];
+                    for (int c = 0; c < 2; ++c) {
+                        uint32_t o[32];
+                        tmem_ld32(tO + c * 32, o);
+                        tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int c0 = c * 32 + 2 * i;
-                    const float p0 = c0 < valid ? ex2_approx(__uint_as_float(v[2 * i]) * p.scale_log2 - m_new) : 0.0f;
-                    const float p1 = c0 + 1 < valid ? ex2_approx(__uint_as_float(v[2 * i + 1]) * p.scale_log2 - m_new) : 0.0f;
-                    rowsum += p0 + p1;
-                    pk[i] = Elem<T>::pack(p0, p1);
+                        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                        tmem_st32(tO + c * 32, o);
+                    }
                 }
+            }
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
                 asm volatile(
                     "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
                     "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(tP + c * 16),
-                    "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3]), "r"(pk[4]), "r"(pk[5]), "r"(pk[6]), "r"(pk[7]),
-                    "r"(pk[8]), "r"(pk[9]), "r"(pk[10]), "r"(pk[11]), "r"(pk[12]), "r"(pk[13]), "r"(pk[14]),
-                    "r"(pk[15]));
-            }
-            tc_fence_before();
-            mbar_arrive(s_empty);
-            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-#pragma unroll
-                for (int c = 0; c < 2; ++c) {
-                    uint32_t o[32];
-                    tmem_ld32(tO + c * 32, o);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                    tmem_st32(tO + c * 32, o);
-                }
-            }
+                    "r"(pk[c][0]), "r"(pk[c][1]), "r"(pk[c][2]), "r"(pk[c][3]), "r"(pk[c][4]), "r"(pk[c][5]),
+                    "r"(pk[c][6]), "r"(pk[c][7]), "r"(pk[c][8]), "r"(pk[c][9]), "r"(pk[c][10]), "r"(pk[c][11]),
+                    "r"(pk[c][12]), "r"(pk[c][13]), "r"(pk[c][14]), "r"(pk[c][15]));
             tmem_wait_st();
             l_run = l_run * alpha + rowsum;
-            m_run = m_new;
+            m_use = m_new;
             tc_fence_before();
             mbar_arrive(p_full);
         }

@@ -45,7 +45,7 @@ void launch(cudaStream_t s, const CUtensorMap& a0, const CUtensorMap& a1, const 
     const int tiles = p.tiles_m * p.tiles_n;
     if (tiles == 0) return;
     const int grid = tiles < num_sms() ? tiles : num_sms();
-    kern<<<grid, 192, C::SMEM_BYTES, s>>>(a0, a1, b, p);
+    kern<<<grid, kGemmThreads, C::SMEM_BYTES, s>>>(a0, a1, b, p);
     M3R_CUDA(cudaGetLastError());
 }
 
