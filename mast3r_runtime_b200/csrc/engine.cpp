@@ -23,6 +23,7 @@
 #include "common.cuh"
 #include "gemm.h"
 #include "kernels.h"
+#include "nccl_dl.h"
 #include "safetensors.h"
 
 namespace m3r {
@@ -573,7 +574,12 @@ Engine::Engine(const m3r_config& cfg) : cfg_(cfg), d_(Dims::from(cfg)) {
     }
 }
 
-Engine::~Engine() = default;
+Engine::~Engine() {
+    if (!nccl_comms_.empty()) {
+        const NcclApi& api = nccl();
+        for (void* c : nccl_comms_) api.CommDestroy(static_cast<ncclComm_t>(c));
+    }
+}
 
 void Engine::load(const std::string& path) {
     SafetensorsFile f(path);
@@ -931,32 +937,37 @@ int Engine::match(const float* d1, const float* d2, int hh, int ww, int dd, int 
         if (timing) timing[M3R_T_TOTAL] = 0.0f;
         return 0;
     }
-    // single device (device 0 of the engine)
-    Device& D = *devs_[0];
-    DeviceGuard g(D.dev());
-    cudaStream_t s = D.stream();
-    D.mws.reserve(n, dd);
-    cudaEvent_t e0, e1;
-    M3R_CUDA(cudaEventCreate(&e0));
-    M3R_CUDA(cudaEventCreate(&e1));
-    M3R_CUDA(cudaMemcpyAsync(D.mws.a, d1, sizeof(float) * n * dd, cudaMemcpyHostToDevice, s));
-    M3R_CUDA(cudaMemcpyAsync(D.mws.b, d2, sizeof(float) * n * dd, cudaMemcpyHostToDevice, s));
-    M3R_CUDA(cudaEventRecord(e0, s));
-    match_normalize(s, D.mws.a, D.mws.a, n, dd);
-    match_normalize(s, D.mws.b, D.mws.b, n, dd);
-    match_argmax(s, D.mws.a, D.mws.b, 0, n, n, dd, D.mws.rowkey, D.mws.colkey, true);
-    const int m = match_select(s, D.mws, n, 0, reciprocal, thr, top_k);
-    M3R_CUDA(cudaEventRecord(e1, s));
-    if (m > 0) {
-        M3R_CUDA(cudaMemcpyAsync(idx1, D.mws.idx1, sizeof(int64_t) * m, cudaMemcpyDeviceToHost, s));
-        M3R_CUDA(cudaMemcpyAsync(idx2, D.mws.idx2, sizeof(int64_t) * m, cudaMemcpyDeviceToHost, s));
-        M3R_CUDA(cudaMemcpyAsync(conf, D.mws.conf, sizeof(float) * m, cudaMemcpyDeviceToHost, s));
-    }
-    M3R_CUDA(cudaStreamSynchronize(s));
+    int m = 0;
     float kms = 0;
-    M3R_CUDA(cudaEventElapsedTime(&kms, e0, e1));
-    cudaEventDestroy(e0);
-    cudaEventDestroy(e1);
+    if (devs_.size() > 1 && n >= static_cast<long long>(devs_.size()) * 128) {
+        m = match_multi(d1, d2, n, ww, dd, top_k, reciprocal, thr, idx1, idx2, conf, &kms);
+    } else {
+        // single device (device 0 of the engine)
+        Device& D = *devs_[0];
+        DeviceGuard g(D.dev());
+        cudaStream_t s = D.stream();
+        D.mws.reserve(n, dd);
+        cudaEvent_t e0, e1;
+        M3R_CUDA(cudaEventCreate(&e0));
+        M3R_CUDA(cudaEventCreate(&e1));
+        M3R_CUDA(cudaMemcpyAsync(D.mws.a, d1, sizeof(float) * n * dd, cudaMemcpyHostToDevice, s));
+        M3R_CUDA(cudaMemcpyAsync(D.mws.b, d2, sizeof(float) * n * dd, cudaMemcpyHostToDevice, s));
+        M3R_CUDA(cudaEventRecord(e0, s));
+        match_normalize(s, D.mws.a, D.mws.a, n, dd);
+        match_normalize(s, D.mws.b, D.mws.b, n, dd);
+        match_argmax(s, D.mws.a, D.mws.b, 0, n, n, dd, D.mws.rowkey, D.mws.colkey, true);
+        m = match_select(s, D.mws, n, 0, reciprocal, thr, top_k);
+        M3R_CUDA(cudaEventRecord(e1, s));
+        if (m > 0) {
+            M3R_CUDA(cudaMemcpyAsync(idx1, D.mws.idx1, sizeof(int64_t) * m, cudaMemcpyDeviceToHost, s));
+            M3R_CUDA(cudaMemcpyAsync(idx2, D.mws.idx2, sizeof(int64_t) * m, cudaMemcpyDeviceToHost, s));
+            M3R_CUDA(cudaMemcpyAsync(conf, D.mws.conf, sizeof(float) * m, cudaMemcpyDeviceToHost, s));
+        }
+        M3R_CUDA(cudaStreamSynchronize(s));
+        M3R_CUDA(cudaEventElapsedTime(&kms, e0, e1));
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+    }
     for (int i = 0; i < m; ++i) {  // matching.cpp:216-222
         p1[2 * i] = static_cast<float>(idx1[i] % ww);
         p1[2 * i + 1] = static_cast<float>(idx1[i] / ww);
@@ -970,6 +981,113 @@ int Engine::match(const float* d1, const float* d2, int hh, int ww, int dd, int 
             static_cast<float>(std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count());
     }
     return m;
+}
+
+// Rows of A sharded over the devices; B replicated.  Each device finds exact row
+// maxima for its rows and column maxima over its rows; the column keys (max value,
+// lowest row) are max-reduced over the devices with NCCL (in place, over NVLink), so
+// every device then holds the exact nn_21 and runs the reciprocal test, threshold and
+// top-k on its own rows.  The per-device results (each <= top_k, exact top-k of its
+// rows) are merged on the host: the global top-k is inside their union.
+int Engine::match_multi(const float* d1, const float* d2, long long n, int ww, int dd, int top_k, int reciprocal,
+                        float thr, int64_t* idx1, int64_t* idx2, float* conf, float* kernel_ms) {
+    const int nd = static_cast<int>(devs_.size());
+    const NcclApi& api = nccl();
+    if (nccl_comms_.empty()) {
+        std::vector<ncclComm_t> comms(nd);
+        std::vector<int> ids(nd);
+        for (int i = 0; i < nd; ++i) ids[i] = devs_[i]->dev();
+        nccl_check(api.CommInitAll(comms.data(), nd, ids.data()), "ncclCommInitAll");
+        for (auto c : comms) nccl_comms_.push_back(c);
+    }
+    struct Part {
+        long long r0 = 0, r1 = 0;
+        int m = 0, total = 0;
+        std::vector<int64_t> i1, i2;
+        std::vector<float> c;
+        cudaEvent_t e0 = nullptr, e1 = nullptr;
+    };
+    std::vector<Part> parts(nd);
+    for (int i = 0; i < nd; ++i) {
+        parts[i].r0 = n * i / nd;
+        parts[i].r1 = n * (i + 1) / nd;
+    }
+    // phase 1: copy in, normalise, arg-max over the device's rows
+    for_each_device(devs_.size(), [&](size_t i) {
+        Device& D = *devs_[i];
+        Part& P = parts[i];
+        DeviceGuard g(D.dev());
+        cudaStream_t s = D.stream();
+        const long long nr = P.r1 - P.r0;
+        D.mws.reserve(n, dd);
+        M3R_CUDA(cudaEventCreate(&P.e0));
+        M3R_CUDA(cudaEventCreate(&P.e1));
+        M3R_CUDA(cudaMemcpyAsync(D.mws.a, d1 + P.r0 * dd, sizeof(float) * nr * dd, cudaMemcpyHostToDevice, s));
+        M3R_CUDA(cudaMemcpyAsync(D.mws.b, d2, sizeof(float) * n * dd, cudaMemcpyHostToDevice, s));
+        M3R_CUDA(cudaEventRecord(P.e0, s));
+        match_normalize(s, D.mws.a, D.mws.a, nr, dd);
+        match_normalize(s, D.mws.b, D.mws.b, n, dd);
+        // A is addressed by global row: rows [r0, r1) live at mws.a[0 .. nr)
+        match_argmax(s, D.mws.a - P.r0 * dd, D.mws.b, P.r0, P.r1, n, dd, D.mws.rowkey, D.mws.colkey, true);
+    });
+    // phase 2: column keys max-reduced over the devices
+    nccl_check(api.GroupStart(), "ncclGroupStart");
+    for (int i = 0; i < nd; ++i) {
+        Device& D = *devs_[i];
+        DeviceGuard g(D.dev());
+        nccl_check(api.AllReduce(D.mws.colkey, D.mws.colkey, static_cast<size_t>(n), ncclUint64, ncclMax,
+                                 static_cast<ncclComm_t>(nccl_comms_[i]), D.stream()),
+                   "ncclAllReduce(column keys)");
+    }
+    nccl_check(api.GroupEnd(), "ncclGroupEnd");
+    // phase 3: reciprocal test, threshold and top-k per shard, results to the host
+    for_each_device(devs_.size(), [&](size_t i) {
+        Device& D = *devs_[i];
+        Part& P = parts[i];
+        DeviceGuard g(D.dev());
+        cudaStream_t s = D.stream();
+        P.m = match_select(s, D.mws, P.r1 - P.r0, P.r0, reciprocal, thr, top_k, &P.total);
+        M3R_CUDA(cudaEventRecord(P.e1, s));
+        P.i1.resize(P.m);
+        P.i2.resize(P.m);
+        P.c.resize(P.m);
+        if (P.m > 0) {
+            M3R_CUDA(cudaMemcpyAsync(P.i1.data(), D.mws.idx1, sizeof(int64_t) * P.m, cudaMemcpyDeviceToHost, s));
+            M3R_CUDA(cudaMemcpyAsync(P.i2.data(), D.mws.idx2, sizeof(int64_t) * P.m, cudaMemcpyDeviceToHost, s));
+            M3R_CUDA(cudaMemcpyAsync(P.c.data(), D.mws.conf, sizeof(float) * P.m, cudaMemcpyDeviceToHost, s));
+        }
+        M3R_CUDA(cudaStreamSynchronize(s));
+    });
+    float kms = 0;
+    long long total = 0;
+    for (int i = 0; i < nd; ++i) {
+        float t = 0;
+        M3R_CUDA(cudaSetDevice(devs_[i]->dev()));
+        M3R_CUDA(cudaEventElapsedTime(&t, parts[i].e0, parts[i].e1));
+        kms = std::max(kms, t);
+        cudaEventDestroy(parts[i].e0);
+        cudaEventDestroy(parts[i].e1);
+        total += parts[i].total;
+    }
+    if (kernel_ms) *kernel_ms = kms;
+    // merge: all candidates in row order when they fit, else the top_k by (conf desc, idx_1 asc)
+    struct C3 {
+        float c;
+        int64_t i, j;
+    };
+    std::vector<C3> all;
+    for (const Part& P : parts)
+        for (int k = 0; k < P.m; ++k) all.push_back({P.c[k], P.i1[k], P.i2[k]});
+    if (total > top_k) {
+        std::sort(all.begin(), all.end(), [](const C3& a, const C3& b) { return a.c > b.c || (a.c == b.c && a.i < b.i); });
+        all.resize(static_cast<size_t>(top_k));
+    }
+    for (size_t k = 0; k < all.size(); ++k) {
+        idx1[k] = all[k].i;
+        idx2[k] = all[k].j;
+        conf[k] = all[k].c;
+    }
+    return static_cast<int>(all.size());
 }
 
 }  // namespace m3r

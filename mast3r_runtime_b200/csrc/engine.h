@@ -74,9 +74,13 @@ public:
 
 private:
     std::vector<std::pair<int, int>> shards(int n_pairs) const;  // (first pair, count) per device
+    // rows of desc_1 sharded over the devices; column keys max-reduced with NCCL
+    int match_multi(const float* d1, const float* d2, long long n, int ww, int dd, int top_k, int reciprocal,
+                    float thr, int64_t* idx1, int64_t* idx2, float* conf, float* kernel_ms);
     m3r_config cfg_;
     Dims d_;
     std::vector<std::unique_ptr<Device>> devs_;
+    std::vector<void*> nccl_comms_;  // ncclComm_t per device, created on the first multi-device match
     bool ready_ = false;
     bool profiling_ = false;
     int staged_pairs_ = 0;

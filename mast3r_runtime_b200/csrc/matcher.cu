@@ -486,7 +486,8 @@ void match_argmax(cudaStream_t s, const float* a_norm, const float* b_norm, long
 }
 
 int match_select(cudaStream_t s, MatchWorkspace& ws, long long nrows, long long row0, int reciprocal, float thr,
-                 int top_k) {
+                 int top_k, int* total_out) {
+    if (total_out) *total_out = 0;
     if (nrows <= 0) return 0;
     const int nblk = static_cast<int>((nrows + kCandBlock - 1) / kCandBlock);
     int* total_d = ws.misc;
@@ -498,6 +499,7 @@ int match_select(cudaStream_t s, MatchWorkspace& ws, long long nrows, long long 
     int total = 0;
     M3R_CUDA(cudaMemcpyAsync(&total, total_d, sizeof(int), cudaMemcpyDeviceToHost, s));
     M3R_CUDA(cudaStreamSynchronize(s));
+    if (total_out) *total_out = total;
     int m = total;
     if (total > top_k) {
         M3R_REQUIRE(top_k <= 4096, "match: top_k must be <= 4096");

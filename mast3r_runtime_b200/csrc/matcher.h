@@ -40,9 +40,10 @@ void match_argmax(cudaStream_t s, const float* a_norm, const float* b_norm, long
                   long long n2, int d, unsigned long long* rowkey, unsigned long long* colkey, bool clear_colkey);
 
 // Reciprocal / threshold / top-k over rows [row0, row0 + nrows) with keys in ws;
-// results in ws.idx1 / ws.idx2 / ws.conf.  Returns the match count.
+// results in ws.idx1 / ws.idx2 / ws.conf.  Returns the match count (<= top_k);
+// *total_out (optional) gets the number of candidates before the top-k cut.
 int match_select(cudaStream_t s, MatchWorkspace& ws, long long nrows, long long row0, int reciprocal, float thr,
-                 int top_k);
+                 int top_k, int* total_out = nullptr);
 
 // Index part of keys -> int32 (nn_12 / nn_21 for tests).
 void match_decode(cudaStream_t s, const unsigned long long* keys, long long n, int32_t* idx);
