@@ -145,14 +145,15 @@ void m3r_host_free(void* p);
 int m3r_attention_fwd(int device, int dtype, const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out,
                       int n_seq, int heads, int nq, int nk, float scale, int iters, float* kernel_ms);
 
-/* GEMM C[M, N] = A[M, K] * W[N, K]^T + bias (16-bit in, fp32 out). */
+/* GEMM C[M, N] = A[M, K] * W[N, K]^T + bias (16-bit in, fp32 out).  cta_pair: 0 = one
+ * CTA per 128-row tile, 1 = CTA pairs (256-row tiles), -1 = chosen from the size. */
 int m3r_gemm_test(int device, int dtype, const uint16_t* a, const uint16_t* w, const float* bias, float* c, int M,
-                  int N, int K, int bn, int iters, float* kernel_ms);
+                  int N, int K, int bn, int cta_pair, int iters, float* kernel_ms);
 
 /* 3x3 conv, stride 1, pad 1, NHWC: x [n, h, w, c], w [cout, 9 * cpad] (tap-major,
  * channel padded to cpad = ceil(c / 64) * 64) -> y [n, h, w, cout] fp32 (bias added). */
 int m3r_conv3_test(int device, int dtype, const uint16_t* x, const uint16_t* w, const float* bias, float* y, int n,
-                   int h, int wd, int c, int cout, int bn);
+                   int h, int wd, int c, int cout, int bn, int cta_pair);
 
 /* Matcher arg-max only: nn_12 [n1] and nn_21 [n2] (lowest index on ties) of the
  * normalised descriptors, and the row maxima best_12 [n1]. */

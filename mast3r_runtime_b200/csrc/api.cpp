@@ -250,7 +250,7 @@ int m3r_attention_fwd(int device, int dtype, const uint16_t* q, const uint16_t* 
 }
 
 int m3r_gemm_test(int device, int dtype, const uint16_t* a, const uint16_t* w, const float* bias, float* c, int M,
-                  int N, int K, int bn, int iters, float* kernel_ms) {
+                  int N, int K, int bn, int cta_pair, int iters, float* kernel_ms) {
     return guarded(nullptr, [&] {
         M3R_REQUIRE(a && w && c && M > 0 && N > 0 && K > 0 && K % 8 == 0 && N % 4 == 0, "gemm_test: bad arguments");
         m3r::DeviceGuard g(device);
@@ -267,9 +267,9 @@ int m3r_gemm_test(int device, int dtype, const uint16_t* a, const uint16_t* w, c
         p.err = derr.as<int>();
         const int it = iters < 1 ? 1 : iters;
         Events ev;
-        m3r::gemm_rows(nullptr, dtype, bn, m3r::EPI_F32, da.p, K, M, K, dw.p, K, N, p);
+        m3r::gemm_rows(nullptr, dtype, bn, m3r::EPI_F32, da.p, K, M, K, dw.p, K, N, p, cta_pair);
         M3R_CUDA(cudaEventRecord(ev.a, nullptr));
-        for (int i = 0; i < it; ++i) m3r::gemm_rows(nullptr, dtype, bn, m3r::EPI_F32, da.p, K, M, K, dw.p, K, N, p);
+        for (int i = 0; i < it; ++i) m3r::gemm_rows(nullptr, dtype, bn, m3r::EPI_F32, da.p, K, M, K, dw.p, K, N, p, cta_pair);
         M3R_CUDA(cudaEventRecord(ev.b, nullptr));
         M3R_CUDA(cudaDeviceSynchronize());
         check_dev_err(derr.as<int>());
@@ -279,7 +279,7 @@ int m3r_gemm_test(int device, int dtype, const uint16_t* a, const uint16_t* w, c
 }
 
 int m3r_conv3_test(int device, int dtype, const uint16_t* x, const uint16_t* w, const float* bias, float* y, int n,
-                   int h, int wd, int c, int cout, int bn) {
+                   int h, int wd, int c, int cout, int bn, int cta_pair) {
     return guarded(nullptr, [&] {
         M3R_REQUIRE(x && w && y && n > 0 && h > 0 && wd > 0 && c > 0 && c % 8 == 0 && cout > 0 && cout % 4 == 0,
                     "conv3_test: bad arguments");
@@ -297,7 +297,7 @@ int m3r_conv3_test(int device, int dtype, const uint16_t* x, const uint16_t* w, 
         p.out = dy.p;
         p.ldo = cout;
         p.err = derr.as<int>();
-        m3r::gemm_conv3(nullptr, dtype, bn, m3r::EPI_F32, dx.p, n, h, wd, c, c, dw.p, cout, p);
+        m3r::gemm_conv3(nullptr, dtype, bn, m3r::EPI_F32, dx.p, n, h, wd, c, c, dw.p, cout, p, cta_pair);
         M3R_CUDA(cudaDeviceSynchronize());
         check_dev_err(derr.as<int>());
         M3R_CUDA(cudaMemcpy(y, dy.p, yn * 4, cudaMemcpyDeviceToHost));

@@ -25,11 +25,11 @@ GemmParams gemm_params() {
 
 namespace {
 
-template <class T, int BN, int AMODE, int EPI>
+template <class T, int BN, int AMODE, int EPI, int CG>
 void launch(cudaStream_t s, const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b,
             const GemmParams& p) {
-    using C = GemmCfg<BN>;
-    auto kern = gemm_tc_kernel<T, BN, AMODE, EPI>;
+    using C = GemmCfg<BN, CG>;
+    auto kern = gemm_tc_kernel<T, BN, AMODE, EPI, CG>;
     static std::once_flag once;  // per instantiation; the attribute is set on every device
     std::call_once(once, [&] {
         int ndev = 0;
@@ -42,21 +42,36 @@ void launch(cudaStream_t s, const CUtensorMap& a0, const CUtensorMap& a1, const 
         }
         M3R_CUDA(cudaSetDevice(cur));
     });
-    const int tiles = p.tiles_m * p.tiles_n;
-    if (tiles == 0) return;
-    const int grid = tiles < num_sms() ? tiles : num_sms();
-    kern<<<grid, kGemmThreads, C::SMEM_BYTES, s>>>(a0, a1, b, p);
-    M3R_CUDA(cudaGetLastError());
+    const int units = ((p.tiles_m + CG - 1) / CG) * p.tiles_n;  // tiles of CG x 128 rows
+    if (units == 0) return;
+    const int max_units = num_sms() / CG;
+    const int grid = CG * (units < max_units ? units : max_units);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = C::SMEM_BYTES;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CG;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    M3R_CUDA(cudaLaunchKernelEx(&cfg, kern, a0, a1, b, p));
 }
 
-#define M3R_GEMM_CASE(BN_, AM_, EPI_)                   \
-    if (bn == BN_ && amode == AM_ && epi == EPI_) {     \
-        launch<T, BN_, AM_, EPI_>(s, a0, a1, b, p);     \
-        return;                                         \
+#define M3R_GEMM_CASE(BN_, AM_, EPI_)                                \
+    if (bn == BN_ && amode == AM_ && epi == EPI_) {                  \
+        if (cg == 2)                                                 \
+            launch<T, BN_, AM_, EPI_, 2>(s, a0, a1, b, p);           \
+        else                                                         \
+            launch<T, BN_, AM_, EPI_, 1>(s, a0, a1, b, p);           \
+        return;                                                      \
     }
 
 template <class T>
-void dispatch_t(cudaStream_t s, int bn, int amode, int epi, const CUtensorMap& a0, const CUtensorMap& a1,
+void dispatch_t(cudaStream_t s, int bn, int amode, int epi, int cg, const CUtensorMap& a0, const CUtensorMap& a1,
                 const CUtensorMap& b, const GemmParams& p) {
     M3R_GEMM_CASE(256, A_PLAIN, EPI_BF16)
     M3R_GEMM_CASE(128, A_PLAIN, EPI_BF16)
@@ -79,60 +94,69 @@ void dispatch_t(cudaStream_t s, int bn, int amode, int epi, const CUtensorMap& a
                              " epi=" + std::to_string(epi));
 }
 
-void dispatch(cudaStream_t s, int dt, int bn, int amode, int epi, const CUtensorMap& a0, const CUtensorMap& a1,
-              const CUtensorMap& b, const GemmParams& p) {
+void dispatch(cudaStream_t s, int dt, int bn, int amode, int epi, int cg, const CUtensorMap& a0,
+              const CUtensorMap& a1, const CUtensorMap& b, const GemmParams& p) {
     if (dt == DT_F16)
-        dispatch_t<__half>(s, bn, amode, epi, a0, a1, b, p);
+        dispatch_t<__half>(s, bn, amode, epi, cg, a0, a1, b, p);
     else if (dt == DT_BF16)
-        dispatch_t<__nv_bfloat16>(s, bn, amode, epi, a0, a1, b, p);
+        dispatch_t<__nv_bfloat16>(s, bn, amode, epi, cg, a0, a1, b, p);
     else
         throw Error(kErrArg, "unknown operand type " + std::to_string(dt));
 }
 
 int cdiv(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
 
+// CTAs per tile.  A CTA pair stages half as much B per CTA (more pipeline stages,
+// half the B traffic per SM) and launches as many CTAs as single-CTA tiles would,
+// so it is used whenever there are row blocks to pair.
+int pick_cg(int cta_pair, int tiles_m) {
+    if (cta_pair == 0) return 1;
+    if (cta_pair == 1) return 2;
+    return tiles_m >= 2 ? 2 : 1;
+}
+
 }  // namespace
 
 void gemm_rows(cudaStream_t s, int dt, int bn, int epi, const void* A, long long lda, int M, int K, const void* W,
-               long long ldw, int N, GemmParams p) {
+               long long ldw, int N, GemmParams p, int cta_pair) {
     M3R_REQUIRE(M >= 0 && N > 0 && K > 0, "gemm: bad shape");
     if (M == 0) return;
-    const CUtensorMap a = tmap_2d(dt, A, M, K, lda, 128);
-    const CUtensorMap b = tmap_2d(dt, W, N, K, ldw, bn);
     p.M = M;
     p.N = N;
     p.num_kb = cdiv(K, 64);
     p.tiles_m = cdiv(M, 128);
     p.tiles_n = cdiv(N, bn);
-    dispatch(s, dt, bn, A_PLAIN, epi, a, a, b, p);
+    const int cg = pick_cg(cta_pair, p.tiles_m);
+    const CUtensorMap a = tmap_2d(dt, A, M, K, lda, 128);
+    const CUtensorMap b = tmap_2d(dt, W, N, K, ldw, bn / cg);
+    dispatch(s, dt, bn, A_PLAIN, epi, cg, a, a, b, p);
 }
 
 void gemm_concat(cudaStream_t s, int dt, int bn, int epi, const void* A0, long long lda0, int K0, const void* A1,
-                 long long lda1, int K1, int M, const void* W, long long ldw, int N, GemmParams p) {
+                 long long lda1, int K1, int M, const void* W, long long ldw, int N, GemmParams p, int cta_pair) {
     M3R_REQUIRE(K0 % 64 == 0, "gemm_concat: K0 must be a multiple of 64");
     if (M == 0) return;
-    const CUtensorMap a0 = tmap_2d(dt, A0, M, K0, lda0, 128);
-    const CUtensorMap a1 = tmap_2d(dt, A1, M, K1, lda1, 128);
-    const CUtensorMap b = tmap_2d(dt, W, N, K0 + K1, ldw, bn);
     p.M = M;
     p.N = N;
     p.a_split_kb = K0 / 64;
     p.num_kb = K0 / 64 + cdiv(K1, 64);
     p.tiles_m = cdiv(M, 128);
     p.tiles_n = cdiv(N, bn);
-    dispatch(s, dt, bn, A_CONCAT, epi, a0, a1, b, p);
+    const int cg = pick_cg(cta_pair, p.tiles_m);
+    const CUtensorMap a0 = tmap_2d(dt, A0, M, K0, lda0, 128);
+    const CUtensorMap a1 = tmap_2d(dt, A1, M, K1, lda1, 128);
+    const CUtensorMap b = tmap_2d(dt, W, N, K0 + K1, ldw, bn / cg);
+    dispatch(s, dt, bn, A_CONCAT, epi, cg, a0, a1, b, p);
 }
 
 void gemm_conv3(cudaStream_t s, int dt, int bn, int epi, const void* X, int n, int h, int w, int c, int cstride,
-                const void* W, int N, GemmParams p) {
+                const void* W, int N, GemmParams p, int cta_pair) {
     M3R_REQUIRE(n > 0 && h > 0 && w > 0 && c > 0 && cstride >= c, "gemm_conv3: bad shape");
     int wbox = 1;
     while (wbox * 2 <= 128 && w % (wbox * 2) == 0) wbox *= 2;
     const int hbox = 128 / wbox;
     M3R_REQUIRE(hbox <= 256, "gemm_conv3: box too tall");
     const int cblocks = cdiv(c, 64);
-    const CUtensorMap a = tmap_nhwc(dt, X, n, h, w, c, cstride, hbox, wbox);
-    const CUtensorMap b = tmap_2d(dt, W, N, 9LL * cblocks * 64, 9LL * cblocks * 64, bn);
     p.M = n * h * w;
     p.N = N;
     p.cv_H = h;
@@ -145,7 +169,10 @@ void gemm_conv3(cudaStream_t s, int dt, int bn, int epi, const void* X, int n, i
     p.num_kb = 9 * cblocks;
     p.tiles_m = n * p.cv_tx * p.cv_ty;
     p.tiles_n = cdiv(N, bn);
-    dispatch(s, dt, bn, A_CONV3, epi, a, a, b, p);
+    const int cg = pick_cg(cta_pair, p.tiles_m);
+    const CUtensorMap a = tmap_nhwc(dt, X, n, h, w, c, cstride, hbox, wbox);
+    const CUtensorMap b = tmap_2d(dt, W, N, 9LL * cblocks * 64, 9LL * cblocks * 64, bn / cg);
+    dispatch(s, dt, bn, A_CONV3, epi, cg, a, a, b, p);
 }
 
 }  // namespace m3r

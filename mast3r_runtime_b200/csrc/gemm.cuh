@@ -74,30 +74,45 @@ constexpr int kGemmThreads = (kGemmEpiWarps + 2) * 32;
 constexpr int kGemmTmaWarp = kGemmEpiWarps;
 constexpr int kGemmMmaWarp = kGemmEpiWarps + 1;
 
-template <int BN>
+// CG = CTAs per tile: 1, or 2 for a CTA pair (cluster of 2) running M = 256 MMAs,
+// in which each CTA stages its own 128 rows of A and half of the tile's BN rows
+// of B, and holds its 128 x BN accumulator rows in its own TMEM.
+template <int BN, int CG>
 struct GemmCfg {
     static constexpr int BM = 128;
     static constexpr int BK = 64;
+    static constexpr int B_ROWS = BN / CG;  // rows of B staged by each CTA
     static constexpr int A_BYTES = BM * BK * 2;
-    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int B_BYTES = B_ROWS * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES = (200 * 1024 / STAGE_BYTES) > 8 ? 8 : (200 * 1024 / STAGE_BYTES);
+    // per-epilogue-warp row staging, 4 KB each (EPI_HEAD4 keeps its partial sums there)
+    static constexpr int EPI_STAGE_BYTES = kGemmEpiWarps * 4096;
+    // stages | epilogue staging | barriers, TMEM slot, abort flag (256 B); + 1 KB alignment slack
+    static constexpr int FIXED_BYTES = 1024 + EPI_STAGE_BYTES + 256;
+    static constexpr int MAX_SMEM = 227 * 1024;  // per-block opt-in limit of sm_100
+    static constexpr int STAGES =
+        ((MAX_SMEM - FIXED_BYTES) / STAGE_BYTES) > 8 ? 8 : ((MAX_SMEM - FIXED_BYTES) / STAGE_BYTES);
     static constexpr int ACC_COLS = BN <= 128 ? 128 : 256;   // per accumulator buffer
     static constexpr int TMEM_COLS = 2 * ACC_COLS;
-    // stages | barriers, TMEM slot, abort flag (256 B) | EPI_HEAD4 partial sums [128][4] fp32
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 + 128 * 4 * 4;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + FIXED_BYTES;
+    static_assert(STAGES >= 3 && SMEM_BYTES <= MAX_SMEM, "shared memory budget");
+    static_assert(BN % (8 * CG) == 0 && B_BYTES % 1024 == 0, "B half-tiles must be whole swizzle atoms");
 };
 
 struct TileGeom {
     int m_idx, n_idx;
+    bool live;        // the 128-row block exists (a CTA pair's odd block may lie past the last one)
     int img, y0, x0;  // A_CONV3 only
 };
 
-template <int AMODE>
-__device__ __forceinline__ TileGeom tile_geom(const GemmParams& p, int t) {
+// Tile t of the persistent loop (N-fastest); a CTA pair covers row blocks 2 m + rank.
+template <int AMODE, int CG>
+__device__ __forceinline__ TileGeom tile_geom(const GemmParams& p, int t, int rank) {
     TileGeom g;
-    g.m_idx = t / p.tiles_n;
-    g.n_idx = t - g.m_idx * p.tiles_n;
+    const int mp = t / p.tiles_n;
+    g.n_idx = t - mp * p.tiles_n;
+    g.m_idx = mp * CG + rank;
+    g.live = g.m_idx < p.tiles_m;
     g.img = g.y0 = g.x0 = 0;
     if (AMODE == A_CONV3) {
         const int per_img = p.cv_tx * p.cv_ty;
@@ -156,6 +171,87 @@ __device__ __forceinline__ void add_bias32(float (&v)[32], const float* bias, in
     }
 }
 
+// 64 values (lo = columns 0-31, hi = 32-63) -> 128 bytes of the 16-bit type T
+template <class T>
+__device__ __forceinline__ void pack16x64(uint4 (&u)[8], const float (&lo)[32], const float (&hi)[32]) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const float* v = q < 4 ? lo + 8 * q : hi + 8 * (q - 4);
+        u[q].x = Elem<T>::pack(v[0], v[1]);
+        u[q].y = Elem<T>::pack(v[2], v[3]);
+        u[q].z = Elem<T>::pack(v[4], v[5]);
+        u[q].w = Elem<T>::pack(v[6], v[7]);
+    }
+}
+
+// Per-warp staging of a 32-row x 128-byte block in shared memory, so that global
+// memory sees whole 128-byte lines.  Each thread owns one row (its TMEM lane); the
+// 16-byte chunks of row r sit at chunk position c ^ (r % 8), which makes both
+// row-per-thread accesses and row-contiguous accesses (8 threads per row, 4 rows
+// per instruction) free of bank conflicts.
+struct RowStage {
+    uint8_t* buf;  // 4 KB of this warp
+    int lane;
+    __device__ __forceinline__ uint4* at(int row, int c) const {
+        return reinterpret_cast<uint4*>(buf + row * 128 + ((c ^ (row & 7)) << 4));
+    }
+    __device__ __forceinline__ void put_own(const uint4 (&v)[8]) const {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) *at(lane, c) = v[c];
+    }
+    __device__ __forceinline__ void get_own(uint4 (&v)[8]) const {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) v[c] = *at(lane, c);
+    }
+    // Row-contiguous global loads of the 32 rows (src = each thread's own row pointer,
+    // null = row absent -> zeros; `bytes` = valid bytes per row, a multiple of 4).
+    __device__ __forceinline__ void fetch(const char* src, int bytes, uint4 (&r)[8]) const {
+        const int c = lane & 7;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int row = i * 4 + (lane >> 3);
+            const char* s = reinterpret_cast<const char*>(
+                __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(src), row));
+            r[i] = make_uint4(0u, 0u, 0u, 0u);
+            if (s != nullptr) {
+                if ((c + 1) * 16 <= bytes) {
+                    r[i] = *reinterpret_cast<const uint4*>(s + c * 16);
+                } else if (c * 16 < bytes) {
+                    uint32_t w[4] = {0u, 0u, 0u, 0u};
+                    for (int b = 0; b < 4 && c * 16 + 4 * b < bytes; ++b)
+                        w[b] = *reinterpret_cast<const uint32_t*>(s + c * 16 + 4 * b);
+                    r[i] = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            }
+        }
+    }
+    __device__ __forceinline__ void deposit(const uint4 (&r)[8]) const {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) *at(i * 4 + (lane >> 3), lane & 7) = r[i];
+    }
+    // Row-contiguous global stores of the staged rows (dst = each thread's own row
+    // pointer, null = skip; `bytes` = valid bytes per row, a multiple of 2).
+    __device__ __forceinline__ void store(char* dst, int bytes) const {
+        const int c = lane & 7;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int row = i * 4 + (lane >> 3);
+            char* d = reinterpret_cast<char*>(__shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(dst), row));
+            const uint4 v = *at(row, c);
+            if (d != nullptr) {
+                if ((c + 1) * 16 <= bytes) {
+                    *reinterpret_cast<uint4*>(d + c * 16) = v;
+                } else if (c * 16 < bytes) {
+                    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                    for (int b = 0; b < 8 && c * 16 + 2 * b < bytes; ++b)
+                        *reinterpret_cast<uint16_t*>(d + c * 16 + 2 * b) =
+                            static_cast<uint16_t>(w[b >> 1] >> ((b & 1) * 16));
+                }
+            }
+        }
+    }
+};
+
 // Epilogue of one tile for one column group (grp 0 / 1) of the rows of this thread
 // (tile row r).  All lanes of a warp execute every tcgen05.ld (they are .sync.aligned).
 // EPI_HEAD4 hand-off between the two column groups: partial sums in smem, guarded by
@@ -168,12 +264,9 @@ struct Head4Sync {
     uint32_t tile;     // this CTA's tile counter (phase parity)
 };
 
-template <class T, int BN, int AMODE, int EPI>
-__device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeom& g, uint32_t tacc, int r, int grp,
-                                              const Head4Sync& h4) {
-    // tile row r -> global output row
-    long long grow;
-    bool valid;
+// Tile row r -> global output row (grow) and whether it exists.
+template <int AMODE>
+__device__ __forceinline__ void tile_row(const GemmParams& p, const TileGeom& g, int r, long long& grow, bool& valid) {
     if (AMODE == A_CONV3) {
         const int y = g.y0 + r / p.cv_wbox;
         const int x = g.x0 + r % p.cv_wbox;
@@ -183,91 +276,140 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
         grow = static_cast<long long>(g.m_idx) * 128 + r;
         valid = grow < p.M;
     }
+}
+
+// EPI_F32_RESID: row-contiguous fetch of the residual block of the unit at tile
+// column c0 (32 fp32 columns) into registers; issued one unit ahead of its use.
+template <int BN>
+__device__ __forceinline__ void fetch_resid(const GemmParams& p, const RowStage& st, long long grow, bool valid,
+                                            int col0, uint4 (&r)[8]) {
+    const int bytes = (col0 + 32 <= p.N ? 32 : p.N - col0) * 4;
+    st.fetch(valid && col0 < p.N ? reinterpret_cast<const char*>(p.resid + grow * p.ldr + col0) : nullptr, bytes, r);
+}
+
+template <class T, int BN, int AMODE, int EPI>
+__device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeom& g, uint32_t tacc, int r, int grp,
+                                              const Head4Sync& h4, const RowStage& st, uint4 (&pre)[8]) {
+    long long grow;
+    bool valid;
+    tile_row<AMODE>(p, g, r, grow, valid);
     const int n0 = g.n_idx * BN;
 
-    if constexpr (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_F32_RESID || EPI == EPI_CONVT) {
+    if constexpr (EPI == EPI_F32 || EPI == EPI_F32_RESID) {
+        // units of 32 fp32 columns = 128 bytes per row, staged and stored row-contiguously
 #pragma unroll 1
         for (int c0 = grp * 32; c0 < BN; c0 += 64) {
             const int col0 = n0 + c0;
+            if (col0 >= p.N) break;  // warp-uniform
             const bool full = col0 + 32 <= p.N;
-            float v[32];
-            // residual rows do not depend on the accumulator: fetch them before the TMEM read
+            uint4 cur[8];
             if constexpr (EPI == EPI_F32_RESID) {
-                if (valid && full) {
-                    const float4* src = reinterpret_cast<const float4*>(p.resid + grow * p.ldr + col0);
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        const float4 rr = src[q];
-                        v[4 * q] = rr.x;
-                        v[4 * q + 1] = rr.y;
-                        v[4 * q + 2] = rr.z;
-                        v[4 * q + 3] = rr.w;
-                    }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = 0.0f;
-                    if (valid)
-                        for (int i = 0; i < 32 && col0 + i < p.N; ++i) v[i] = p.resid[grow * p.ldr + col0 + i];
-                }
+                for (int i = 0; i < 8; ++i) cur[i] = pre[i];
+                if (c0 + 64 < BN) fetch_resid<BN>(p, st, grow, valid, col0 + 64, pre);
             }
             uint32_t raw[32];
             tmem_ld32(tacc + c0, raw);
             tmem_wait_ld();
-            if (!valid || col0 >= p.N) continue;
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[i]);
+            __syncwarp();  // the previous unit's row-contiguous reads of the stage are done
             if constexpr (EPI == EPI_F32_RESID) {
+                st.deposit(cur);
+                __syncwarp();
+                uint4 rr[8];
+                st.get_own(rr);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] += __uint_as_float(raw[i]);
-            } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[i]);
-            }
-            if constexpr (EPI == EPI_CONVT) {
-                // column = (dy * s + dx) * cout + co, cout % 32 == 0: one bias window
-                const int q = col0 / p.ct_cout;
-                const int co = col0 - q * p.ct_cout;
-                add_bias32(v, p.bias, co, p.ct_cout, true);
-                const int dy = q / p.ct_s, dx = q - (q / p.ct_s) * p.ct_s;
-                const int per_img = p.ct_h * p.ct_w;
-                const int img = static_cast<int>(grow / per_img);
-                const int rem = static_cast<int>(grow - static_cast<long long>(img) * per_img);
-                const int yy = rem / p.ct_w, xx = rem - (rem / p.ct_w) * p.ct_w;
-                const int OH = p.ct_h * p.ct_s, OW = p.ct_w * p.ct_s;
-                const long long opix = (static_cast<long long>(img) * OH + (yy * p.ct_s + dy)) * OW + (xx * p.ct_s + dx);
-                store16x32<T>(reinterpret_cast<T*>(p.out) + opix * p.ldo + co, v);
-            } else {
-                add_bias32(v, p.bias, col0, p.N, full);
-                if constexpr (EPI == EPI_BF16) {
-                    if (p.act == ACT_GELU) {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) v[i] = gelu_fast(v[i]);
-                    } else if (p.act == ACT_RELU) {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.0f);
-                    }
-                    T* dst = reinterpret_cast<T*>(p.out) + grow * p.ldo + col0;
-                    if (full) {
-                        store16x32<T>(dst, v);
-                    } else {
-                        for (int i = 0; i < 32 && col0 + i < p.N; ++i) dst[i] = Elem<T>::from(v[i]);
-                    }
-                } else {
-                    float* dst = reinterpret_cast<float*>(p.out) + grow * p.ldo + col0;
-                    if (full) {
-#pragma unroll
-                        for (int q = 0; q < 8; ++q)
-                            *reinterpret_cast<float4*>(dst + 4 * q) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-                    } else {
-                        for (int i = 0; i < 32 && col0 + i < p.N; ++i) dst[i] = v[i];
-                    }
+                for (int q = 0; q < 8; ++q) {
+                    v[4 * q] += __uint_as_float(rr[q].x);
+                    v[4 * q + 1] += __uint_as_float(rr[q].y);
+                    v[4 * q + 2] += __uint_as_float(rr[q].z);
+                    v[4 * q + 3] += __uint_as_float(rr[q].w);
                 }
             }
+            add_bias32(v, p.bias, col0, p.N, full);
+            uint4 o[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                o[q] = make_uint4(__float_as_uint(v[4 * q]), __float_as_uint(v[4 * q + 1]), __float_as_uint(v[4 * q + 2]),
+                                  __float_as_uint(v[4 * q + 3]));
+            st.put_own(o);
+            __syncwarp();
+            st.store(valid ? reinterpret_cast<char*>(reinterpret_cast<float*>(p.out) + grow * p.ldo + col0) : nullptr,
+                     (full ? 32 : p.N - col0) * 4);
+        }
+    } else if constexpr (EPI == EPI_BF16) {
+        // units of 64 16-bit columns = 128 bytes per row, staged and stored row-contiguously
+#pragma unroll 1
+        for (int c0 = grp * 64; c0 < BN; c0 += 128) {
+            const int col0 = n0 + c0;
+            if (col0 >= p.N) break;  // warp-uniform
+            uint32_t ra[32], rb[32];
+            tmem_ld32(tacc + c0, ra);
+            tmem_ld32(tacc + c0 + 32, rb);
+            tmem_wait_ld();
+            float lo[32], hi[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                lo[i] = __uint_as_float(ra[i]);
+                hi[i] = __uint_as_float(rb[i]);
+            }
+            add_bias32(lo, p.bias, col0, p.N, col0 + 32 <= p.N);
+            add_bias32(hi, p.bias, col0 + 32, p.N, col0 + 64 <= p.N);
+            if (p.act == ACT_GELU) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    lo[i] = gelu_fast(lo[i]);
+                    hi[i] = gelu_fast(hi[i]);
+                }
+            } else if (p.act == ACT_RELU) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    lo[i] = fmaxf(lo[i], 0.0f);
+                    hi[i] = fmaxf(hi[i], 0.0f);
+                }
+            }
+            uint4 o[8];
+            pack16x64<T>(o, lo, hi);
+            __syncwarp();
+            st.put_own(o);
+            __syncwarp();
+            st.store(valid ? reinterpret_cast<char*>(reinterpret_cast<T*>(p.out) + grow * p.ldo + col0) : nullptr,
+                     (col0 + 64 <= p.N ? 64 : p.N - col0) * 2);
+        }
+    } else if constexpr (EPI == EPI_CONVT) {
+#pragma unroll 1
+        for (int c0 = grp * 32; c0 < BN; c0 += 64) {
+            const int col0 = n0 + c0;
+            uint32_t raw[32];
+            tmem_ld32(tacc + c0, raw);
+            tmem_wait_ld();
+            if (!valid || col0 >= p.N) continue;
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[i]);
+            // column = (dy * s + dx) * cout + co, cout % 32 == 0: one bias window
+            const int q = col0 / p.ct_cout;
+            const int co = col0 - q * p.ct_cout;
+            add_bias32(v, p.bias, co, p.ct_cout, true);
+            const int dy = q / p.ct_s, dx = q - (q / p.ct_s) * p.ct_s;
+            const int per_img = p.ct_h * p.ct_w;
+            const int img = static_cast<int>(grow / per_img);
+            const int rem = static_cast<int>(grow - static_cast<long long>(img) * per_img);
+            const int yy = rem / p.ct_w, xx = rem - (rem / p.ct_w) * p.ct_w;
+            const int OH = p.ct_h * p.ct_s, OW = p.ct_w * p.ct_s;
+            const long long opix = (static_cast<long long>(img) * OH + (yy * p.ct_s + dy)) * OW + (xx * p.ct_s + dx);
+            store16x32<T>(reinterpret_cast<T*>(p.out) + opix * p.ldo + co, v);
         }
     } else if constexpr (EPI == EPI_HEADS) {
-        // The tile lies inside one section (sec_len % BN == 0); 64 columns = one head.
+        // The tile lies inside one section (sec_len % BN == 0); 64 columns = one head,
+        // 128 bytes per row of the head-major output, staged and stored row-contiguously.
         const int sec = n0 / p.sec_len;
         const int nh = p.sec_len / 64;
-        const int seq = static_cast<int>(grow / p.n_tok);
-        const int tok = static_cast<int>(grow - static_cast<long long>(seq) * p.n_tok);
+        const long long vrow = valid ? grow : 0;  // absent rows: in-range table indices, no store
+        const int seq = static_cast<int>(vrow / p.n_tok);
+        const int tok = static_cast<int>(vrow - static_cast<long long>(seq) * p.n_tok);
         const int py = tok / p.grid_w, px = tok - (tok / p.grid_w) * p.grid_w;
         const bool rope = p.sec_rope[sec] != 0;
         T* base = reinterpret_cast<T*>(p.sec_out[sec]);
@@ -277,7 +419,6 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
             tmem_ld32(tacc + c0, ra);
             tmem_ld32(tacc + c0 + 32, rb);
             tmem_wait_ld();
-            if (!valid) continue;
             const int col0 = n0 + c0;
             const int head = (col0 - sec * p.sec_len) >> 6;
             float lo[32], hi[32];
@@ -309,9 +450,13 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
                     }
                 }
             }
+            uint4 o[8];
+            pack16x64<T>(o, lo, hi);
+            __syncwarp();
+            st.put_own(o);
+            __syncwarp();
             T* dst = base + ((static_cast<long long>(seq) * nh + head) * p.n_tok + tok) * 64;
-            store16x32<T>(dst, lo);
-            store16x32<T>(dst + 32, hi);
+            st.store(valid ? reinterpret_cast<char*>(dst) : nullptr, 128);
         }
     } else if constexpr (EPI == EPI_DESC) {
         // Columns are groups of 24 channels, one group per (dy, dx) of the patch
@@ -398,17 +543,23 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
 }
 
 // ------------------------------------------------------------------------- kernel
-template <class T, int BN, int AMODE, int EPI>
+// CG = 2: launched as clusters of 2 CTAs (grid = 2 x pairs).  The even CTA's
+// thread issues the M = 256 MMAs; both CTAs run producer and epilogue roles on
+// the same tile sequence.  A wait that runs out raises the abort flag of both
+// CTAs; neither CTA leaves before the other (cluster barrier at the end).
+template <class T, int BN, int AMODE, int EPI, int CG>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_constant__ CUtensorMap mapA1,
                    const __grid_constant__ CUtensorMap mapB, const __grid_constant__ GemmParams p) {
-    using C = GemmCfg<BN>;
+    static_assert(CG == 1 || CG == 2, "one CTA or a CTA pair per tile");
+    using C = GemmCfg<BN, CG>;
     constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * C::A_BYTES;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+    uint8_t* epi_stage = smem + STAGES * C::STAGE_BYTES;  // 1024-aligned: stage sizes are whole KB
+    uint64_t* bars = reinterpret_cast<uint64_t*>(epi_stage + C::EPI_STAGE_BYTES);
     uint64_t* full = bars;
     uint64_t* empty = bars + STAGES;
     uint64_t* tfull = bars + 2 * STAGES;
@@ -418,11 +569,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t* h4_empty = bars + 2 * STAGES + 6;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 7);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    float* head4_part = reinterpret_cast<float*>(smem + STAGES * C::STAGE_BYTES + 256);
+    float* head4_part = reinterpret_cast<float*>(epi_stage);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int num_tiles = p.tiles_m * p.tiles_n;
+    const int rank = CG == 2 ? static_cast<int>(cluster_rank()) : 0;
+    const bool leader = rank == 0;
+    const int unit = blockIdx.x / CG;        // CTA or CTA pair
+    const int num_units = gridDim.x / CG;
+    const int num_tiles = ((p.tiles_m + CG - 1) / CG) * p.tiles_n;
 
     if (warp == kGemmTmaWarp && lane == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -431,7 +586,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], kGemmEpiWarps * 32);
+            mbar_init(&tempty[b], CG * kGemmEpiWarps);  // one arrival per epilogue warp of each CTA
         }
         mbar_init(mma_done, 1);
         mbar_init(h4_full, 128);
@@ -442,65 +597,123 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (AMODE == A_CONCAT) prefetch_tmap(&mapA1);
         prefetch_tmap(&mapB);
     }
-    if (warp == kGemmMmaWarp) tmem_alloc(tmem_slot, C::TMEM_COLS);
-    __syncthreads();
+    if (warp == kGemmMmaWarp) {
+        if (CG == 2)
+            tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+        else
+            tmem_alloc(tmem_slot, C::TMEM_COLS);
+    }
+    tc_fence_before();
+    if (CG == 2)
+        cluster_sync();  // barriers of both CTAs initialised before any cross-CTA signal
+    else
+        __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // shared::cluster addresses: the even CTA's full / tmem-empty barriers, the peer's abort flag
+    const uint32_t full_c = CG == 2 ? cluster_addr(smem_u32(full), 0) : smem_u32(full);
+    const uint32_t tempty_c = CG == 2 ? cluster_addr(smem_u32(tempty), 0) : smem_u32(tempty);
+    const uint32_t peer_abort_c =
+        CG == 2 ? cluster_addr(smem_u32(const_cast<int*>(abort_flag)), static_cast<uint32_t>(rank ^ 1)) : 0u;
+    auto abort_pair = [&]() {
+        *abort_flag = 1;
+        if (CG == 2) st_cluster_u32(peer_abort_c, 1u);
+    };
 
     if (warp == kGemmTmaWarp) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
             uint32_t it = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-                const TileGeom g = tile_geom<AMODE>(p, t);
+            for (int t = unit; t < num_tiles && ok; t += num_units) {
+                const TileGeom g = tile_geom<AMODE, CG>(p, t, rank);
                 for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1;
-                    if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, kDevTimeoutProducer, p.err)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-                    uint8_t* a_dst = sA + s * C::A_BYTES;
-                    if (AMODE == A_PLAIN) {
-                        tma_load_2d(a_dst, &mapA0, &full[s], kb * 64, g.m_idx * 128);
-                    } else if (AMODE == A_CONCAT) {
-                        if (kb < p.a_split_kb)
-                            tma_load_2d(a_dst, &mapA0, &full[s], kb * 64, g.m_idx * 128);
-                        else
-                            tma_load_2d(a_dst, &mapA1, &full[s], (kb - p.a_split_kb) * 64, g.m_idx * 128);
-                    } else {
-                        const int tap = kb / p.cv_cblocks;
-                        const int cb = kb - tap * p.cv_cblocks;
-                        const int dy = tap / 3 - 1, dx = tap % 3 - 1;
-                        tma_load_4d(a_dst, &mapA0, &full[s], cb * 64, g.x0 + dx, g.y0 + dy, g.img);
+                    if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, kDevTimeoutProducer, p.err)) {
+                        ok = false;
+                        abort_pair();
+                        break;
                     }
-                    tma_load_2d(sB + s * C::B_BYTES, &mapB, &full[s], kb * 64, g.n_idx * BN);
+                    // the even CTA's full barrier counts the bytes of both CTAs
+                    if (leader) mbar_arrive_expect_tx(&full[s], CG * C::STAGE_BYTES);
+                    uint8_t* a_dst = sA + s * C::A_BYTES;
+                    uint8_t* b_dst = sB + s * C::B_BYTES;
+                    const uint32_t bar = full_c + s * 8;
+                    const int brow = g.n_idx * BN + rank * C::B_ROWS;
+                    if (CG == 2) {
+                        if (AMODE == A_PLAIN) {
+                            tma_load_2d_pair(a_dst, &mapA0, bar, kb * 64, g.m_idx * 128);
+                        } else if (AMODE == A_CONCAT) {
+                            if (kb < p.a_split_kb)
+                                tma_load_2d_pair(a_dst, &mapA0, bar, kb * 64, g.m_idx * 128);
+                            else
+                                tma_load_2d_pair(a_dst, &mapA1, bar, (kb - p.a_split_kb) * 64, g.m_idx * 128);
+                        } else {
+                            const int tap = kb / p.cv_cblocks;
+                            const int cb = kb - tap * p.cv_cblocks;
+                            const int dy = tap / 3 - 1, dx = tap % 3 - 1;
+                            tma_load_4d_pair(a_dst, &mapA0, bar, cb * 64, g.x0 + dx, g.y0 + dy, g.img);
+                        }
+                        tma_load_2d_pair(b_dst, &mapB, bar, kb * 64, brow);
+                    } else {
+                        if (AMODE == A_PLAIN) {
+                            tma_load_2d(a_dst, &mapA0, &full[s], kb * 64, g.m_idx * 128);
+                        } else if (AMODE == A_CONCAT) {
+                            if (kb < p.a_split_kb)
+                                tma_load_2d(a_dst, &mapA0, &full[s], kb * 64, g.m_idx * 128);
+                            else
+                                tma_load_2d(a_dst, &mapA1, &full[s], (kb - p.a_split_kb) * 64, g.m_idx * 128);
+                        } else {
+                            const int tap = kb / p.cv_cblocks;
+                            const int cb = kb - tap * p.cv_cblocks;
+                            const int dy = tap / 3 - 1, dx = tap % 3 - 1;
+                            tma_load_4d(a_dst, &mapA0, &full[s], cb * 64, g.x0 + dx, g.y0 + dy, g.img);
+                        }
+                        tma_load_2d(b_dst, &mapB, &full[s], kb * 64, brow);
+                    }
                 }
             }
             if (!ok) {
-                // drain: wait (bounded) for loads that may still be in flight
-                const uint32_t first = it > STAGES ? it - STAGES : 0;
-                for (uint32_t j = first; j < it; ++j) {
-                    volatile int dummy = 0;
-                    mbar_wait(&full[j % STAGES], (j / STAGES) & 1, &dummy, kDevTimeoutProducer, p.err);
+                if (CG == 1) {
+                    // drain: wait (bounded) for loads that may still be in flight
+                    const uint32_t first = it > STAGES ? it - STAGES : 0;
+                    for (uint32_t j = first; j < it; ++j) {
+                        volatile int dummy = 0;
+                        mbar_wait(&full[j % STAGES], (j / STAGES) & 1, &dummy, kDevTimeoutProducer, p.err);
+                    }
+                } else {
+                    // this CTA's loads signal the even CTA's barriers: give loads in flight
+                    // 1 ms (TMA loads take microseconds) before the CTA may leave
+                    const unsigned long long t0 = global_timer_ns();
+                    while (global_timer_ns() - t0 < 1000000ull) __nanosleep(1000);
                 }
             }
         }
     } else if (warp == kGemmMmaWarp) {
-        // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t idesc = idesc_f16kind<T>(128, BN, false, false);
+        // ------------------------------------------------ MMA issuer (even CTA of a pair)
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = idesc_f16kind<T>(128 * CG, BN, false, false);
             uint32_t it = 0, tcount = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++tcount) {
+            for (int t = unit; t < num_tiles && ok; t += num_units, ++tcount) {
                 const uint32_t buf = tcount & 1;
                 const uint32_t tph = (tcount >> 1) & 1;
-                if (!mbar_wait(&tempty[buf], tph ^ 1, abort_flag, kDevTimeoutMma, p.err)) { ok = false; break; }
+                if (!mbar_wait(&tempty[buf], tph ^ 1, abort_flag, kDevTimeoutMma, p.err)) {
+                    ok = false;
+                    abort_pair();
+                    break;
+                }
                 tc_fence_after();
                 const uint32_t dacc = tmem_base + buf * C::ACC_COLS;
                 for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
                     const int s = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1;
-                    if (!mbar_wait(&full[s], ph, abort_flag, kDevTimeoutMma, p.err)) { ok = false; break; }
+                    if (!mbar_wait(&full[s], ph, abort_flag, kDevTimeoutMma, p.err)) {
+                        ok = false;
+                        abort_pair();
+                        break;
+                    }
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(sA + s * C::A_BYTES);
                     const uint32_t b_addr = smem_u32(sB + s * C::B_BYTES);
@@ -508,14 +721,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     for (int k = 0; k < 4; ++k) {
                         const uint64_t ad = umma_desc_sw128(a_addr + k * 32, 16, 1024);
                         const uint64_t bd = umma_desc_sw128(b_addr + k * 32, 16, 1024);
-                        mma_f16_ss(dacc, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                        if (CG == 2)
+                            mma_f16_ss_pair(dacc, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                        else
+                            mma_f16_ss(dacc, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
                     }
-                    mma_commit(&empty[s]);
+                    if (CG == 2)
+                        mma_commit_pair_both(&empty[s]);
+                    else
+                        mma_commit(&empty[s]);
                 }
-                if (ok) mma_commit(&tfull[buf]);
+                if (ok) {
+                    if (CG == 2)
+                        mma_commit_pair_both(&tfull[buf]);
+                    else
+                        mma_commit(&tfull[buf]);
+                }
             }
-            // all issued MMAs complete before the CTA may release TMEM
-            mma_commit(mma_done);
+            // all issued MMAs complete before either CTA may release TMEM or leave
+            if (CG == 2)
+                mma_commit_pair_local(mma_done);
+            else
+                mma_commit(mma_done);
             volatile int dummy = 0;
             mbar_wait(mma_done, 0, &dummy, kDevTimeoutMma, p.err);
         }
@@ -524,24 +751,51 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int quarter = warp & 3;
         const int grp = warp >> 2;
         const int r = quarter * 32 + lane;
-        uint32_t tcount = 0;
-        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++tcount) {
+        const RowStage st{epi_stage + warp * 4096, lane};
+        uint4 pre[8];  // EPI_F32_RESID: residual block of the next unit, fetched ahead
+        uint32_t tcount = 0, h4count = 0;
+        for (int t = unit; t < num_tiles; t += num_units, ++tcount) {
             const uint32_t buf = tcount & 1;
             const uint32_t tph = (tcount >> 1) & 1;
-            if (!mbar_wait(&tfull[buf], tph, abort_flag, kDevTimeoutEpilogue, p.err)) break;
+            const TileGeom g = tile_geom<AMODE, CG>(p, t, rank);
+            if (EPI == EPI_F32_RESID && g.live) {
+                // the residual does not depend on the accumulator: fetch before waiting for it
+                long long grow;
+                bool valid;
+                tile_row<AMODE>(p, g, r, grow, valid);
+                fetch_resid<BN>(p, st, grow, valid, g.n_idx * BN + grp * 32, pre);
+            }
+            if (!mbar_wait(&tfull[buf], tph, abort_flag, kDevTimeoutEpilogue, p.err)) {
+                abort_pair();
+                break;
+            }
             tc_fence_after();
-            const TileGeom g = tile_geom<AMODE>(p, t);
-            const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * C::ACC_COLS;
-            const Head4Sync h4{head4_part, h4_full, h4_empty, abort_flag, tcount};
-            epilogue_tile<T, BN, AMODE, EPI>(p, g, tacc, r, grp, h4);
+            if (g.live) {
+                const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * C::ACC_COLS;
+                const Head4Sync h4{head4_part, h4_full, h4_empty, abort_flag, h4count++};
+                epilogue_tile<T, BN, AMODE, EPI>(p, g, tacc, r, grp, h4, st, pre);
+            }
             tc_fence_before();
-            mbar_arrive(&tempty[buf]);
+            __syncwarp();
+            if (lane == 0) {
+                if (CG == 2)
+                    mbar_arrive_cluster(tempty_c + buf * 8);
+                else
+                    mbar_arrive(&tempty[buf]);
+            }
         }
     }
-    __syncthreads();
+    __syncwarp();
+    if (CG == 2)
+        cluster_sync();  // no CTA leaves while its peer may still signal or read it
+    else
+        __syncthreads();
     if (warp == kGemmMmaWarp) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, C::TMEM_COLS);
+        if (CG == 2)
+            tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+        else
+            tmem_dealloc(tmem_base, C::TMEM_COLS);
     }
 }
 

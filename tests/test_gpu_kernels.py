@@ -32,6 +32,7 @@ def P(a):
 
 
 # ---------------------------------------------------------------------------- GEMM
+@pytest.mark.parametrize("pair", [0, 1], ids=["cta", "pair"])
 @pytest.mark.parametrize("dtype", ["fp16", "bf16"])
 @pytest.mark.parametrize("M,N,K,bn", [
     (128, 256, 64, 256),
@@ -40,7 +41,7 @@ def P(a):
     (1000, 96, 96, 128),
     (2048, 768, 3072, 256),
 ])
-def test_gemm_matches_fp64(lib, M, N, K, bn, dtype):
+def test_gemm_matches_fp64(lib, M, N, K, bn, dtype, pair):
     from mast3r_runtime_b200 import _lib
 
     rng = np.random.default_rng(M + N + K)
@@ -50,7 +51,7 @@ def test_gemm_matches_fp64(lib, M, N, K, bn, dtype):
     c = np.zeros((M, N), np.float32)
     ms = ctypes.c_float(0)
     _lib.check(lib.m3r_gemm_test(0, DTYPES[dtype], P(to16(a, dtype)), P(to16(w, dtype)), P(bias), P(c), M, N, K, bn,
-                                 2, ctypes.byref(ms)))
+                                 pair, 2, ctypes.byref(ms)))
     ref = a.astype(np.float64) @ w.astype(np.float64).T + bias
     # fp32 accumulation of K exact 16-bit products: relative error ~ sqrt(K) * 2^-24
     assert rel_l2(c, ref) < 1e-5, rel_l2(c, ref)
@@ -68,6 +69,7 @@ def _conv3_ref(x, w, b):
     return out + b
 
 
+@pytest.mark.parametrize("pair", [0, 1], ids=["cta", "pair"])
 @pytest.mark.parametrize("dtype", ["fp16", "bf16"])
 @pytest.mark.parametrize("n,h,wd,c,cout,bn", [
     (2, 8, 16, 64, 128, 128),
@@ -75,7 +77,7 @@ def _conv3_ref(x, w, b):
     (2, 5, 32, 192, 128, 128),    # h not a multiple of the box height
     (1, 16, 128, 128, 128, 128),
 ])
-def test_conv3_matches_fp64(lib, n, h, wd, c, cout, bn, dtype):
+def test_conv3_matches_fp64(lib, n, h, wd, c, cout, bn, dtype, pair):
     from mast3r_runtime_b200 import _lib
 
     rng = np.random.default_rng(n * 1000 + h + wd + c)
@@ -86,7 +88,7 @@ def test_conv3_matches_fp64(lib, n, h, wd, c, cout, bn, dtype):
     b = rng.standard_normal(cout).astype(np.float32)
     y = np.zeros((n, h, wd, cout), np.float32)
     _lib.check(lib.m3r_conv3_test(0, DTYPES[dtype], P(to16(x, dtype)), P(to16(w, dtype)), P(b), P(y), n, h, wd, c,
-                                  cout, bn))
+                                  cout, bn, pair))
     ref = _conv3_ref(x, w, b)
     assert rel_l2(y, ref) < 1e-5, rel_l2(y, ref)
 
