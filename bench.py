@@ -296,6 +296,7 @@ def run_ours(args):
     eng.set_profiling(True)
     eng.run_resident(per)
     prof = eng.profile()
+    ops = eng.profile_ops()
     eng.set_profiling(False)
     launches_per_step = int(prof["gemm_launches"] + prof["attn_launches"] + prof["other_launches"])
 
@@ -325,6 +326,9 @@ def run_ours(args):
                           "ms_per_step": prof["attn_ms"], "launches_per_step": int(prof["attn_launches"])},
             "model_tflops": fpp * total_pairs * args.steps / (total_ms / 1000.0) / 1e12,
             "kernel_ms_per_step": {"gemm": prof["gemm_ms"], "attention": prof["attn_ms"], "other": prof["other_ms"]},
+            # per operation of the model: [device ms per step, TFLOP/s (0 for non-contractions)]
+            "ops": {k: [round(o["ms"], 3), round(o["flop"] / (o["ms"] * 1e-3) / 1e12, 1) if o["ms"] > 0 else 0.0]
+                    for k, o in ops.items()},
             "e2e": e2e_line,
             "wall_ms_per_step": 1000.0 * wall / args.steps,
             "gpu_launches": launches_per_step * args.steps,

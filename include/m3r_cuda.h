@@ -130,6 +130,12 @@ int m3r_fetch_outputs(m3r_engine* engine, int n_pairs, float* pts3d_1, float* pt
 int m3r_set_profiling(m3r_engine* engine, int on);
 int m3r_get_profile(const m3r_engine* engine, double* out8);
 
+/* The same profile per operation of the model ("enc.qkv", "enc.attn", "dec.fc2",
+ * "head.layer_rn", ...), one line per operation in order of first launch:
+ * "<name>\t<ms>\t<flop>\t<launches>\n".  Writes at most cap bytes including the
+ * terminating NUL; *needed (when not NULL) gets the full length + 1. */
+int m3r_get_profile_ops(const m3r_engine* engine, char* buf, int cap, int* needed);
+
 /* Pinned host memory for zero-staging transfers. */
 void* m3r_host_alloc(size_t bytes);
 void m3r_host_free(void* p);

@@ -192,6 +192,18 @@ class NativeEngine:
                 "other_launches")
         return dict(zip(keys, map(float, a)))
 
+    def profile_ops(self) -> dict:
+        """{op: {"ms", "flop", "launches"}} of the last profiled pass, in launch order."""
+        need = ctypes.c_int(0)
+        _lib.check(self.lib.m3r_get_profile_ops(self.h, None, 0, ctypes.byref(need)), self.h)
+        buf = ctypes.create_string_buffer(max(need.value, 1))
+        _lib.check(self.lib.m3r_get_profile_ops(self.h, buf, len(buf), None), self.h)
+        ops = {}
+        for line in buf.value.decode().splitlines():
+            name, ms, flop, launches = line.split("\t")
+            ops[name] = {"ms": float(ms), "flop": float(flop), "launches": int(launches)}
+        return ops
+
     def match(self, desc_1, desc_2, top_k=512, reciprocal=True, confidence_threshold=0.5):
         d1 = np.ascontiguousarray(desc_1, dtype=np.float32)
         d2 = np.ascontiguousarray(desc_2, dtype=np.float32)

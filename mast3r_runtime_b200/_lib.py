@@ -79,6 +79,7 @@ SIGNATURES = {
     "m3r_fetch_outputs": (_I, [_P, _I, _P, _P, _P, _P, _P, _P]),
     "m3r_set_profiling": (_I, [_P, _I]),
     "m3r_get_profile": (_I, [_P, _P]),
+    "m3r_get_profile_ops": (_I, [_P, ctypes.c_char_p, _I, ctypes.POINTER(_I)]),
     "m3r_host_alloc": (_P, [ctypes.c_size_t]),
     "m3r_host_free": (None, [_P]),
     "m3r_attention_fwd": (_I, [_I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I, ctypes.POINTER(_F)]),

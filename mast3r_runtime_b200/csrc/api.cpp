@@ -1,5 +1,6 @@
 // C ABI (include/m3r_cuda.h): argument checks, exception -> status code mapping,
 // per-engine and thread-local last-error strings.
+#include <algorithm>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -207,6 +208,18 @@ int m3r_set_profiling(m3r_engine* engine, int on) {
 int m3r_get_profile(const m3r_engine* engine, double* out8) {
     if (!engine || !out8) return M3R_ERR_ARG;
     engine->impl->profile(out8);
+    return M3R_OK;
+}
+
+int m3r_get_profile_ops(const m3r_engine* engine, char* buf, int cap, int* needed) {
+    if (!engine || (cap > 0 && !buf)) return M3R_ERR_ARG;
+    const std::string t = engine->impl->profile_ops();
+    if (needed) *needed = static_cast<int>(t.size()) + 1;
+    if (cap > 0) {
+        const size_t n = std::min(t.size(), static_cast<size_t>(cap - 1));
+        std::memcpy(buf, t.data(), n);
+        buf[n] = '\0';
+    }
     return M3R_OK;
 }
 

@@ -29,6 +29,47 @@ constexpr int kTileBytes = kTile * 64 * 2;  // 16 KB: 128 rows x 128 bytes
 constexpr int kSmemBytes = 5 * kTileBytes + 1024 + 256;
 constexpr uint32_t kColS = 0, kColP = 128, kColO = 192, kTmemCols = 256;
 
+// fp16 operands take the packed fp16 exponential path of the softmax; bf16 keeps
+// fp32 exponentials (an 8-bit significand for the exponent would cost ~0.5% on P).
+template <class T>
+constexpr bool kHalfExp = false;
+template <>
+constexpr bool kHalfExp<__half> = true;
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// (a, b) * s + t in one fma.rn.f32x2
+__device__ __forceinline__ float2 fma2(float a, float b, float s, float t) {
+    unsigned long long ab, ss, tt, r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(ab) : "f"(a), "f"(b));
+    asm("mov.b64 %0, {%1, %1};" : "=l"(ss) : "f"(s));
+    asm("mov.b64 %0, {%1, %1};" : "=l"(tt) : "f"(t));
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(ab), "l"(ss), "l"(tt));
+    float2 o;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(o.x), "=f"(o.y) : "l"(r));
+    return o;
+}
+
+// fp16 pair (low half = x0) of 2^x0, 2^x1
+__device__ __forceinline__ uint32_t ex2_h2(float x0, float x1) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    uint32_t e;
+    asm("ex2.approx.f16x2 %0, %1;" : "=r"(e) : "r"(*reinterpret_cast<const uint32_t*>(&h)));
+    return e;
+}
+
+// s0 += low fp16 of h, s1 += high fp16 of h (fp32 accumulation)
+__device__ __forceinline__ void add_h2_f32(float& s0, float& s1, uint32_t h) {
+    asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+        "add.f32.f16 %0, lo, %0;\n\tadd.f32.f16 %1, hi, %1;\n\t}"
+        : "+f"(s0), "+f"(s1)
+        : "r"(h));
+}
+
 struct AttnParams {
     int nq, nk, heads, n_kv_tiles;
     float scale_log2;  // scale * log2(e)
@@ -179,38 +220,70 @@ __global__ void __launch_bounds__(192, 2)
             mbar_arrive(s_empty);  // S is in registers: the next S may overwrite it
             const int valid = p.nk - j * kTile;  // keys valid in this tile (>= 1)
             const bool full_tile = valid >= kTile;
-            float mx = -INFINITY;
+            // row maximum as 8 independent partial maxima (short dependency chains)
+            float mp[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) mp[u] = -INFINITY;
             if (full_tile) {
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(v[c][i]));
+                    for (int i = 0; i < 32; i += 2) {
+                        float& m = mp[(c * 16 + i / 2) & 7];
+                        m = max3(m, __uint_as_float(v[c][i]), __uint_as_float(v[c][i + 1]));
+                    }
             } else {
 #pragma unroll
                 for (int c = 0; c < 4; ++c)
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
-                        if (c * 32 + i < valid) mx = fmaxf(mx, __uint_as_float(v[c][i]));
+                        if (c * 32 + i < valid) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(v[c][i]));
             }
+            const float mx = max3(max3(mp[0], mp[1], mp[2]), max3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
             const float m_cand = mx * sl2;
             const float m_new = (m_cand > m_use + 8.0f) ? m_cand : m_use;
             const float alpha = ex2_approx(m_use - m_new);  // 1 when m_use is kept, 0 on the first tile
             float rowsum = 0.0f;
             uint32_t pk[4][16];
+            if (kHalfExp<T> && full_tile) {
+                // fp16 operands: the exponent x = s * scale * log2(e) - m is formed in fp32
+                // (two lanes per fma.rn.f32x2), rounded to fp16 and exponentiated two at a
+                // time (ex2.approx.f16x2), which yields P already packed for the PV MMA and
+                // halves the MUFU work; the row sum accumulates the fp16 P values in fp32.
+                float rs[8];
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
+                for (int u = 0; u < 8; ++u) rs[u] = 0.0f;
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int c0 = c * 32 + 2 * i;
-                    float p0 = ex2_approx(__uint_as_float(v[c][2 * i]) * sl2 - m_new);
-                    float p1 = ex2_approx(__uint_as_float(v[c][2 * i + 1]) * sl2 - m_new);
-                    if (!full_tile) {
-                        p0 = c0 < valid ? p0 : 0.0f;
-                        p1 = c0 + 1 < valid ? p1 : 0.0f;
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float2 x = fma2(__uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1]), sl2, -m_new);
+                        pk[c][i] = ex2_h2(x.x, x.y);
+                        const int u = 2 * (i & 3);
+                        add_h2_f32(rs[u], rs[u + 1], pk[c][i]);
                     }
-                    rowsum += p0 + p1;
-                    pk[c][i] = Elem<T>::pack(p0, p1);
-                }
+                rowsum = ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
+            } else {
+                float rs[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) rs[u] = 0.0f;
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int c0 = c * 32 + 2 * i;
+                        float p0 = ex2_approx(__uint_as_float(v[c][2 * i]) * sl2 - m_new);
+                        float p1 = ex2_approx(__uint_as_float(v[c][2 * i + 1]) * sl2 - m_new);
+                        if (!full_tile) {
+                            p0 = c0 < valid ? p0 : 0.0f;
+                            p1 = c0 + 1 < valid ? p1 : 0.0f;
+                        }
+                        rs[2 * (i & 3)] += p0;
+                        rs[2 * (i & 3) + 1] += p1;
+                        pk[c][i] = Elem<T>::pack(p0, p1);
+                    }
+                rowsum = ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
+            }
             if (j > 0) {
                 // P buffer free and O stable once PV of the previous tile is done
                 if (!mbar_wait(o_done, (j - 1) & 1, abort_flag, kDevTimeoutSoftmax, p.err)) { ok = false; break; }

@@ -67,6 +67,7 @@ public:
               int64_t* idx1, int64_t* idx2, float* conf, float* p1, float* p2, float* timing);
     void set_profiling(bool on) { profiling_ = on; }
     void profile(double* out8) const;
+    std::string profile_ops() const;  // "<op>\t<ms>\t<flop>\t<launches>\n" per operation
 
     std::string last_error;
     const Dims& dims() const { return d_; }

@@ -25,9 +25,13 @@ GemmParams gemm_params() {
 
 namespace {
 
+struct Maps {
+    CUtensorMap a0, a1, b;
+    CUtensorMap c[3];  // epilogue TMA-store maps (unused ones zero)
+};
+
 template <class T, int BN, int AMODE, int EPI, int CG>
-void launch(cudaStream_t s, const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b,
-            const GemmParams& p) {
+void launch(cudaStream_t s, const Maps& m, const GemmParams& p) {
     using C = GemmCfg<BN, CG>;
     auto kern = gemm_tc_kernel<T, BN, AMODE, EPI, CG>;
     static std::once_flag once;  // per instantiation; the attribute is set on every device
@@ -58,21 +62,20 @@ void launch(cudaStream_t s, const CUtensorMap& a0, const CUtensorMap& a1, const 
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    M3R_CUDA(cudaLaunchKernelEx(&cfg, kern, a0, a1, b, p));
+    M3R_CUDA(cudaLaunchKernelEx(&cfg, kern, m.a0, m.a1, m.b, m.c[0], m.c[1], m.c[2], p));
 }
 
 #define M3R_GEMM_CASE(BN_, AM_, EPI_)                                \
     if (bn == BN_ && amode == AM_ && epi == EPI_) {                  \
         if (cg == 2)                                                 \
-            launch<T, BN_, AM_, EPI_, 2>(s, a0, a1, b, p);           \
+            launch<T, BN_, AM_, EPI_, 2>(s, m, p);                   \
         else                                                         \
-            launch<T, BN_, AM_, EPI_, 1>(s, a0, a1, b, p);           \
+            launch<T, BN_, AM_, EPI_, 1>(s, m, p);                   \
         return;                                                      \
     }
 
 template <class T>
-void dispatch_t(cudaStream_t s, int bn, int amode, int epi, int cg, const CUtensorMap& a0, const CUtensorMap& a1,
-                const CUtensorMap& b, const GemmParams& p) {
+void dispatch_t(cudaStream_t s, int bn, int amode, int epi, int cg, const Maps& m, const GemmParams& p) {
     M3R_GEMM_CASE(256, A_PLAIN, EPI_BF16)
     M3R_GEMM_CASE(128, A_PLAIN, EPI_BF16)
     M3R_GEMM_CASE(256, A_PLAIN, EPI_F32)
@@ -94,12 +97,11 @@ void dispatch_t(cudaStream_t s, int bn, int amode, int epi, int cg, const CUtens
                              " epi=" + std::to_string(epi));
 }
 
-void dispatch(cudaStream_t s, int dt, int bn, int amode, int epi, int cg, const CUtensorMap& a0,
-              const CUtensorMap& a1, const CUtensorMap& b, const GemmParams& p) {
+void dispatch(cudaStream_t s, int dt, int bn, int amode, int epi, int cg, const Maps& m, const GemmParams& p) {
     if (dt == DT_F16)
-        dispatch_t<__half>(s, bn, amode, epi, cg, a0, a1, b, p);
+        dispatch_t<__half>(s, bn, amode, epi, cg, m, p);
     else if (dt == DT_BF16)
-        dispatch_t<__nv_bfloat16>(s, bn, amode, epi, cg, a0, a1, b, p);
+        dispatch_t<__nv_bfloat16>(s, bn, amode, epi, cg, m, p);
     else
         throw Error(kErrArg, "unknown operand type " + std::to_string(dt));
 }
@@ -115,6 +117,34 @@ int pick_cg(int cta_pair, int tiles_m) {
     return tiles_m >= 2 ? 2 : 1;
 }
 
+// Epilogue TMA-store maps: BF16 / F32 / F32_RESID outputs as a [rows, N] matrix and
+// EPI_HEADS sections as [seq * heads, n_tok, 64], with 32-row boxes.  p.c_tma stays 0
+// (row-staged thread stores) when the layout does not allow whole 32-row boxes.
+void out_maps(int dt, int epi, long long rows, bool rows_consecutive, GemmParams& p, Maps& m) {
+    std::memset(m.c, 0, sizeof(m.c));
+    p.c_tma = 0;
+    if (!rows_consecutive) return;
+    const bool out_ok = p.out != nullptr && reinterpret_cast<uintptr_t>(p.out) % 16 == 0;
+    if (epi == EPI_BF16) {
+        if (!out_ok || (p.ldo * 2) % 16 != 0) return;
+        m.c[0] = tmap_2d(dt, p.out, rows, p.N, p.ldo, 32);
+        p.c_tma = 1;
+    } else if (epi == EPI_F32 || epi == EPI_F32_RESID) {
+        if (!out_ok || (p.ldo * 4) % 16 != 0) return;
+        m.c[0] = tmap_2d_f32(p.out, rows, p.N, p.ldo, 32);
+        p.c_tma = 1;
+    } else if (epi == EPI_HEADS) {
+        if (p.n_tok <= 0 || p.n_tok % 32 != 0 || rows % p.n_tok != 0 || p.sec_len % 64 != 0) return;
+        const long long nseq_heads = rows / p.n_tok * (p.sec_len / 64);
+        for (int i = 0; i < 3; ++i) {
+            if (p.sec_out[i] == nullptr) continue;
+            if (reinterpret_cast<uintptr_t>(p.sec_out[i]) % 16 != 0) return;
+            m.c[i] = tmap_3d_rows64(dt, p.sec_out[i], p.n_tok, nseq_heads, 32);
+        }
+        p.c_tma = 1;
+    }
+}
+
 }  // namespace
 
 void gemm_rows(cudaStream_t s, int dt, int bn, int epi, const void* A, long long lda, int M, int K, const void* W,
@@ -127,9 +157,11 @@ void gemm_rows(cudaStream_t s, int dt, int bn, int epi, const void* A, long long
     p.tiles_m = cdiv(M, 128);
     p.tiles_n = cdiv(N, bn);
     const int cg = pick_cg(cta_pair, p.tiles_m);
-    const CUtensorMap a = tmap_2d(dt, A, M, K, lda, 128);
-    const CUtensorMap b = tmap_2d(dt, W, N, K, ldw, bn / cg);
-    dispatch(s, dt, bn, A_PLAIN, epi, cg, a, a, b, p);
+    Maps m;
+    m.a0 = m.a1 = tmap_2d(dt, A, M, K, lda, 128);
+    m.b = tmap_2d(dt, W, N, K, ldw, bn / cg);
+    out_maps(dt, epi, M, true, p, m);
+    dispatch(s, dt, bn, A_PLAIN, epi, cg, m, p);
 }
 
 void gemm_concat(cudaStream_t s, int dt, int bn, int epi, const void* A0, long long lda0, int K0, const void* A1,
@@ -143,10 +175,12 @@ void gemm_concat(cudaStream_t s, int dt, int bn, int epi, const void* A0, long l
     p.tiles_m = cdiv(M, 128);
     p.tiles_n = cdiv(N, bn);
     const int cg = pick_cg(cta_pair, p.tiles_m);
-    const CUtensorMap a0 = tmap_2d(dt, A0, M, K0, lda0, 128);
-    const CUtensorMap a1 = tmap_2d(dt, A1, M, K1, lda1, 128);
-    const CUtensorMap b = tmap_2d(dt, W, N, K0 + K1, ldw, bn / cg);
-    dispatch(s, dt, bn, A_CONCAT, epi, cg, a0, a1, b, p);
+    Maps m;
+    m.a0 = tmap_2d(dt, A0, M, K0, lda0, 128);
+    m.a1 = tmap_2d(dt, A1, M, K1, lda1, 128);
+    m.b = tmap_2d(dt, W, N, K0 + K1, ldw, bn / cg);
+    out_maps(dt, epi, M, true, p, m);
+    dispatch(s, dt, bn, A_CONCAT, epi, cg, m, p);
 }
 
 void gemm_conv3(cudaStream_t s, int dt, int bn, int epi, const void* X, int n, int h, int w, int c, int cstride,
@@ -170,9 +204,12 @@ void gemm_conv3(cudaStream_t s, int dt, int bn, int epi, const void* X, int n, i
     p.tiles_m = n * p.cv_tx * p.cv_ty;
     p.tiles_n = cdiv(N, bn);
     const int cg = pick_cg(cta_pair, p.tiles_m);
-    const CUtensorMap a = tmap_nhwc(dt, X, n, h, w, c, cstride, hbox, wbox);
-    const CUtensorMap b = tmap_2d(dt, W, N, 9LL * cblocks * 64, 9LL * cblocks * 64, bn / cg);
-    dispatch(s, dt, bn, A_CONV3, epi, cg, a, a, b, p);
+    Maps m;
+    m.a0 = m.a1 = tmap_nhwc(dt, X, n, h, w, c, cstride, hbox, wbox);
+    m.b = tmap_2d(dt, W, N, 9LL * cblocks * 64, 9LL * cblocks * 64, bn / cg);
+    // a warp's 32 output pixels are consecutive in one image row when boxes are >= 32 wide
+    out_maps(dt, epi, p.M, wbox >= 32, p, m);
+    dispatch(s, dt, bn, A_CONV3, epi, cg, m, p);
 }
 
 }  // namespace m3r

@@ -65,8 +65,15 @@ struct GemmParams {
     const float* b4;   // [4]
     // EPI_CONVT
     int ct_s, ct_cout, ct_h, ct_w;
+    // 1: the output goes out through TMA stores of whole 32-row boxes (maps C0-C2:
+    // the output matrix, or the three head-major sections of EPI_HEADS)
+    int c_tma;
     // device status word: a wait that runs out of time records its code here
     int* err;
+};
+
+struct StoreMaps {
+    const CUtensorMap* c[3];
 };
 
 constexpr int kGemmEpiWarps = 8;
@@ -289,11 +296,18 @@ __device__ __forceinline__ void fetch_resid(const GemmParams& p, const RowStage&
 
 template <class T, int BN, int AMODE, int EPI>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeom& g, uint32_t tacc, int r, int grp,
-                                              const Head4Sync& h4, const RowStage& st, uint4 (&pre)[8]) {
+                                              const Head4Sync& h4, const RowStage& st, uint4 (&pre)[8],
+                                              const StoreMaps& maps) {
     long long grow;
     bool valid;
     tile_row<AMODE>(p, g, r, grow, valid);
     const int n0 = g.n_idx * BN;
+    // TMA stores: the warp's 32 rows are consecutive output rows starting at wrow0
+    // (A_CONV3 only with boxes at least 32 pixels wide); wok = that row exists
+    long long wrow0;
+    bool wok;
+    tile_row<AMODE>(p, g, r - st.lane, wrow0, wok);
+    const int lane = st.lane;
 
     if constexpr (EPI == EPI_F32 || EPI == EPI_F32_RESID) {
         // units of 32 fp32 columns = 128 bytes per row, staged and stored row-contiguously
@@ -314,7 +328,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
             float v[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[i]);
-            __syncwarp();  // the previous unit's row-contiguous reads of the stage are done
+            if (p.c_tma && lane == 0) bulk_wait_read_all();
+            __syncwarp();  // the previous unit's reads of the stage (threads or TMA) are done
             if constexpr (EPI == EPI_F32_RESID) {
                 st.deposit(cur);
                 __syncwarp();
@@ -335,9 +350,19 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
                 o[q] = make_uint4(__float_as_uint(v[4 * q]), __float_as_uint(v[4 * q + 1]), __float_as_uint(v[4 * q + 2]),
                                   __float_as_uint(v[4 * q + 3]));
             st.put_own(o);
-            __syncwarp();
-            st.store(valid ? reinterpret_cast<char*>(reinterpret_cast<float*>(p.out) + grow * p.ldo + col0) : nullptr,
-                     (full ? 32 : p.N - col0) * 4);
+            if (p.c_tma) {
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0 && wok) {
+                    tma_store_2d(maps.c[0], st.buf, col0, static_cast<int>(wrow0));
+                    bulk_commit();
+                }
+            } else {
+                __syncwarp();
+                st.store(valid ? reinterpret_cast<char*>(reinterpret_cast<float*>(p.out) + grow * p.ldo + col0)
+                               : nullptr,
+                         (full ? 32 : p.N - col0) * 4);
+            }
         }
     } else if constexpr (EPI == EPI_BF16) {
         // units of 64 16-bit columns = 128 bytes per row, staged and stored row-contiguously
@@ -372,11 +397,21 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
             }
             uint4 o[8];
             pack16x64<T>(o, lo, hi);
+            if (p.c_tma && lane == 0) bulk_wait_read_all();
             __syncwarp();
             st.put_own(o);
-            __syncwarp();
-            st.store(valid ? reinterpret_cast<char*>(reinterpret_cast<T*>(p.out) + grow * p.ldo + col0) : nullptr,
-                     (col0 + 64 <= p.N ? 64 : p.N - col0) * 2);
+            if (p.c_tma) {
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0 && wok) {
+                    tma_store_2d(maps.c[0], st.buf, col0, static_cast<int>(wrow0));
+                    bulk_commit();
+                }
+            } else {
+                __syncwarp();
+                st.store(valid ? reinterpret_cast<char*>(reinterpret_cast<T*>(p.out) + grow * p.ldo + col0) : nullptr,
+                         (col0 + 64 <= p.N ? 64 : p.N - col0) * 2);
+            }
         }
     } else if constexpr (EPI == EPI_CONVT) {
 #pragma unroll 1
@@ -452,11 +487,24 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
             }
             uint4 o[8];
             pack16x64<T>(o, lo, hi);
+            if (p.c_tma && lane == 0) bulk_wait_read_all();
             __syncwarp();
             st.put_own(o);
-            __syncwarp();
-            T* dst = base + ((static_cast<long long>(seq) * nh + head) * p.n_tok + tok) * 64;
-            st.store(valid ? reinterpret_cast<char*>(dst) : nullptr, 128);
+            if (p.c_tma) {
+                // n_tok % 32 == 0: the warp's rows are tokens tok0 .. tok0 + 31 of one sequence
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0 && wok) {
+                    const int seq0 = static_cast<int>(wrow0 / p.n_tok);
+                    const int tok0 = static_cast<int>(wrow0 - static_cast<long long>(seq0) * p.n_tok);
+                    tma_store_3d(maps.c[sec], st.buf, 0, tok0, seq0 * nh + head);
+                    bulk_commit();
+                }
+            } else {
+                __syncwarp();
+                T* dst = base + ((static_cast<long long>(seq) * nh + head) * p.n_tok + tok) * 64;
+                st.store(valid ? reinterpret_cast<char*>(dst) : nullptr, 128);
+            }
         }
     } else if constexpr (EPI == EPI_DESC) {
         // Columns are groups of 24 channels, one group per (dy, dx) of the patch
@@ -515,13 +563,25 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
             tmem_ld32(tacc + c0, raw);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const int c = c0 + i;
-                const float v = fmaxf(__uint_as_float(raw[i]) + __ldg(p.bias + c), 0.0f);
-                o0 += v * __ldg(p.w4 + c);
-                o1 += v * __ldg(p.w4 + 128 + c);
-                o2 += v * __ldg(p.w4 + 256 + c);
-                o3 += v * __ldg(p.w4 + 384 + c);
+            for (int q = 0; q < 8; ++q) {
+                // bias and the four 1x1 weight rows, four columns per vector load
+                const int c = c0 + 4 * q;
+                const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + c));
+                const float4 wa = __ldg(reinterpret_cast<const float4*>(p.w4 + c));
+                const float4 wb = __ldg(reinterpret_cast<const float4*>(p.w4 + 128 + c));
+                const float4 wc = __ldg(reinterpret_cast<const float4*>(p.w4 + 256 + c));
+                const float4 wd = __ldg(reinterpret_cast<const float4*>(p.w4 + 384 + c));
+                const float bb[4] = {b.x, b.y, b.z, b.w};
+                const float aa[4] = {wa.x, wa.y, wa.z, wa.w}, ab[4] = {wb.x, wb.y, wb.z, wb.w};
+                const float ac[4] = {wc.x, wc.y, wc.z, wc.w}, ad[4] = {wd.x, wd.y, wd.z, wd.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float v = fmaxf(__uint_as_float(raw[4 * q + e]) + bb[e], 0.0f);
+                    o0 += v * aa[e];
+                    o1 += v * ab[e];
+                    o2 += v * ac[e];
+                    o3 += v * ad[e];
+                }
             }
         }
         const uint32_t ph = h4.tile & 1;
@@ -550,7 +610,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
 template <class T, int BN, int AMODE, int EPI, int CG>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_constant__ CUtensorMap mapA1,
-                   const __grid_constant__ CUtensorMap mapB, const __grid_constant__ GemmParams p) {
+                   const __grid_constant__ CUtensorMap mapB, const __grid_constant__ CUtensorMap mapC0,
+                   const __grid_constant__ CUtensorMap mapC1, const __grid_constant__ CUtensorMap mapC2,
+                   const __grid_constant__ GemmParams p) {
     static_assert(CG == 1 || CG == 2, "one CTA or a CTA pair per tile");
     using C = GemmCfg<BN, CG>;
     constexpr int STAGES = C::STAGES;
@@ -752,6 +814,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int grp = warp >> 2;
         const int r = quarter * 32 + lane;
         const RowStage st{epi_stage + warp * 4096, lane};
+        const StoreMaps maps{{&mapC0, &mapC1, &mapC2}};
         uint4 pre[8];  // EPI_F32_RESID: residual block of the next unit, fetched ahead
         uint32_t tcount = 0, h4count = 0;
         for (int t = unit; t < num_tiles; t += num_units, ++tcount) {
@@ -773,7 +836,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (g.live) {
                 const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * C::ACC_COLS;
                 const Head4Sync h4{head4_part, h4_full, h4_empty, abort_flag, h4count++};
-                epilogue_tile<T, BN, AMODE, EPI>(p, g, tacc, r, grp, h4, st, pre);
+                epilogue_tile<T, BN, AMODE, EPI>(p, g, tacc, r, grp, h4, st, pre, maps);
             }
             tc_fence_before();
             __syncwarp();
@@ -784,6 +847,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     mbar_arrive(&tempty[buf]);
             }
         }
+        if (lane == 0) bulk_wait_all();  // TMA stores of this warp complete before the CTA ends
     }
     __syncwarp();
     if (CG == 2)

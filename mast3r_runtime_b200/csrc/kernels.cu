@@ -159,47 +159,87 @@ __device__ __forceinline__ void bilerp_acc(const T* base, int hi, int wi, int C,
     }
 }
 
-template <class T>
-__global__ void dpt_fuse_kernel(const T* __restrict__ f0, const T* __restrict__ f1, int h1, int w1,
-                                const T* __restrict__ f2, int h2, int w2, const T* __restrict__ f3, int h3, int w3,
-                                int n, int H0, int W0, int C, T* __restrict__ out) {
-    const int c8n = C / 8;
-    const long long total = static_cast<long long>(n) * H0 * W0 * c8n;
-    for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
-         e += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const int c8 = static_cast<int>(e % c8n) * 8;
-        long long pix = e / c8n;
-        const int x = static_cast<int>(pix % W0);
-        pix /= W0;
-        const int y = static_cast<int>(pix % H0);
-        const int im = static_cast<int>(pix / H0);
-        F8 acc;
-        load8(f0 + ((static_cast<long long>(im) * H0 + y) * W0 + x) * C + c8, acc);
-        bilerp_acc(f1 + static_cast<long long>(im) * h1 * w1 * C, h1, w1, C, H0, W0, y, x, c8, acc);
-        bilerp_acc(f2 + static_cast<long long>(im) * h2 * w2 * C, h2, w2, C, H0, W0, y, x, c8, acc);
-        bilerp_acc(f3 + static_cast<long long>(im) * h3 * w3 * C, h3, w3, C, H0, W0, y, x, c8, acc);
-        store8(out + ((static_cast<long long>(im) * H0 + y) * W0 + x) * C + c8, acc);
+// Grid of the NHWC elementwise kernels below: blockIdx.z = image, blockIdx.y =
+// (output) row, x = (pixel in the row, 8-channel chunk); no 64-bit division.
+struct RowGrid {
+    int c8n;  // 8-channel chunks per pixel
+    __device__ __forceinline__ bool at(int w, int& x, int& c8) const {
+        const int e = blockIdx.x * blockDim.x + threadIdx.x;
+        x = e / c8n;
+        c8 = (e - x * c8n) * 8;
+        return x < w;
     }
+};
+
+inline dim3 row_grid(int n, int rows, int w, int c8n, int block) {
+    return dim3((w * c8n + block - 1) / block, rows, n);
 }
 
 template <class T>
-__global__ void resize_kernel(const T* __restrict__ x, int n, int hi, int wi, int C, int ho, int wo,
-                              T* __restrict__ y) {
-    const int c8n = C / 8;
-    const long long total = static_cast<long long>(n) * ho * wo * c8n;
-    for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
-         e += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const int c8 = static_cast<int>(e % c8n) * 8;
-        long long pix = e / c8n;
-        const int xx = static_cast<int>(pix % wo);
-        pix /= wo;
-        const int yy = static_cast<int>(pix % ho);
-        const int im = static_cast<int>(pix / ho);
-        F8 acc;
+__global__ void dpt_fuse_kernel(const T* __restrict__ f0, const T* __restrict__ f1, int h1, int w1,
+                                const T* __restrict__ f2, int h2, int w2, const T* __restrict__ f3, int h3, int w3,
+                                int H0, int W0, int C, T* __restrict__ out) {
+    int x, c8;
+    if (!RowGrid{C / 8}.at(W0, x, c8)) return;
+    const int y = blockIdx.y;
+    const long long im = blockIdx.z;
+    F8 acc;
+    load8(f0 + ((im * H0 + y) * W0 + x) * C + c8, acc);
+    bilerp_acc(f1 + im * h1 * w1 * C, h1, w1, C, H0, W0, y, x, c8, acc);
+    bilerp_acc(f2 + im * h2 * w2 * C, h2, w2, C, H0, W0, y, x, c8, acc);
+    bilerp_acc(f3 + im * h3 * w3 * C, h3, w3, C, H0, W0, y, x, c8, acc);
+    store8(out + ((im * H0 + y) * W0 + x) * C + c8, acc);
+}
+
+template <class T>
+__global__ void resize_kernel(const T* __restrict__ x, int hi, int wi, int C, int ho, int wo, T* __restrict__ y) {
+    int ox, c8;
+    if (!RowGrid{C / 8}.at(wo, ox, c8)) return;
+    const int oy = blockIdx.y;
+    const long long im = blockIdx.z;
+    F8 acc;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc.v[i] = 0.0f;
-        bilerp_acc(x + static_cast<long long>(im) * hi * wi * C, hi, wi, C, ho, wo, yy, xx, c8, acc);
-        store8(y + ((static_cast<long long>(im) * ho + yy) * wo + xx) * C + c8, acc);
+    for (int i = 0; i < 8; ++i) acc.v[i] = 0.0f;
+    bilerp_acc(x + im * hi * wi * C, hi, wi, C, ho, wo, oy, ox, c8, acc);
+    store8(y + ((im * ho + oy) * wo + ox) * C + c8, acc);
+}
+
+// Exact 2x upsampling (half-pixel centres): output row 2i takes input rows i-1, i
+// with weights 0.25, 0.75 and row 2i+1 takes i, i+1 with 0.75, 0.25, the
+// neighbours clamped at the borders (which reproduces the clamped source
+// coordinate of bilerp_acc); the same along x.  The thread of input pixel
+// (iy, ix) writes the four output pixels (2iy + a, 2ix + b) from its clamped 3x3
+// neighbourhood.
+template <class T>
+__global__ void resize2x_kernel(const T* __restrict__ x, int hi, int wi, int C, T* __restrict__ y) {
+    int ix, c8;
+    if (!RowGrid{C / 8}.at(wi, ix, c8)) return;
+    const int iy = blockIdx.y;
+    const long long im = blockIdx.z;
+    const T* base = x + im * hi * wi * C + c8;
+    const int ho = 2 * hi, wo = 2 * wi;
+    const int ry[3] = {max(iy - 1, 0), iy, min(iy + 1, hi - 1)};
+    const int rx[3] = {max(ix - 1, 0), ix, min(ix + 1, wi - 1)};
+    F8 nb[3][3];
+#pragma unroll
+    for (int a = 0; a < 3; ++a)
+#pragma unroll
+        for (int b = 0; b < 3; ++b) load8(base + (static_cast<long long>(ry[a]) * wi + rx[b]) * C, nb[a][b]);
+    constexpr float kF[2] = {0.75f, 0.25f};  // fraction towards the second tap, output phase 0 / 1
+#pragma unroll
+    for (int a = 0; a < 2; ++a) {
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+            const float fy = kF[a], fx = kF[b];
+            F8 o;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float top = nb[a][b].v[i] * (1.0f - fx) + nb[a][b + 1].v[i] * fx;
+                const float bot = nb[a + 1][b].v[i] * (1.0f - fx) + nb[a + 1][b + 1].v[i] * fx;
+                o.v[i] = top * (1.0f - fy) + bot * fy;
+            }
+            store8(y + ((im * ho + 2 * iy + a) * wo + 2 * ix + b) * C + c8, o);
+        }
     }
 }
 
@@ -299,18 +339,23 @@ void cast16(cudaStream_t s, int dt, const float* x, long long n, void* y) {
 void dpt_fuse(cudaStream_t s, int dt, const void* f0, const void* f1, int h1, int w1, const void* f2, int h2, int w2,
               const void* f3, int h3, int w3, int n, int H0, int W0, int C, void* out) {
     M3R_REQUIRE(C % 8 == 0, "dpt_fuse: C % 8");
-    const long long total = static_cast<long long>(n) * H0 * W0 * (C / 8);
-    M3R_BY_DT(dt, dpt_fuse_kernel<T><<<grid_for(total, 256), 256, 0, s>>>(
+    M3R_REQUIRE(n <= 65535 && H0 <= 65535, "dpt_fuse: grid too large");
+    M3R_BY_DT(dt, dpt_fuse_kernel<T><<<row_grid(n, H0, W0, C / 8, 128), 128, 0, s>>>(
                       static_cast<const T*>(f0), static_cast<const T*>(f1), h1, w1, static_cast<const T*>(f2), h2, w2,
-                      static_cast<const T*>(f3), h3, w3, n, H0, W0, C, static_cast<T*>(out)));
+                      static_cast<const T*>(f3), h3, w3, H0, W0, C, static_cast<T*>(out)));
     M3R_CUDA(cudaGetLastError());
 }
 
 void resize16(cudaStream_t s, int dt, const void* x, int n, int hi, int wi, int C, int ho, int wo, void* y) {
     M3R_REQUIRE(C % 8 == 0, "resize16: C % 8");
-    const long long total = static_cast<long long>(n) * ho * wo * (C / 8);
-    M3R_BY_DT(dt, resize_kernel<T><<<grid_for(total, 256), 256, 0, s>>>(static_cast<const T*>(x), n, hi, wi, C, ho, wo,
-                                                                        static_cast<T*>(y)));
+    M3R_REQUIRE(n <= 65535 && ho <= 65535, "resize16: grid too large");
+    if (ho == 2 * hi && wo == 2 * wi) {
+        M3R_BY_DT(dt, resize2x_kernel<T><<<row_grid(n, hi, wi, C / 8, 128), 128, 0, s>>>(
+                          static_cast<const T*>(x), hi, wi, C, static_cast<T*>(y)));
+    } else {
+        M3R_BY_DT(dt, resize_kernel<T><<<row_grid(n, ho, wo, C / 8, 128), 128, 0, s>>>(
+                          static_cast<const T*>(x), hi, wi, C, ho, wo, static_cast<T*>(y)));
+    }
     M3R_CUDA(cudaGetLastError());
 }
 

@@ -31,7 +31,9 @@ CUtensorMap encode(int dt, const void* ptr, int rank, const cuuint64_t* dims, co
         M3R_REQUIRE(strides_bytes[i] % 16 == 0, "tensor map strides must be multiples of 16 bytes");
     CUtensorMap m;
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-    const CUtensorMapDataType type = dt == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const CUtensorMapDataType type = dt == kTmapF32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                     : dt == 1      ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                    : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     const CUresult r = encode_fn()(&m, type, rank, const_cast<void*>(ptr), dims, strides_bytes, box, estr,
                                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -46,6 +48,13 @@ CUtensorMap tmap_2d(int dt, const void* ptr, uint64_t rows, uint64_t cols, uint6
     const cuuint64_t str[1] = {ld * 2};
     const cuuint32_t box[2] = {64, box_rows};
     return encode(dt, ptr, 2, dims, str, box);
+}
+
+CUtensorMap tmap_2d_f32(const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t str[1] = {ld * 4};
+    const cuuint32_t box[2] = {32, box_rows};
+    return encode(kTmapF32, ptr, 2, dims, str, box);
 }
 
 CUtensorMap tmap_3d_rows64(int dt, const void* ptr, uint64_t d1, uint64_t d2, uint32_t box_d1) {

@@ -1,7 +1,7 @@
 // Host-side TMA tensor-map encoding (cuTensorMapEncodeTiled through the runtime's
 // driver entry point, so the library does not link libcuda directly).  All maps
-// are of 16-bit elements (fp16 or bf16, `dt` = Dt), 128-byte swizzled boxes whose
-// inner extent is 64 elements; out-of-bounds box elements read as zero.
+// use 128-byte swizzled boxes whose inner extent is 128 bytes (64 16-bit or 32
+// fp32 elements); out-of-bounds box elements read as zero and are not stored.
 #pragma once
 
 #include <cuda.h>
@@ -42,8 +42,14 @@ constexpr int kErrNoMem = -7;
         if (!(cond)) throw ::m3r::Error(::m3r::kErrArg, std::string(msg)); \
     } while (0)
 
+// Element type code of the fp32 maps (the 16-bit maps take a Dt code: 0 bf16, 1 fp16).
+constexpr int kTmapF32 = 2;
+
 // row-major matrix [rows, cols] with row stride ld (elements); box [box_rows, 64].
 CUtensorMap tmap_2d(int dt, const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows);
+
+// row-major fp32 matrix [rows, cols], row stride ld (elements); box [box_rows, 32].
+CUtensorMap tmap_2d_f32(const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows);
 
 // tensor [d2, d1, 64] (innermost 64 = head dim), box [box_d1, 64].
 CUtensorMap tmap_3d_rows64(int dt, const void* ptr, uint64_t d1, uint64_t d2, uint32_t box_d1);

@@ -131,3 +131,29 @@ def test_drop_in_engine_contract(tmp_path):
     assert len(m.idx_1) <= 128 and "match_ms" in dict(m.timing)
     with pytest.raises(RuntimeError):
         eng.infer(np.zeros((10, 10), np.uint8), np.zeros((10, 10), np.uint8))
+
+
+def test_profile_per_operation(tmp_path):
+    """The profiled pass attributes every launch to one operation of the model; the
+    per-operation times add up to the per-family totals."""
+    from mast3r_runtime_b200 import NativeEngine, make_weights, save_safetensors
+    from mast3r_runtime_b200.weights import tiny_dims
+
+    d = tiny_dims()
+    path = save_safetensors(tmp_path / "u.safetensors", make_weights(d, seed=5))
+    rng = np.random.default_rng(2)
+    eng = NativeEngine(d, (64, 96), [0], 2)
+    eng.load(str(path))
+    eng.stage(rng.integers(0, 256, (2, 64, 96, 3), dtype=np.uint8), rng.integers(0, 256, (2, 64, 96, 3), dtype=np.uint8))
+    eng.set_profiling(True)
+    eng.run_resident(2)
+    fam = eng.profile()
+    ops = eng.profile_ops()
+    eng.close()
+    for k in ("patch.gemm", "enc.qkv", "enc.attn", "enc.fc1", "dec.attn_cross", "dec.fc2", "head.layer_rn", "lf.fc2"):
+        assert k in ops, k
+    assert ops["enc.attn"]["launches"] == d.enc_depth
+    assert ops["dec.attn_cross"]["launches"] == 2 * d.dec_depth
+    total = sum(o["ms"] for o in ops.values())
+    assert abs(total - (fam["gemm_ms"] + fam["attn_ms"] + fam["other_ms"])) < 1e-3 * max(total, 1.0)
+    assert sum(o["launches"] for o in ops.values()) == fam["gemm_launches"] + fam["attn_launches"] + fam["other_launches"]
