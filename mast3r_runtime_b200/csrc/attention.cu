@@ -4,13 +4,19 @@
 //   Q, K, V : head-major [seq, head, tok, 64] (written by the QKV GEMM epilogue)
 //   O       : token-major [seq, tok, head * 64] (the A operand of the output projection)
 //
-// One CTA = 128 query rows of one (seq, head).  192 threads: warps 0-3 softmax
-// (thread = query row = TMEM lane), warp 4 TMA producer, warp 5 MMA issuer.
-// TMEM (256 columns, so two CTAs fit on an SM): S = Q K^T in [0,128), P (two
-// 16-bit values per column) in [128,192), O in [192,256).  S uses an SS MMA;
-// O += P V uses a TS MMA with P from TMEM and V read MN-major straight from its
-// TMA tile.  K/V tiles of 128 keys are double-buffered; keys beyond Nk are masked
-// to -inf (their V rows are zero-filled by TMA).  Scores never touch HBM.
+// One CTA = 128 query rows of one (seq, head), two CTAs per SM.  320 threads:
+// warps 0-7 softmax, warp 8 TMA producer, warp 9 MMA issuer.  Each query row (TMEM
+// lane) is shared by two softmax threads, warp w and warp w + 4 (same TMEM lane
+// quarter): thread half h takes keys [64 h, 64 h + 64) of every tile and output
+// columns [32 h, 32 h + 32), which halves the per-thread softmax latency of a tile.
+// The two halves agree on the row maximum through shared memory each tile and add
+// their row sums once at the end.
+// TMEM (256 columns per CTA): S = Q K^T in [0,128), P (two 16-bit values per
+// column) in [128,192), O in [192,256).  S uses an SS MMA; O += P V uses a TS MMA
+// with P from TMEM and V read MN-major straight from its TMA tile.  K and V tiles of
+// 128 keys stream through separate rings, so a K stage is refilled as soon as its
+// Q K^T has run; keys beyond Nk are masked to -inf (their V rows are zero-filled by
+// TMA).  Scores never touch HBM.
 //
 // Semantics: softmax(Q K^T * scale) V per head, as
 // backends/python/croco_encoder.py:80-85 and croco_decoder.py:76-82, 171-177.
@@ -26,7 +32,21 @@ namespace {
 
 constexpr int kTile = 128;
 constexpr int kTileBytes = kTile * 64 * 2;  // 16 KB: 128 rows x 128 bytes
-constexpr int kSmemBytes = 5 * kTileBytes + 1024 + 256;
+constexpr int kKStages = 2;                 // K ring (a stage frees when its Q K^T has run)
+constexpr int kVStages = 3;                 // V ring (a stage frees when its P V has run)
+constexpr int kSoftmaxWarps = 8;
+constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
+constexpr int kProducerWarp = kSoftmaxWarps;
+constexpr int kMmaWarp = kSoftmaxWarps + 1;
+constexpr int kThreads = (kSoftmaxWarps + 2) * 32;
+// shared memory: Q | K ring | V ring | row-maximum exchange [2 parities][2 halves][128]
+// | row-sum exchange [2 halves][128] | barriers.  The dynamic shared memory base is
+// 1024-byte aligned (declared alignment, checked at run time), so two CTAs fit in
+// one SM with their 1 KB reserves.
+constexpr int kXmOff = (1 + kKStages + kVStages) * kTileBytes;
+constexpr int kXlOff = kXmOff + 2 * 2 * kTile * 4;
+constexpr int kBarOff = kXlOff + 2 * kTile * 4;
+constexpr int kSmemBytes = kBarOff + 256;
 constexpr uint32_t kColS = 0, kColP = 128, kColO = 192, kTmemCols = 256;
 
 // fp16 operands take the packed fp16 exponential path of the softmax; bf16 keeps
@@ -70,6 +90,14 @@ __device__ __forceinline__ void add_h2_f32(float& s0, float& s1, uint32_t h) {
         : "r"(h));
 }
 
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]));
+}
+
 struct AttnParams {
     int nq, nk, heads, n_kv_tiles;
     float scale_log2;  // scale * log2(e)
@@ -78,24 +106,33 @@ struct AttnParams {
 };
 
 template <class T>
-__global__ void __launch_bounds__(192, 2)
+__global__ void __launch_bounds__(kThreads, 2)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
                     const __grid_constant__ CUtensorMap mapV, const __grid_constant__ AttnParams p) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    extern __shared__ __align__(1024) uint8_t smem[];
+    if ((smem_u32(smem) & 1023u) != 0) {  // 128-byte swizzled tiles need 1024-byte alignment
+        if (threadIdx.x == 0) atomicCAS(p.err, 0, kDevBadSmemAlign);
+        return;
+    }
     uint8_t* sQ = smem;
-    uint8_t* sK = smem + kTileBytes;       // 2 stages
-    uint8_t* sV = smem + 3 * kTileBytes;   // 2 stages
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 5 * kTileBytes);
+    uint8_t* sK = smem + kTileBytes;                   // kKStages
+    uint8_t* sV = smem + (1 + kKStages) * kTileBytes;  // kVStages
+    float* xm = reinterpret_cast<float*>(smem + kXmOff);  // [parity][half][row] partial row maxima
+    float* xl = reinterpret_cast<float*>(smem + kXlOff);  // [half][row] partial row sums
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
     uint64_t* q_full = bars + 0;
-    uint64_t* kv_full = bars + 1;   // [2]
-    uint64_t* kv_empty = bars + 3;  // [2]
-    uint64_t* s_full = bars + 5;
-    uint64_t* s_empty = bars + 6;
-    uint64_t* p_full = bars + 7;
-    uint64_t* o_done = bars + 8;
-    uint64_t* mma_done = bars + 9;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+    uint64_t* k_full = bars + 1;                         // [kKStages]
+    uint64_t* k_empty = k_full + kKStages;               // [kKStages]
+    uint64_t* v_full = k_empty + kKStages;               // [kVStages]
+    uint64_t* v_empty = v_full + kVStages;               // [kVStages]
+    uint64_t* s_full = v_empty + kVStages;
+    uint64_t* s_empty = s_full + 1;
+    uint64_t* p_full = s_full + 2;
+    uint64_t* o_done = s_full + 3;
+    uint64_t* mma_done = s_full + 4;
+    uint64_t* xm_bar = s_full + 5;   // all softmax threads published their tile maxima
+    uint64_t* xl_bar = s_full + 6;   // all softmax threads published their row sums
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 7);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -106,76 +143,95 @@ __global__ void __launch_bounds__(192, 2)
     const int plane = seq * p.heads + head;
     const int nkv = p.n_kv_tiles;
 
-    if (warp == 4 && lane == 0) {
+    if (warp == kProducerWarp && lane == 0) {
         mbar_init(q_full, 1);
-        for (int s = 0; s < 2; ++s) {
-            mbar_init(&kv_full[s], 1);
-            mbar_init(&kv_empty[s], 1);
+        for (int s = 0; s < kKStages; ++s) {
+            mbar_init(&k_full[s], 1);
+            mbar_init(&k_empty[s], 1);
+        }
+        for (int s = 0; s < kVStages; ++s) {
+            mbar_init(&v_full[s], 1);
+            mbar_init(&v_empty[s], 1);
         }
         mbar_init(s_full, 1);
-        mbar_init(s_empty, 128);
-        mbar_init(p_full, 128);
+        mbar_init(s_empty, kSoftmaxThreads);
+        mbar_init(p_full, kSoftmaxThreads);
         mbar_init(o_done, 1);
         mbar_init(mma_done, 1);
+        mbar_init(xm_bar, kSoftmaxThreads);
+        mbar_init(xl_bar, kSoftmaxThreads);
         *abort_flag = 0;
         fence_barrier_init();
         prefetch_tmap(&mapQ);
         prefetch_tmap(&mapK);
         prefetch_tmap(&mapV);
     }
-    if (warp == 5) tmem_alloc(tmem_slot, kTmemCols);
+    if (warp == kMmaWarp) tmem_alloc(tmem_slot, kTmemCols);
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 4) {
+    if (warp == kProducerWarp) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
             mbar_arrive_expect_tx(q_full, kTileBytes);
             tma_load_3d(sQ, &mapQ, q_full, 0, q0, plane);
-            int issued = 0;
+            int k_issued = 0, v_issued = 0;
             bool ok = true;
-            for (int j = 0; j < nkv; ++j) {
-                const int st = j & 1;
-                const uint32_t ph = (j >> 1) & 1;
-                if (!mbar_wait(&kv_empty[st], ph ^ 1, abort_flag, kDevTimeoutProducer, p.err)) { ok = false; break; }
-                mbar_arrive_expect_tx(&kv_full[st], 2 * kTileBytes);
-                tma_load_3d(sK + st * kTileBytes, &mapK, &kv_full[st], 0, j * kTile, plane);
-                tma_load_3d(sV + st * kTileBytes, &mapV, &kv_full[st], 0, j * kTile, plane);
-                issued = j + 1;
+            for (int j = 0; j < nkv && ok; ++j) {
+                const int sk = j % kKStages, sv = j % kVStages;
+                if (!mbar_wait(&k_empty[sk], ((j / kKStages) & 1) ^ 1, abort_flag, kDevTimeoutProducer, p.err)) {
+                    ok = false;
+                    break;
+                }
+                mbar_arrive_expect_tx(&k_full[sk], kTileBytes);
+                tma_load_3d(sK + sk * kTileBytes, &mapK, &k_full[sk], 0, j * kTile, plane);
+                k_issued = j + 1;
+                if (!mbar_wait(&v_empty[sv], ((j / kVStages) & 1) ^ 1, abort_flag, kDevTimeoutProducer, p.err)) {
+                    ok = false;
+                    break;
+                }
+                mbar_arrive_expect_tx(&v_full[sv], kTileBytes);
+                tma_load_3d(sV + sv * kTileBytes, &mapV, &v_full[sv], 0, j * kTile, plane);
+                v_issued = j + 1;
             }
             if (!ok) {
+                // drain: wait (bounded) for loads that may still be in flight
                 volatile int dummy = 0;
                 mbar_wait(q_full, 0, &dummy, kDevTimeoutProducer, p.err);
-                for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j)
-                    mbar_wait(&kv_full[j & 1], (j >> 1) & 1, &dummy, kDevTimeoutProducer, p.err);
+                for (int j = k_issued > kKStages ? k_issued - kKStages : 0; j < k_issued; ++j)
+                    mbar_wait(&k_full[j % kKStages], (j / kKStages) & 1, &dummy, kDevTimeoutProducer, p.err);
+                for (int j = v_issued > kVStages ? v_issued - kVStages : 0; j < v_issued; ++j)
+                    mbar_wait(&v_full[j % kVStages], (j / kVStages) & 1, &dummy, kDevTimeoutProducer, p.err);
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == kMmaWarp) {
         // ------------------------------------------------------------ MMA issuer
-        // S_{j+1} = Q K_{j+1}^T is issued as soon as the softmax warps have read S_j
+        // S_{j+1} = Q K_{j+1}^T is issued as soon as the softmax threads have read S_j
         // into registers, so it overlaps their exponentials; O += P_j V_j follows P_j.
         if (lane == 0) {
             constexpr uint32_t idesc_s = idesc_f16kind<T>(128, 128, false, false);
             constexpr uint32_t idesc_o = idesc_f16kind<T>(128, 64, false, true);
             const uint32_t q_addr = smem_u32(sQ);
             auto issue_s = [&](int j) {
-                const uint32_t k_addr = smem_u32(sK + (j & 1) * kTileBytes);
+                const uint32_t k_addr = smem_u32(sK + (j % kKStages) * kTileBytes);
 #pragma unroll
                 for (int k = 0; k < 4; ++k)
                     mma_f16_ss(tmem + kColS, umma_desc_sw128(q_addr + k * 32, 16, 1024),
                                umma_desc_sw128(k_addr + k * 32, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
                 mma_commit(s_full);
+                mma_commit(&k_empty[j % kKStages]);
             };
             bool ok = mbar_wait(q_full, 0, abort_flag, kDevTimeoutMma, p.err) &&
-                      mbar_wait(&kv_full[0], 0, abort_flag, kDevTimeoutMma, p.err);
+                      mbar_wait(&k_full[0], 0, abort_flag, kDevTimeoutMma, p.err);
             if (ok) {
                 tc_fence_after();
                 issue_s(0);
             }
             for (int j = 0; j < nkv && ok; ++j) {
                 if (j + 1 < nkv) {
-                    if (!mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, abort_flag, kDevTimeoutMma, p.err) ||
+                    if (!mbar_wait(&k_full[(j + 1) % kKStages], ((j + 1) / kKStages) & 1, abort_flag, kDevTimeoutMma,
+                                   p.err) ||
                         !mbar_wait(s_empty, j & 1, abort_flag, kDevTimeoutMma, p.err)) {
                         ok = false;
                         break;
@@ -183,14 +239,18 @@ __global__ void __launch_bounds__(192, 2)
                     tc_fence_after();
                     issue_s(j + 1);
                 }
-                if (!mbar_wait(p_full, j & 1, abort_flag, kDevTimeoutMma, p.err)) { ok = false; break; }
+                if (!mbar_wait(&v_full[j % kVStages], (j / kVStages) & 1, abort_flag, kDevTimeoutMma, p.err) ||
+                    !mbar_wait(p_full, j & 1, abort_flag, kDevTimeoutMma, p.err)) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
-                const uint32_t v_addr = smem_u32(sV + (j & 1) * kTileBytes);
+                const uint32_t v_addr = smem_u32(sV + (j % kVStages) * kTileBytes);
 #pragma unroll
                 for (int k = 0; k < 8; ++k)
                     mma_f16_ts(tmem + kColO, tmem + kColP + k * 8, umma_desc_sw128(v_addr + k * 2048, 16384, 1024),
                                idesc_o, (j > 0 || k > 0) ? 1u : 0u);
-                mma_commit(&kv_empty[j & 1]);
+                mma_commit(&v_empty[j % kVStages]);
                 mma_commit(o_done);
             }
             mma_commit(mma_done);
@@ -198,35 +258,37 @@ __global__ void __launch_bounds__(192, 2)
             mbar_wait(mma_done, 0, &dummy, kDevTimeoutMma, p.err);
         }
     } else {
-        // ------------------------------------------------------------ softmax (warps 0-3)
+        // ------------------------------------------------------------ softmax (warps 0-7)
         // Lazy rescaling: the exponent offset m_use only moves when the row maximum
         // exceeds it by more than 8 (log2 units), so P <= 2^8 and O is rescaled rarely.
-        const int r = warp * 32 + lane;
-        const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-        const uint32_t tS = tmem + lane_base + kColS;
-        const uint32_t tP = tmem + lane_base + kColP;
-        const uint32_t tO = tmem + lane_base + kColO;
+        // Both halves of a row take the same decisions (same maxima, same order).
+        const int quarter = warp & 3, half = warp >> 2;
+        const int r = quarter * 32 + lane;
+        const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+        const uint32_t tS = tmem + lane_base + kColS + 64 * half;
+        const uint32_t tP = tmem + lane_base + kColP + 32 * half;
+        const uint32_t tO = tmem + lane_base + kColO + 32 * half;
         const float sl2 = p.scale_log2;
         float m_use = -INFINITY, l_run = 0.0f;
         bool ok = true;
         for (int j = 0; j < nkv; ++j) {
             if (!mbar_wait(s_full, j & 1, abort_flag, kDevTimeoutSoftmax, p.err)) { ok = false; break; }
             tc_fence_after();
-            uint32_t v[4][32];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, v[c]);
+            uint32_t v[2][32];
+            tmem_ld32(tS, v[0]);
+            tmem_ld32(tS + 32, v[1]);
             tmem_wait_ld();
             tc_fence_before();
             mbar_arrive(s_empty);  // S is in registers: the next S may overwrite it
-            const int valid = p.nk - j * kTile;  // keys valid in this tile (>= 1)
-            const bool full_tile = valid >= kTile;
-            // row maximum as 8 independent partial maxima (short dependency chains)
+            const int valid = p.nk - j * kTile - 64 * half;  // keys of this half that exist (may be <= 0)
+            const bool full_half = valid >= 64;
+            // partial row maximum over this half, 8 independent chains
             float mp[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) mp[u] = -INFINITY;
-            if (full_tile) {
+            if (full_half) {
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
+                for (int c = 0; c < 2; ++c)
 #pragma unroll
                     for (int i = 0; i < 32; i += 2) {
                         float& m = mp[(c * 16 + i / 2) & 7];
@@ -234,27 +296,34 @@ __global__ void __launch_bounds__(192, 2)
                     }
             } else {
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
+                for (int c = 0; c < 2; ++c)
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
                         if (c * 32 + i < valid) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(v[c][i]));
             }
-            const float mx = max3(max3(mp[0], mp[1], mp[2]), max3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+            const float pmax = max3(max3(mp[0], mp[1], mp[2]), max3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+            // exchange with the other half of the row (parity-buffered slots: a slot is
+            // rewritten two tiles later, after the partner has passed the next exchange)
+            float* slot = xm + (j & 1) * 2 * kTile;
+            slot[half * kTile + r] = pmax;
+            mbar_arrive(xm_bar);
+            if (!mbar_wait(xm_bar, j & 1, abort_flag, kDevTimeoutSoftmax, p.err)) { ok = false; break; }
+            const float mx = fmaxf(slot[r], slot[kTile + r]);  // same operand order in both halves
             const float m_cand = mx * sl2;
             const float m_new = (m_cand > m_use + 8.0f) ? m_cand : m_use;
             const float alpha = ex2_approx(m_use - m_new);  // 1 when m_use is kept, 0 on the first tile
             float rowsum = 0.0f;
-            uint32_t pk[4][16];
-            if (kHalfExp<T> && full_tile) {
+            uint32_t pk[2][16];
+            if (kHalfExp<T> && full_half) {
                 // fp16 operands: the exponent x = s * scale * log2(e) - m is formed in fp32
                 // (two lanes per fma.rn.f32x2), rounded to fp16 and exponentiated two at a
-                // time (ex2.approx.f16x2), which yields P already packed for the PV MMA and
-                // halves the MUFU work; the row sum accumulates the fp16 P values in fp32.
+                // time (ex2.approx.f16x2), which yields P already packed for the PV MMA;
+                // the row sum accumulates the fp16 P values in fp32.
                 float rs[8];
 #pragma unroll
                 for (int u = 0; u < 8; ++u) rs[u] = 0.0f;
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
+                for (int c = 0; c < 2; ++c)
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         const float2 x = fma2(__uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1]), sl2, -m_new);
@@ -268,13 +337,13 @@ __global__ void __launch_bounds__(192, 2)
 #pragma unroll
                 for (int u = 0; u < 8; ++u) rs[u] = 0.0f;
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
+                for (int c = 0; c < 2; ++c)
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         const int c0 = c * 32 + 2 * i;
                         float p0 = ex2_approx(__uint_as_float(v[c][2 * i]) * sl2 - m_new);
                         float p1 = ex2_approx(__uint_as_float(v[c][2 * i + 1]) * sl2 - m_new);
-                        if (!full_tile) {
+                        if (!full_half) {
                             p0 = c0 < valid ? p0 : 0.0f;
                             p1 = c0 + 1 < valid ? p1 : 0.0f;
                         }
@@ -289,58 +358,51 @@ __global__ void __launch_bounds__(192, 2)
                 if (!mbar_wait(o_done, (j - 1) & 1, abort_flag, kDevTimeoutSoftmax, p.err)) { ok = false; break; }
                 tc_fence_after();
                 if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+                    uint32_t o[32];
+                    tmem_ld32(tO, o);
+                    tmem_wait_ld();
 #pragma unroll
-                    for (int c = 0; c < 2; ++c) {
-                        uint32_t o[32];
-                        tmem_ld32(tO + c * 32, o);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                        tmem_st32(tO + c * 32, o);
-                    }
+                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                    tmem_st32(tO, o);
                 }
             }
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-                asm volatile(
-                    "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-                    "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(tP + c * 16),
-                    "r"(pk[c][0]), "r"(pk[c][1]), "r"(pk[c][2]), "r"(pk[c][3]), "r"(pk[c][4]), "r"(pk[c][5]),
-                    "r"(pk[c][6]), "r"(pk[c][7]), "r"(pk[c][8]), "r"(pk[c][9]), "r"(pk[c][10]), "r"(pk[c][11]),
-                    "r"(pk[c][12]), "r"(pk[c][13]), "r"(pk[c][14]), "r"(pk[c][15]));
+            tmem_st16(tP, pk[0]);
+            tmem_st16(tP + 16, pk[1]);
             tmem_wait_st();
             l_run = l_run * alpha + rowsum;
             m_use = m_new;
             tc_fence_before();
             mbar_arrive(p_full);
         }
-        if (ok && mbar_wait(o_done, (nkv - 1) & 1, abort_flag, kDevTimeoutSoftmax, p.err)) {
+        // row sum: this half's share + the other half's
+        xl[half * kTile + r] = l_run;
+        mbar_arrive(xl_bar);
+        if (ok && mbar_wait(xl_bar, 0, abort_flag, kDevTimeoutSoftmax, p.err) &&
+            mbar_wait(o_done, (nkv - 1) & 1, abort_flag, kDevTimeoutSoftmax, p.err)) {
             tc_fence_after();
-            uint32_t o[2][32];
-            tmem_ld32(tO, o[0]);
-            tmem_ld32(tO + 32, o[1]);
+            uint32_t o[32];
+            tmem_ld32(tO, o);
             tmem_wait_ld();
             const int q = q0 + r;
             if (q < p.nq) {
-                const float inv = 1.0f / l_run;
-                T* dst = reinterpret_cast<T*>(p.out) + (static_cast<long long>(seq) * p.nq + q) * (p.heads * 64) + head * 64;
+                const float inv = 1.0f / (xl[r] + xl[kTile + r]);  // same operand order in both halves
+                T* dst = reinterpret_cast<T*>(p.out) + (static_cast<long long>(seq) * p.nq + q) * (p.heads * 64) +
+                         head * 64 + 32 * half;
                 uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-                for (int h = 0; h < 2; ++h)
-#pragma unroll
-                    for (int qq = 0; qq < 4; ++qq) {
-                        uint4 u;
-                        u.x = Elem<T>::pack(__uint_as_float(o[h][qq * 8 + 0]) * inv, __uint_as_float(o[h][qq * 8 + 1]) * inv);
-                        u.y = Elem<T>::pack(__uint_as_float(o[h][qq * 8 + 2]) * inv, __uint_as_float(o[h][qq * 8 + 3]) * inv);
-                        u.z = Elem<T>::pack(__uint_as_float(o[h][qq * 8 + 4]) * inv, __uint_as_float(o[h][qq * 8 + 5]) * inv);
-                        u.w = Elem<T>::pack(__uint_as_float(o[h][qq * 8 + 6]) * inv, __uint_as_float(o[h][qq * 8 + 7]) * inv);
-                        d4[h * 4 + qq] = u;
-                    }
+                for (int qq = 0; qq < 4; ++qq) {
+                    uint4 u;
+                    u.x = Elem<T>::pack(__uint_as_float(o[qq * 8 + 0]) * inv, __uint_as_float(o[qq * 8 + 1]) * inv);
+                    u.y = Elem<T>::pack(__uint_as_float(o[qq * 8 + 2]) * inv, __uint_as_float(o[qq * 8 + 3]) * inv);
+                    u.z = Elem<T>::pack(__uint_as_float(o[qq * 8 + 4]) * inv, __uint_as_float(o[qq * 8 + 5]) * inv);
+                    u.w = Elem<T>::pack(__uint_as_float(o[qq * 8 + 6]) * inv, __uint_as_float(o[qq * 8 + 7]) * inv);
+                    d4[qq] = u;
+                }
             }
         }
     }
     __syncthreads();
-    if (warp == 5) {
+    if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
@@ -360,7 +422,7 @@ void launch(cudaStream_t s, const CUtensorMap& mq, const CUtensorMap& mk, const 
         }
         M3R_CUDA(cudaSetDevice(cur));
     });
-    attn_fwd_kernel<T><<<grid, 192, kSmemBytes, s>>>(mq, mk, mv, p);
+    attn_fwd_kernel<T><<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, p);
     M3R_CUDA(cudaGetLastError());
 }
 

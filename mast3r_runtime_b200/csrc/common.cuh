@@ -21,6 +21,7 @@ enum DeviceError : int {
     kDevTimeoutMma = 2,
     kDevTimeoutEpilogue = 3,
     kDevTimeoutSoftmax = 4,
+    kDevBadSmemAlign = 5,  // dynamic shared memory not at the alignment the kernel declares
 };
 
 // Spin budget for every mbarrier wait: the wait gives up after about two
