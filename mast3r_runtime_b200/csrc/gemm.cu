@@ -32,7 +32,7 @@ struct Maps {
 
 template <class T, int BN, int AMODE, int EPI, int CG>
 void launch(cudaStream_t s, const Maps& m, const GemmParams& p) {
-    using C = GemmCfg<BN, CG>;
+    using C = GemmCfg<BN, CG, AMODE>;
     auto kern = gemm_tc_kernel<T, BN, AMODE, EPI, CG>;
     static std::once_flag once;  // per instantiation; the attribute is set on every device
     std::call_once(once, [&] {
@@ -74,6 +74,13 @@ void launch(cudaStream_t s, const Maps& m, const GemmParams& p) {
         return;                                                      \
     }
 
+// A_CONV3W variants exist for CTA pairs only
+#define M3R_GEMM_CASE_PAIR(BN_, AM_, EPI_)                 \
+    if (bn == BN_ && amode == AM_ && epi == EPI_ && cg == 2) { \
+        launch<T, BN_, AM_, EPI_, 2>(s, m, p);             \
+        return;                                            \
+    }
+
 template <class T>
 void dispatch_t(cudaStream_t s, int bn, int amode, int epi, int cg, const Maps& m, const GemmParams& p) {
     M3R_GEMM_CASE(256, A_PLAIN, EPI_BF16)
@@ -93,6 +100,9 @@ void dispatch_t(cudaStream_t s, int bn, int amode, int epi, int cg, const Maps& 
     M3R_GEMM_CASE(128, A_CONV3, EPI_HEAD4)
     M3R_GEMM_CASE(128, A_CONV3, EPI_F32)  // conv parity test entry
     M3R_GEMM_CASE(256, A_CONV3, EPI_F32)
+    M3R_GEMM_CASE_PAIR(128, A_CONV3W, EPI_BF16)
+    M3R_GEMM_CASE_PAIR(128, A_CONV3W, EPI_HEAD4)
+    M3R_GEMM_CASE_PAIR(128, A_CONV3W, EPI_F32)  // conv parity test entry
     throw Error(kErrArg, "no GEMM variant for bn=" + std::to_string(bn) + " amode=" + std::to_string(amode) +
                              " epi=" + std::to_string(epi));
 }
@@ -204,12 +214,16 @@ void gemm_conv3(cudaStream_t s, int dt, int bn, int epi, const void* X, int n, i
     p.tiles_m = n * p.cv_tx * p.cv_ty;
     p.tiles_n = cdiv(N, bn);
     const int cg = pick_cg(cta_pair, p.tiles_m);
+    // 128-pixel row tiles on CTA pairs with 128 output channels per tile: one wide box
+    // per (dy, channel block) serves the three dx taps
+    const bool wide = cg == 2 && wbox == 128 && bn == 128;
+    if (wide) p.num_kb = 3 * cblocks;
     Maps m;
-    m.a0 = m.a1 = tmap_nhwc(dt, X, n, h, w, c, cstride, hbox, wbox);
+    m.a0 = m.a1 = tmap_nhwc(dt, X, n, h, w, c, cstride, hbox, wide ? GemmCfg<128, 2, A_CONV3W>::WIDE_ROWS : wbox);
     m.b = tmap_2d(dt, W, N, 9LL * cblocks * 64, 9LL * cblocks * 64, bn / cg);
     // a warp's 32 output pixels are consecutive in one image row when boxes are >= 32 wide
     out_maps(dt, epi, p.M, wbox >= 32, p, m);
-    dispatch(s, dt, bn, A_CONV3, epi, cg, m, p);
+    dispatch(s, dt, bn, wide ? A_CONV3W : A_CONV3, epi, cg, m, p);
 }
 
 }  // namespace m3r

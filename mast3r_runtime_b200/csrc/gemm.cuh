@@ -17,6 +17,10 @@
 //   A_CONV3   4-D map [img, H, W, C]: implicit-GEMM 3x3 convolution, stride 1,
 //             pad 1; the 9 taps are TMA boxes shifted by (dy, dx), zero padding
 //             comes from TMA out-of-bounds fill.  A tile is wbox x hbox pixels.
+//   A_CONV3W  the same convolution for tiles of 128 pixels of one image row (W a
+//             multiple of 128): one 136-pixel box per (dy, 64-channel block), from
+//             x0 - 1, serves the three dx taps (MMA operand start 0, 1 or 2 rows
+//             into it), a third of A_CONV3's operand traffic.  CTA pairs only.
 // Epilogues: see enum Epi.
 #pragma once
 
@@ -24,7 +28,7 @@
 
 namespace m3r {
 
-enum AMode : int { A_PLAIN = 0, A_CONCAT = 1, A_CONV3 = 2 };
+enum AMode : int { A_PLAIN = 0, A_CONCAT = 1, A_CONV3 = 2, A_CONV3W = 3 };
 
 enum Epi : int {
     EPI_BF16 = 0,       // out_T = act(acc + bias)   (16-bit output of the operand type T)
@@ -40,7 +44,7 @@ enum Act : int { ACT_NONE = 0, ACT_GELU = 1, ACT_RELU = 2 };
 
 struct GemmParams {
     int M, N;          // output rows (plain/concat) and columns
-    int num_kb;        // k-blocks (of 64) per tile
+    int num_kb;        // k-blocks (of 64) per tile; A_CONV3W: (dy, channel block) groups of 3 k-blocks
     int tiles_m, tiles_n;
     int a_split_kb;    // A_CONCAT: k-blocks taken from map A0
     // A_CONV3 geometry
@@ -84,13 +88,17 @@ constexpr int kGemmMmaWarp = kGemmEpiWarps + 1;
 // CG = CTAs per tile: 1, or 2 for a CTA pair (cluster of 2) running M = 256 MMAs,
 // in which each CTA stages its own 128 rows of A and half of the tile's BN rows
 // of B, and holds its 128 x BN accumulator rows in its own TMEM.
-template <int BN, int CG>
+// A_CONV3W stages one 136-pixel A box and the B blocks of three taps per stage.
+template <int BN, int CG, int AMODE = A_PLAIN>
 struct GemmCfg {
     static constexpr int BM = 128;
     static constexpr int BK = 64;
     static constexpr int B_ROWS = BN / CG;  // rows of B staged by each CTA
-    static constexpr int A_BYTES = BM * BK * 2;
-    static constexpr int B_BYTES = B_ROWS * BK * 2;
+    static constexpr int WIDE_ROWS = 136;   // A_CONV3W box: 128 pixels + 2 halo, rounded to 8 rows
+    static constexpr int TAPS = AMODE == A_CONV3W ? 3 : 1;  // B blocks per stage
+    static constexpr int A_BYTES = (AMODE == A_CONV3W ? WIDE_ROWS : BM) * BK * 2;
+    static constexpr int B_TAP_BYTES = B_ROWS * BK * 2;
+    static constexpr int B_BYTES = TAPS * B_TAP_BYTES;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     // per-epilogue-warp row staging, 4 KB each (EPI_HEAD4 keeps its partial sums there)
     static constexpr int EPI_STAGE_BYTES = kGemmEpiWarps * 4096;
@@ -103,7 +111,9 @@ struct GemmCfg {
     static constexpr int TMEM_COLS = 2 * ACC_COLS;
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + FIXED_BYTES;
     static_assert(STAGES >= 3 && SMEM_BYTES <= MAX_SMEM, "shared memory budget");
-    static_assert(BN % (8 * CG) == 0 && B_BYTES % 1024 == 0, "B half-tiles must be whole swizzle atoms");
+    static_assert(BN % (8 * CG) == 0 && B_TAP_BYTES % 1024 == 0 && A_BYTES % 1024 == 0,
+                  "operand tiles must be whole swizzle atoms");
+    static_assert(AMODE != A_CONV3W || CG == 2, "A_CONV3W runs on CTA pairs");
 };
 
 struct TileGeom {
@@ -121,7 +131,7 @@ __device__ __forceinline__ TileGeom tile_geom(const GemmParams& p, int t, int ra
     g.m_idx = mp * CG + rank;
     g.live = g.m_idx < p.tiles_m;
     g.img = g.y0 = g.x0 = 0;
-    if (AMODE == A_CONV3) {
+    if (AMODE == A_CONV3 || AMODE == A_CONV3W) {
         const int per_img = p.cv_tx * p.cv_ty;
         g.img = g.m_idx / per_img;
         const int rem = g.m_idx - g.img * per_img;
@@ -265,6 +275,7 @@ struct RowStage {
 // two mbarriers (h4[0] "partials written", h4[1] "partials consumed") with bounded waits.
 struct Head4Sync {
     float* part;       // [128][4]
+    const float* wts;  // [128] float4 1x1 weights (channel-major) + [128] bias, in shared memory
     uint64_t* full;    // count 128: group 1 arrives after writing
     uint64_t* empty;   // count 128: group 0 arrives after reading
     volatile int* abort_flag;
@@ -274,7 +285,7 @@ struct Head4Sync {
 // Tile row r -> global output row (grow) and whether it exists.
 template <int AMODE>
 __device__ __forceinline__ void tile_row(const GemmParams& p, const TileGeom& g, int r, long long& grow, bool& valid) {
-    if (AMODE == A_CONV3) {
+    if (AMODE == A_CONV3 || AMODE == A_CONV3W) {
         const int y = g.y0 + r / p.cv_wbox;
         const int x = g.x0 + r % p.cv_wbox;
         valid = y < p.cv_H;
@@ -556,7 +567,11 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
     } else if constexpr (EPI == EPI_HEAD4) {
         // BN == 128 == all channels of one pixel: relu(conv3x3 + b) then 1x1 conv to 4.
         // Group g takes columns [64 g, 64 g + 64); group 1 hands its partial sums to group 0.
+        // The bias and the 1x1 weights (column-major, one float4 per channel) sit in
+        // shared memory (Head4Sync::wts), read as warp-wide broadcasts.
         float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+        const float4* wt = reinterpret_cast<const float4*>(h4.wts);   // [128] (w0c, w1c, w2c, w3c)
+        const float4* bs = reinterpret_cast<const float4*>(h4.wts + 4 * 128);  // bias, [32] float4
 #pragma unroll 1
         for (int c0 = grp * 64; c0 < grp * 64 + 64; c0 += 32) {
             uint32_t raw[32];
@@ -564,23 +579,16 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
             tmem_wait_ld();
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
-                // bias and the four 1x1 weight rows, four columns per vector load
-                const int c = c0 + 4 * q;
-                const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + c));
-                const float4 wa = __ldg(reinterpret_cast<const float4*>(p.w4 + c));
-                const float4 wb = __ldg(reinterpret_cast<const float4*>(p.w4 + 128 + c));
-                const float4 wc = __ldg(reinterpret_cast<const float4*>(p.w4 + 256 + c));
-                const float4 wd = __ldg(reinterpret_cast<const float4*>(p.w4 + 384 + c));
+                const float4 b = bs[(c0 >> 2) + q];
                 const float bb[4] = {b.x, b.y, b.z, b.w};
-                const float aa[4] = {wa.x, wa.y, wa.z, wa.w}, ab[4] = {wb.x, wb.y, wb.z, wb.w};
-                const float ac[4] = {wc.x, wc.y, wc.z, wc.w}, ad[4] = {wd.x, wd.y, wd.z, wd.w};
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
+                    const float4 w = wt[c0 + 4 * q + e];
                     const float v = fmaxf(__uint_as_float(raw[4 * q + e]) + bb[e], 0.0f);
-                    o0 += v * aa[e];
-                    o1 += v * ab[e];
-                    o2 += v * ac[e];
-                    o3 += v * ad[e];
+                    o0 += v * w.x;
+                    o1 += v * w.y;
+                    o2 += v * w.z;
+                    o3 += v * w.w;
                 }
             }
         }
@@ -614,7 +622,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                    const __grid_constant__ CUtensorMap mapC1, const __grid_constant__ CUtensorMap mapC2,
                    const __grid_constant__ GemmParams p) {
     static_assert(CG == 1 || CG == 2, "one CTA or a CTA pair per tile");
-    using C = GemmCfg<BN, CG>;
+    using C = GemmCfg<BN, CG, AMODE>;
     constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -632,6 +640,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 7);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     float* head4_part = reinterpret_cast<float*>(epi_stage);
+    float* head4_wts = reinterpret_cast<float*>(epi_stage + 2048);  // EPI_HEAD4: 640 floats
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -658,6 +667,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         prefetch_tmap(&mapA0);
         if (AMODE == A_CONCAT) prefetch_tmap(&mapA1);
         prefetch_tmap(&mapB);
+    }
+    if (EPI == EPI_HEAD4 && warp < kGemmEpiWarps) {
+        // stage the 1x1 weights transposed (w[o][c] -> wts[4 c + o]) and the bias
+        for (int i = threadIdx.x; i < 128; i += kGemmEpiWarps * 32) {
+            head4_wts[4 * i + 0] = p.w4[i];
+            head4_wts[4 * i + 1] = p.w4[128 + i];
+            head4_wts[4 * i + 2] = p.w4[256 + i];
+            head4_wts[4 * i + 3] = p.w4[384 + i];
+            head4_wts[512 + i] = p.bias[i];
+        }
     }
     if (warp == kGemmMmaWarp) {
         if (CG == 2)
@@ -711,13 +730,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                 tma_load_2d_pair(a_dst, &mapA0, bar, kb * 64, g.m_idx * 128);
                             else
                                 tma_load_2d_pair(a_dst, &mapA1, bar, (kb - p.a_split_kb) * 64, g.m_idx * 128);
-                        } else {
+                        } else if (AMODE == A_CONV3) {
                             const int tap = kb / p.cv_cblocks;
                             const int cb = kb - tap * p.cv_cblocks;
                             const int dy = tap / 3 - 1, dx = tap % 3 - 1;
                             tma_load_4d_pair(a_dst, &mapA0, bar, cb * 64, g.x0 + dx, g.y0 + dy, g.img);
+                        } else {
+                            // group kb = (dy, channel block): one wide A box, B of taps (dy, -1..1)
+                            const int dyi = kb / p.cv_cblocks;
+                            const int cb = kb - dyi * p.cv_cblocks;
+                            tma_load_4d_pair(a_dst, &mapA0, bar, cb * 64, g.x0 - 1, g.y0 + dyi - 1, g.img);
+                            for (int j = 0; j < 3; ++j)
+                                tma_load_2d_pair(b_dst + j * C::B_TAP_BYTES, &mapB, bar,
+                                                 ((dyi * 3 + j) * p.cv_cblocks + cb) * 64, brow);
                         }
-                        tma_load_2d_pair(b_dst, &mapB, bar, kb * 64, brow);
+                        if (AMODE != A_CONV3W) tma_load_2d_pair(b_dst, &mapB, bar, kb * 64, brow);
                     } else {
                         if (AMODE == A_PLAIN) {
                             tma_load_2d(a_dst, &mapA0, &full[s], kb * 64, g.m_idx * 128);
@@ -779,15 +806,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(sA + s * C::A_BYTES);
                     const uint32_t b_addr = smem_u32(sB + s * C::B_BYTES);
+                    // A_CONV3W: tap dx = j - 1 reads the wide box from row j (pixel x0 + dx)
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const uint64_t ad = umma_desc_sw128(a_addr + k * 32, 16, 1024);
-                        const uint64_t bd = umma_desc_sw128(b_addr + k * 32, 16, 1024);
-                        if (CG == 2)
-                            mma_f16_ss_pair(dacc, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-                        else
-                            mma_f16_ss(dacc, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-                    }
+                    for (int j = 0; j < C::TAPS; ++j)
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            const uint64_t ad = umma_desc_sw128(a_addr + j * 128 + k * 32, 16, 1024);
+                            const uint64_t bd = umma_desc_sw128(b_addr + j * C::B_TAP_BYTES + k * 32, 16, 1024);
+                            const uint32_t acc = (kb > 0 || j > 0 || k > 0) ? 1u : 0u;
+                            if (CG == 2)
+                                mma_f16_ss_pair(dacc, ad, bd, idesc, acc);
+                            else
+                                mma_f16_ss(dacc, ad, bd, idesc, acc);
+                        }
                     if (CG == 2)
                         mma_commit_pair_both(&empty[s]);
                     else
@@ -835,7 +866,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tc_fence_after();
             if (g.live) {
                 const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * C::ACC_COLS;
-                const Head4Sync h4{head4_part, h4_full, h4_empty, abort_flag, h4count++};
+                const Head4Sync h4{head4_part, head4_wts, h4_full, h4_empty, abort_flag, h4count++};
                 epilogue_tile<T, BN, AMODE, EPI>(p, g, tacc, r, grp, h4, st, pre, maps);
             }
             tc_fence_before();

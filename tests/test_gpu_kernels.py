@@ -76,6 +76,8 @@ def _conv3_ref(x, w, b):
     (1, 12, 12, 96, 256, 256),    # channels padded to 128; w = 12 -> 4-wide boxes
     (2, 5, 32, 192, 128, 128),    # h not a multiple of the box height
     (1, 16, 128, 128, 128, 128),
+    (2, 3, 256, 64, 128, 128),    # 128-pixel row tiles: wide-box taps on CTA pairs, borders
+    (1, 5, 384, 192, 128, 128),
 ])
 def test_conv3_matches_fp64(lib, n, h, wd, c, cout, bn, dtype, pair):
     from mast3r_runtime_b200 import _lib
