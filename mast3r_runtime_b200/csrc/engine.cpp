@@ -190,6 +190,7 @@ public:
     Lin dec_embed;
     std::vector<DecBlock> dec[2];
     Norm dec_norm;
+    Norm unit_norm;  // gamma 1, beta 0 (decoder width): norm_y without its affine part
     Head head[2];
     float* rope_cos = nullptr;
     float* rope_sin = nullptr;
@@ -495,11 +496,14 @@ public:
         const int Dd = d.dec_dim;
         linear("dec.embed", enc_out, T, dec_embed, EPI_F32, encp, Dd);
         M3R_CUDA(cudaMemcpyAsync(xdec, encp, sizeof(float) * T * Dd, cudaMemcpyDeviceToDevice, stream_));
+        // normalised projected encoder output of both views (norm_y's affine part lives
+        // in the K/V projection weights)
+        ln("dec.ln", encp, T, Dd, unit_norm, yn);
         for (int i = 0; i < d.dec_depth; ++i) {
             for (int view = 0; view < 2; ++view) {
                 const DecBlock& B = dec[view][i];
                 float* xv = xdec + view * Tv * Dd;
-                const float* yo = encp + (1 - view) * Tv * Dd;
+                const uint16_t* yno = yn + (1 - view) * Tv * Dd;  // the other view
                 uint16_t* xnv = xn + view * Tv * Dd;
                 uint16_t* aov = ao + view * Tv * Dd;
                 // self attention
@@ -510,8 +514,7 @@ public:
                 // cross attention: queries from this view, keys/values from the other view's projected encoder output
                 ln("dec.ln", xv, Tv, Dd, B.n2, xnv);
                 linear_heads("dec.q", xnv, Tv, B.q, Dd, q, 1, nullptr, 0, nullptr, 0);
-                ln("dec.ln", yo, Tv, Dd, B.ny, yn);
-                linear_heads("dec.kv", yn, Tv, B.kv, Dd, k, 1, v, 0, nullptr, 0);
+                linear_heads("dec.kv", yno, Tv, B.kv, Dd, k, 1, v, 0, nullptr, 0);
                 attn("dec.attn_cross", q, k, v, aov, n, d.dec_heads);
                 linear("dec.cproj", aov, Tv, B.cproj, EPI_F32_RESID, xv, Dd, ACT_NONE, xv);
                 // MLP
@@ -728,6 +731,18 @@ void Engine::load(const std::string& path) {
                 auto bv = V(b + "cross_attn.projv.bias", Dd);
                 wk.insert(wk.end(), wv.begin(), wv.end());
                 bk.insert(bk.end(), bv.begin(), bv.end());
+                // norm_y's affine part folded into the K/V projection:
+                //   (yhat * g + beta) W^T + b = yhat (W diag(g))^T + (b + W beta),
+                // so the normalisation yhat of the other view's projected encoder output
+                // (the same input for every block) is computed once per pass
+                const std::vector<float>& gy = e.n[4];
+                const std::vector<float>& by = e.n[5];
+                for (int o = 0; o < 2 * Dd; ++o) {
+                    double acc = bk[o];
+                    for (int i = 0; i < Dd; ++i) acc += static_cast<double>(wk[static_cast<size_t>(o) * Dd + i]) * by[i];
+                    bk[o] = static_cast<float>(acc);
+                    for (int i = 0; i < Dd; ++i) wk[static_cast<size_t>(o) * Dd + i] *= gy[i];
+                }
                 e.kv = to16(dt, wk, 2 * Dd, Dd, bk);
             }
             e.cproj = L(b + "cross_attn.proj", Dd, Dd);
@@ -820,7 +835,6 @@ void Engine::load(const std::string& path) {
                 DecBlock& B = D.dec[view][i];
                 B.n1 = D.upload_norm(e.n[0], e.n[1]);
                 B.n2 = D.upload_norm(e.n[2], e.n[3]);
-                B.ny = D.upload_norm(e.n[4], e.n[5]);
                 B.n3 = D.upload_norm(e.n[6], e.n[7]);
                 B.qkv = D.upload(e.qkv);
                 B.proj = D.upload(e.proj);
@@ -832,6 +846,7 @@ void Engine::load(const std::string& path) {
             }
         }
         D.dec_norm = D.upload_norm(dng, dnb);
+        D.unit_norm = D.upload_norm(std::vector<float>(Dd, 1.0f), std::vector<float>(Dd, 0.0f));
         for (int view = 0; view < 2; ++view) {
             const HostHead& H = hh[view];
             Head& O = D.head[view];

@@ -39,7 +39,7 @@ struct EncBlock {
     Lin qkv, proj, fc1, fc2;
 };
 struct DecBlock {
-    Norm n1, n2, ny, n3;
+    Norm n1, n2, n3;  // norm_y is folded into kv (Engine::load)
     Lin qkv, proj, q, kv, cproj, fc1, fc2;
 };
 struct Head {
