@@ -282,7 +282,8 @@ def run_ours(args):
         p1[...] = img1
         p2[...] = img2
         outs = eng._out_arrays(per, alloc=_lib.pinned_empty)
-        eng.infer_batch(p1, p2, out=outs)
+        for _ in range(2):  # direct launches, then CUDA-graph capture of the sub-batch passes
+            eng.infer_batch(p1, p2, out=outs)
         barrier()
         t0 = time.perf_counter()
         for _ in range(args.steps):

@@ -15,6 +15,7 @@
 #include <algorithm>
 #include <array>
 #include <map>
+#include <mutex>
 #include <cstdio>
 #include <chrono>
 #include <cmath>
@@ -140,6 +141,7 @@ public:
     Device(int dev, const Dims& d, int max_pairs) : dev_(dev), d_(d), max_pairs_(max_pairs) {
         DeviceGuard g(dev_);
         M3R_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+        M3R_CUDA(cudaStreamCreateWithFlags(&copy_stream_, cudaStreamNonBlocking));
         err_ = static_cast<int*>(alloc(sizeof(int)));
         M3R_CUDA(cudaMemset(err_, 0, sizeof(int)));
         for (int i = 0; i < 8; ++i) M3R_CUDA(cudaEventCreate(&stage_ev_[i]));
@@ -153,6 +155,11 @@ public:
                 if (e) cudaGraphExecDestroy(e);
         for (auto& e : prof_ev_) cudaEventDestroy(e);
         for (int i = 0; i < 8; ++i) cudaEventDestroy(stage_ev_[i]);
+        for (auto& e : chunk_ev_) cudaEventDestroy(e);
+        if (copy_stream_) {
+            cudaStreamSynchronize(copy_stream_);
+            cudaStreamDestroy(copy_stream_);
+        }
         for (void* p : allocs_) cudaFree(p);
         if (stream_) cudaStreamDestroy(stream_);
     }
@@ -390,46 +397,56 @@ public:
     }
 
     // ------------------------------------------------------------ forward
-    // One forward pass over the n staged pairs, in four stages (patch embedding,
-    // encoder, decoder, heads) with a timing event before and after each.  The first
-    // pass for a given n launches directly (it also sets the kernels' attributes);
-    // later passes replay one CUDA graph per stage, captured on the second pass.
-    // Profiled passes always launch directly (events around every launch).
+    // One forward pass over n pairs whose images sit in input slots [slot, slot + n)
+    // and whose outputs go to output slots [slot, slot + n), in four stages (patch
+    // embedding, encoder, decoder, heads) with a timing event (ev[0..4]) before and
+    // after each.  The first pass for a given (n, slot) launches directly (it also sets
+    // the kernels' attributes); later passes replay one CUDA graph per stage, captured
+    // on the second pass.  Profiled passes always launch directly (events around every
+    // launch).  enqueue_forward only enqueues; forward also waits and reads the timings.
     static constexpr int kStages = 4;
-    void forward(int n, float* stage_ms) {
+    void enqueue_forward(int n, int slot, const cudaEvent_t* ev) {
         DeviceGuard g(dev_);
         profiling_reset();
-        const bool use_graph = !profiling && direct_runs_[n]++ > 0;
-        auto& gs = graphs_[n];
-        M3R_CUDA(cudaEventRecord(stage_ev_[0], stream_));
+        const std::pair<int, int> key(n, slot);
+        const bool use_graph = !profiling && direct_runs_[key]++ > 0;
+        auto& gs = graphs_[key];
+        M3R_CUDA(cudaEventRecord(ev[0], stream_));
         for (int st = 0; st < kStages; ++st) {
             if (!use_graph) {
-                enqueue_stage(st, n);
+                enqueue_stage(st, n, slot);
             } else {
-                if (gs[st] == nullptr) gs[st] = capture_stage(st, n);
+                if (gs[st] == nullptr) gs[st] = capture_stage(st, n, slot);
                 M3R_CUDA(cudaGraphLaunch(gs[st], stream_));
             }
-            M3R_CUDA(cudaEventRecord(stage_ev_[st + 1], stream_));
-        }
-        M3R_CUDA(cudaStreamSynchronize(stream_));
-        check_error();
-        if (profiling) collect_profile();
-        if (stage_ms) {
-            float ms;
-            for (int i = 0; i < kStages; ++i) {
-                M3R_CUDA(cudaEventElapsedTime(&ms, stage_ev_[i], stage_ev_[i + 1]));
-                stage_ms[i] = ms;
-            }
-            M3R_CUDA(cudaEventElapsedTime(&ms, stage_ev_[0], stage_ev_[kStages]));
-            stage_ms[kStages] = ms;
+            M3R_CUDA(cudaEventRecord(ev[st + 1], stream_));
         }
     }
 
-    cudaGraphExec_t capture_stage(int st, int n) {
+    // stage_ms[0..3] per stage, stage_ms[4] whole pass, from events ev[0..4]
+    static void stage_times(const cudaEvent_t* ev, float* stage_ms) {
+        float ms;
+        for (int i = 0; i < kStages; ++i) {
+            M3R_CUDA(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
+            stage_ms[i] = ms;
+        }
+        M3R_CUDA(cudaEventElapsedTime(&ms, ev[0], ev[kStages]));
+        stage_ms[kStages] = ms;
+    }
+
+    void forward(int n, float* stage_ms) {
+        enqueue_forward(n, 0, stage_ev_);
+        M3R_CUDA(cudaStreamSynchronize(stream_));
+        check_error();
+        if (profiling) collect_profile();
+        if (stage_ms) stage_times(stage_ev_, stage_ms);
+    }
+
+    cudaGraphExec_t capture_stage(int st, int n, int slot) {
         cudaGraph_t graph = nullptr;
         M3R_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
         try {
-            enqueue_stage(st, n);
+            enqueue_stage(st, n, slot);
         } catch (...) {
             cudaStreamEndCapture(stream_, &graph);
             if (graph) cudaGraphDestroy(graph);
@@ -443,23 +460,35 @@ public:
         return exec;
     }
 
+    // Slot layout of the inputs and outputs: view v of the pair in slot s is image /
+    // output v * max_pairs + s, so sub-batches in different slots never overlap.
+    uint8_t* img_slot(int view, int slot) const {
+        return img + (static_cast<size_t>(view) * max_pairs_ + slot) * d_.H * d_.W * 3;
+    }
+    float* out_slot(const float* base, int per_pixel, int view, int slot) const {
+        return const_cast<float*>(base) + (static_cast<size_t>(view) * max_pairs_ + slot) * d_.H * d_.W * per_pixel;
+    }
+
     // Enqueues every launch of stage st of one forward pass on the device's stream.
-    void enqueue_stage(int st, int n) {
+    void enqueue_stage(int st, int n, int slot) {
         switch (st) {
-            case 0: stage_patch(n); break;
+            case 0: stage_patch(n, slot); break;
             case 1: stage_encoder(n); break;
             case 2: stage_decoder(n); break;
             default:
                 // heads, one view at a time (downstream_head1 / downstream_head2)
-                for (int view = 0; view < 2; ++view) heads(view, n);
+                for (int view = 0; view < 2; ++view) heads(view, n, slot);
         }
     }
 
     // patch embedding (+ ImageNet normalisation fused into the im2col)
-    void stage_patch(int n) {
+    void stage_patch(int n, int slot) {
         const Dims& d = d_;
         const long long T = 2LL * n * d.ntok;
-        launch(kOther, 0, "patch.im2col", [&] { patch_im2col(stream_, d_.dt, img, 2 * n, d.H, d.W, d.patch, d.kpad, patches); });
+        launch(kOther, 0, "patch.im2col", [&] {
+            patch_im2col(stream_, d_.dt, img_slot(0, slot), img_slot(1, slot), n, 2 * n, d.H, d.W, d.patch, d.kpad,
+                         patches);
+        });
         GemmParams p = gp();
         p.bias = patch.b;
         p.out = xenc;
@@ -528,7 +557,7 @@ public:
         ln("dec.ln", xdec, T, Dd, dec_norm, dec_out);
     }
 
-    void heads(int view, int n) {
+    void heads(int view, int n, int slot) {
         const Dims& d = d_;
         const Head& Hh = head[view];
         const long long N = d.ntok, Tv = static_cast<long long>(n) * N;
@@ -583,8 +612,8 @@ public:
         conv3("head.conv0", up1, n, 2 * H0, 2 * W0, 256, Hh.hd0, EPI_BF16, hd0, ACT_RELU, 128);
         launch(kOther, 0, "head.resize", [&] { resize16(stream_, d_.dt, hd0, n, 2 * H0, 2 * W0, 128, 4 * H0, 4 * W0, up2); });
         conv3("head.conv_out", up2, n, 4 * H0, 4 * W0, 128, Hh.hd2, EPI_HEAD4, out4, ACT_RELU, 128, Hh.w4, Hh.b4);
-        float* pts = o_pts + static_cast<long long>(view) * n * d.H * d.W * 3;
-        float* conf = o_conf + static_cast<long long>(view) * n * d.H * d.W;
+        float* pts = out_slot(o_pts, 3, view, slot);
+        float* conf = out_slot(o_conf, 1, view, slot);
         launch(kOther, 0, "head.split", [&] { head_split(stream_, out4, n, 4 * H0, 4 * W0, d.H, d.W, pts, conf); });
 
         // local features (mpsgraph_engine.mm:425-437): MLP(enc || dec) -> pixel shuffle -> L2 norm
@@ -602,7 +631,7 @@ public:
         {
             GemmParams p = gp();
             p.bias = Hh.lf2.b;
-            p.out = o_desc + static_cast<long long>(view) * n * d.H * d.W * d.desc_dim;
+            p.out = out_slot(o_desc, d.desc_dim, view, slot);
             p.n_tok = d.ntok;
             p.grid_w = wg;
             p.grid_h = hg;
@@ -612,6 +641,78 @@ public:
                 gemm_rows(stream_, d_.dt, bn, EPI_DESC, lf1, d.lf_hidden, static_cast<int>(Tv), d.lf_hidden, Hh.lf2.w, d.lf_hidden, Hh.lf2.out, p);
             });
         }
+    }
+
+    // Whole inference of n pairs on this device with host buffers: the pairs run in
+    // sub-batches (input / output slots k * c), all inputs are copied in first on the
+    // copy stream, and each sub-batch's outputs are copied back there as soon as its
+    // heads are done, overlapping the next sub-batch's compute.  outs[] point at this
+    // device's first pair.  stage_ms[5] (summed over sub-batches), *h2d_ms (input
+    // copies), *d2h_ms (output copies, summed) are device times.  Afterwards the input
+    // slots hold these n pairs, as after stage().
+    static constexpr int kChunkEvents = 8;
+    void infer_pipelined(const uint8_t* img1, const uint8_t* img2, int n, float* const outs[6], float* stage_ms,
+                         float* h2d_ms, float* d2h_ms) {
+        DeviceGuard g(dev_);
+        M3R_REQUIRE(n >= 1 && n <= max_pairs_, "infer: pair count out of range for this device");
+        const int nsub = n >= 32 ? 4 : (n >= 16 ? 2 : 1);
+        const int c = (n + nsub - 1) / nsub;
+        while (chunk_ev_.size() < static_cast<size_t>(kChunkEvents * nsub + 1)) {
+            cudaEvent_t e;
+            M3R_CUDA(cudaEventCreate(&e));
+            chunk_ev_.push_back(e);
+        }
+        auto ev = [&](int k, int i) { return chunk_ev_[1 + k * kChunkEvents + i]; };  // i: 0-4 stages, 5 in, 6-7 out
+        const size_t ib = static_cast<size_t>(d_.H) * d_.W * 3;
+        const size_t px = static_cast<size_t>(d_.H) * d_.W;
+        const int per_px[3] = {3, d_.desc_dim, 1};
+        const float* bases[3] = {o_pts, o_desc, o_conf};
+        const bool prof = profiling;
+        profiling = false;  // per-launch profiling is a run_resident feature
+        M3R_CUDA(cudaEventRecord(chunk_ev_[0], copy_stream_));
+        for (int k = 0; k < nsub; ++k) {
+            const int slot = k * c, nk = std::min(c, n - slot);
+            if (nk <= 0) break;
+            M3R_CUDA(cudaMemcpyAsync(img_slot(0, slot), img1 + slot * ib, nk * ib, cudaMemcpyHostToDevice, copy_stream_));
+            M3R_CUDA(cudaMemcpyAsync(img_slot(1, slot), img2 + slot * ib, nk * ib, cudaMemcpyHostToDevice, copy_stream_));
+            M3R_CUDA(cudaEventRecord(ev(k, 5), copy_stream_));
+        }
+        int last = 0;
+        for (int k = 0; k < nsub; ++k) {
+            const int slot = k * c, nk = std::min(c, n - slot);
+            if (nk <= 0) break;
+            last = k;
+            M3R_CUDA(cudaStreamWaitEvent(stream_, ev(k, 5), 0));
+            const cudaEvent_t sev[5] = {ev(k, 0), ev(k, 1), ev(k, 2), ev(k, 3), ev(k, 4)};
+            enqueue_forward(nk, slot, sev);
+            M3R_CUDA(cudaStreamWaitEvent(copy_stream_, ev(k, 4), 0));
+            M3R_CUDA(cudaEventRecord(ev(k, 6), copy_stream_));
+            for (int kind = 0; kind < 3; ++kind)
+                for (int view = 0; view < 2; ++view) {
+                    float* dst = outs[2 * kind + view];
+                    if (!dst) continue;
+                    M3R_CUDA(cudaMemcpyAsync(dst + slot * px * per_px[kind], out_slot(bases[kind], per_px[kind], view, slot),
+                                             sizeof(float) * nk * px * per_px[kind], cudaMemcpyDeviceToHost, copy_stream_));
+                }
+            M3R_CUDA(cudaEventRecord(ev(k, 7), copy_stream_));
+        }
+        profiling = prof;
+        M3R_CUDA(cudaStreamSynchronize(copy_stream_));
+        M3R_CUDA(cudaStreamSynchronize(stream_));
+        staged = n;
+        check_error();
+        for (int i = 0; i < 5; ++i) stage_ms[i] = 0.0f;
+        *d2h_ms = 0.0f;
+        for (int k = 0; k <= last; ++k) {
+            float sm[5];
+            const cudaEvent_t sev[5] = {ev(k, 0), ev(k, 1), ev(k, 2), ev(k, 3), ev(k, 4)};
+            stage_times(sev, sm);
+            for (int i = 0; i < 5; ++i) stage_ms[i] += sm[i];
+            float ms;
+            M3R_CUDA(cudaEventElapsedTime(&ms, ev(k, 6), ev(k, 7)));
+            *d2h_ms += ms;
+        }
+        M3R_CUDA(cudaEventElapsedTime(h2d_ms, chunk_ev_[0], ev(last, 5)));
     }
 
     void check_error() {
@@ -632,11 +733,13 @@ private:
     Dims d_;
     int max_pairs_;
     cudaStream_t stream_ = nullptr;
+    cudaStream_t copy_stream_ = nullptr;  // host <-> device copies of pipelined infer
+    std::vector<cudaEvent_t> chunk_ev_;   // per sub-batch: 5 stage events, input, 2 output-copy events
     int* err_ = nullptr;
     cudaEvent_t stage_ev_[8];
     std::vector<void*> allocs_;
-    std::map<int, std::array<cudaGraphExec_t, 4>> graphs_;  // forward stages per pair count
-    std::map<int, int> direct_runs_;
+    std::map<std::pair<int, int>, std::array<cudaGraphExec_t, 4>> graphs_;  // forward stages per (pairs, slot)
+    std::map<std::pair<int, int>, int> direct_runs_;
 };
 
 // ---------------------------------------------------------------------------- engine
@@ -920,9 +1023,10 @@ void Engine::stage(const uint8_t* img1, const uint8_t* img2, int n_pairs) {
         const int first = sh[i].first, cnt = sh[i].second;
         D.staged = cnt;
         if (cnt == 0) return;
-        M3R_CUDA(cudaMemcpyAsync(D.img, img1 + first * img_bytes, cnt * img_bytes, cudaMemcpyHostToDevice, D.stream()));
-        M3R_CUDA(cudaMemcpyAsync(D.img + cnt * img_bytes, img2 + first * img_bytes, cnt * img_bytes,
-                                 cudaMemcpyHostToDevice, D.stream()));
+        M3R_CUDA(cudaMemcpyAsync(D.img_slot(0, 0), img1 + first * img_bytes, cnt * img_bytes, cudaMemcpyHostToDevice,
+                                 D.stream()));
+        M3R_CUDA(cudaMemcpyAsync(D.img_slot(1, 0), img2 + first * img_bytes, cnt * img_bytes, cudaMemcpyHostToDevice,
+                                 D.stream()));
         M3R_CUDA(cudaStreamSynchronize(D.stream()));
     });
     staged_pairs_ = n_pairs;
@@ -955,14 +1059,14 @@ void Engine::fetch(int n_pairs, float* const outs[6]) {
         DeviceGuard g(D.dev());
         const int first = sh[i].first, cnt = sh[i].second;
         if (cnt == 0) return;
-        const size_t sizes[3] = {px * 3, px * static_cast<size_t>(d_.desc_dim), px};
+        const int per_px[3] = {3, d_.desc_dim, 1};
         const float* src[3] = {D.o_pts, D.o_desc, D.o_conf};
         for (int k = 0; k < 3; ++k)
             for (int view = 0; view < 2; ++view) {
                 float* dst = outs[2 * k + view];
                 if (!dst) continue;
-                M3R_CUDA(cudaMemcpyAsync(dst + first * sizes[k], src[k] + static_cast<size_t>(view) * cnt * sizes[k],
-                                         sizeof(float) * cnt * sizes[k], cudaMemcpyDeviceToHost, D.stream()));
+                M3R_CUDA(cudaMemcpyAsync(dst + first * px * per_px[k], D.out_slot(src[k], per_px[k], view, 0),
+                                         sizeof(float) * cnt * px * per_px[k], cudaMemcpyDeviceToHost, D.stream()));
             }
         M3R_CUDA(cudaStreamSynchronize(D.stream()));
     });
@@ -970,39 +1074,50 @@ void Engine::fetch(int n_pairs, float* const outs[6]) {
 
 void Engine::infer(const uint8_t* img1, const uint8_t* img2, int n_pairs, float* const outs[6], float* timing) {
     if (!ready_) throw Error(kErrState, "engine is not loaded");
+    M3R_REQUIRE(n_pairs >= 1, "n_pairs must be >= 1");
     const auto t0 = std::chrono::steady_clock::now();
     float st[5] = {0, 0, 0, 0, 0};
-    double h2d = 0, d2h = 0, dev = 0;
-    // launch in chunks of max_pairs per device
+    float h2d = 0, d2h = 0;
+    std::mutex mu;
+    const size_t ib = static_cast<size_t>(d_.H) * d_.W * 3;
+    const size_t px = static_cast<size_t>(d_.H) * d_.W;
+    const int per_px[3] = {3, d_.desc_dim, 1};
+    // launches of up to max_pairs per device; every device pipelines its share
+    // (sub-batches whose output copies overlap the next sub-batch's compute)
     const int per_launch = cfg_.max_pairs * static_cast<int>(devs_.size());
     for (int first = 0; first < n_pairs; first += per_launch) {
         const int cnt = std::min(per_launch, n_pairs - first);
-        const size_t ib = static_cast<size_t>(d_.H) * d_.W * 3;
-        const size_t px = static_cast<size_t>(d_.H) * d_.W;
-        auto a = std::chrono::steady_clock::now();
-        stage(img1 + first * ib, img2 + first * ib, cnt);
-        auto b = std::chrono::steady_clock::now();
-        float cs[5];
-        dev += run_resident(cnt, cs);
-        for (int k = 0; k < 5; ++k) st[k] += cs[k];
-        auto c = std::chrono::steady_clock::now();
-        float* o[6] = {outs[0] ? outs[0] + first * px * 3 : nullptr, outs[1] ? outs[1] + first * px * 3 : nullptr,
-                       outs[2] ? outs[2] + first * px * d_.desc_dim : nullptr,
-                       outs[3] ? outs[3] + first * px * d_.desc_dim : nullptr, outs[4] ? outs[4] + first * px : nullptr,
-                       outs[5] ? outs[5] + first * px : nullptr};
-        fetch(cnt, o);
-        auto e = std::chrono::steady_clock::now();
-        h2d += std::chrono::duration<double, std::milli>(b - a).count();
-        d2h += std::chrono::duration<double, std::milli>(e - c).count();
+        const auto sh = shards(cnt);
+        float launch_st[5] = {0, 0, 0, 0, 0}, launch_h2d = 0, launch_d2h = 0;
+        for_each_device(devs_.size(), [&](size_t i) {
+            const int f = first + sh[i].first, c = sh[i].second;
+            devs_[i]->staged = c;
+            if (c == 0) return;
+            float* o[6];
+            for (int k = 0; k < 3; ++k)
+                for (int view = 0; view < 2; ++view)
+                    o[2 * k + view] = outs[2 * k + view] ? outs[2 * k + view] + f * px * per_px[k] : nullptr;
+            float sm[5], hm = 0, dm = 0;
+            devs_[i]->infer_pipelined(img1 + f * ib, img2 + f * ib, c, o, sm, &hm, &dm);
+            std::lock_guard<std::mutex> lk(mu);  // the slowest device sets the launch's times
+            if (sm[4] >= launch_st[4])
+                for (int k = 0; k < 5; ++k) launch_st[k] = sm[k];
+            launch_h2d = std::max(launch_h2d, hm);
+            launch_d2h = std::max(launch_d2h, dm);
+        });
+        for (int k = 0; k < 5; ++k) st[k] += launch_st[k];
+        h2d += launch_h2d;
+        d2h += launch_d2h;
+        staged_pairs_ = cnt;  // the input slots hold this launch's pairs, as after stage()
     }
     if (timing) {
         timing[M3R_T_PREPROCESS] = st[0];
         timing[M3R_T_ENCODER] = st[1];
         timing[M3R_T_DECODER] = st[2];
         timing[M3R_T_HEADS] = st[3];
-        timing[M3R_T_H2D] = static_cast<float>(h2d);
-        timing[M3R_T_D2H] = static_cast<float>(d2h);
-        timing[M3R_T_INFERENCE] = static_cast<float>(dev);
+        timing[M3R_T_H2D] = h2d;
+        timing[M3R_T_D2H] = d2h;
+        timing[M3R_T_INFERENCE] = st[4];
         timing[M3R_T_TOTAL] =
             static_cast<float>(std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count());
     }

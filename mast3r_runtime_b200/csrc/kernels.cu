@@ -15,8 +15,8 @@ inline int grid_for(long long n, int block) {
 }
 
 template <class T>
-__global__ void patch_im2col_kernel(const uint8_t* __restrict__ img, int n, int H, int W, int p, int kpad,
-                                    T* __restrict__ out) {
+__global__ void patch_im2col_kernel(const uint8_t* __restrict__ img_a, const uint8_t* __restrict__ img_b, int na,
+                                    int n, int H, int W, int p, int kpad, T* __restrict__ out) {
     const int hg = H / p, wg = W / p;
     const long long total = static_cast<long long>(n) * hg * wg * kpad;
     const float mean[3] = {0.485f, 0.456f, 0.406f};
@@ -33,7 +33,9 @@ __global__ void patch_im2col_kernel(const uint8_t* __restrict__ img, int n, int 
             const int im = static_cast<int>(row / (hg * wg));
             const int t = static_cast<int>(row - static_cast<long long>(im) * hg * wg);
             const int gy = t / wg, gx = t - (t / wg) * wg;
-            const uint8_t u = img[((static_cast<long long>(im) * H + gy * p + ky) * W + gx * p + kx) * 3 + c];
+            const uint8_t* img = im < na ? img_a + static_cast<long long>(im) * H * W * 3
+                                         : img_b + static_cast<long long>(im - na) * H * W * 3;
+            const uint8_t u = img[(static_cast<long long>(gy * p + ky) * W + gx * p + kx) * 3 + c];
             v = (static_cast<float>(u) / 255.0f - mean[c]) / stdv[c];
         }
         out[e] = Elem<T>::from(v);
@@ -314,9 +316,11 @@ __global__ void head_split_kernel(const float* __restrict__ o4, int n, int h4, i
 
 }  // namespace
 
-void patch_im2col(cudaStream_t s, int dt, const uint8_t* img, int n, int H, int W, int p, int kpad, void* out) {
+void patch_im2col(cudaStream_t s, int dt, const uint8_t* img_a, const uint8_t* img_b, int na, int n, int H, int W,
+                  int p, int kpad, void* out) {
     const long long total = static_cast<long long>(n) * (H / p) * (W / p) * kpad;
-    M3R_BY_DT(dt, patch_im2col_kernel<T><<<grid_for(total, 256), 256, 0, s>>>(img, n, H, W, p, kpad, static_cast<T*>(out)));
+    M3R_BY_DT(dt, patch_im2col_kernel<T><<<grid_for(total, 256), 256, 0, s>>>(img_a, img_b, na, n, H, W, p, kpad,
+                                                                                  static_cast<T*>(out)));
     M3R_CUDA(cudaGetLastError());
 }
 

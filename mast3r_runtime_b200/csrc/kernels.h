@@ -9,7 +9,9 @@ namespace m3r {
 
 // uint8 [n, H, W, 3] -> patch rows [n * (H/p) * (W/p), kpad]; column c*p*p + ky*p + kx,
 // value (x/255 - mean_c) / std_c (python_engine.py:176-188), zero in [3*p*p, kpad).
-void patch_im2col(cudaStream_t s, int dt, const uint8_t* img, int n, int H, int W, int p, int kpad, void* out);
+// images [0, na) from img_a, [na, n) from img_b (u8 HWC each); rows of 3 p^2 values padded to kpad
+void patch_im2col(cudaStream_t s, int dt, const uint8_t* img_a, const uint8_t* img_b, int na, int n, int H, int W,
+                  int p, int kpad, void* out);
 
 // y = LayerNorm(x) * gamma + beta (eps 1e-6), x fp32 [rows, D], y 16-bit [rows, D].
 void layernorm(cudaStream_t s, int dt, const float* x, int rows, int D, const float* gamma, const float* beta, void* y);
