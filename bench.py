@@ -42,6 +42,12 @@ def env_rank():
             int(os.environ.get("WORLD_SIZE", "1")))
 
 
+# DRAM bytes (read + write) per token row of the encoder fc1 launch (K 1024 -> N 4096, GELU,
+# 16-bit output), from an ncu capture of that launch at 16 pairs (24576 rows: 58.8 MB read +
+# 147.7 MB written); traffic grows with the rows, so a launch moves this many bytes per row.
+FC1_DRAM_BYTES_PER_ROW = (58836992 + 147696128) / 24576
+
+
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -310,6 +316,9 @@ def run_ours(args):
         gemm_tf = prof["gemm_flop"] / (prof["gemm_ms"] * 1e-3) / 1e12 if prof["gemm_ms"] > 0 else 0.0
         attn_tf = prof["attn_flop"] / (prof["attn_ms"] * 1e-3) / 1e12 if prof["attn_ms"] > 0 else 0.0
         peak_tc = float(pk["bf16_tflops_sustained"])
+        fc1 = ops.get("enc.fc1", {"ms": 0.0, "flop": 0.0, "launches": 1})
+        fc1_tf = (fc1["flop"] / fc1["launches"]) / (fc1["ms"] / fc1["launches"] * 1e-3) / 1e12 if fc1["ms"] > 0 else 0.0
+        fc1_rows = 2 * per * (IMAGE_HW[0] // d.patch) * (IMAGE_HW[1] // d.patch)
         fpp = flops_per_pair(d, IMAGE_HW)
         line = {
             "metric": METRIC, "value": value, "unit": "pairs/s", "n_gpus": world, "steps": args.steps,
@@ -320,9 +329,17 @@ def run_ours(args):
                        "image": "384x512", "parallelism": f"dp{world} (pairs sharded, no collectives)",
                        "l2": f"working set per step >> L2 (activations of {per} pairs, several GB)"},
             "per_gpu": value / world,
-            "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (all GEMM/conv launches of a step)",
-                         "achieved": gemm_tf, "peak": peak_tc, "unit": "TFLOP/s", "frac": gemm_tf / peak_tc,
-                         "peak_source": f"{src} bf16_tflops_sustained", "traffic": None},
+            # the dominant kernel's largest launch: encoder fc1 (one launch per block)
+            "roofline": {"bound": "tensor", "kernel": f"gemm_tc_kernel enc.fc1 (M={fc1_rows}, N={d.enc_mlp}, "
+                                                      f"K={d.enc_dim}, GELU, CTA pairs)",
+                         "achieved": fc1_tf, "peak": peak_tc, "unit": "TFLOP/s", "frac": fc1_tf / peak_tc,
+                         "peak_source": f"{src} bf16_tflops_sustained",
+                         "traffic": FC1_DRAM_BYTES_PER_ROW * fc1_rows,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one fc1 launch at "
+                                           "16 pairs, scaled by rows"},
+            "gemm_family": {"kernel": "gemm_tc_kernel (all GEMM/conv launches of a step)", "achieved": gemm_tf,
+                            "peak": peak_tc, "unit": "TFLOP/s", "frac": gemm_tf / peak_tc,
+                            "ms_per_step": prof["gemm_ms"], "launches_per_step": int(prof["gemm_launches"])},
             "attention": {"achieved": attn_tf, "peak": peak_tc, "unit": "TFLOP/s", "frac": attn_tf / peak_tc,
                           "ms_per_step": prof["attn_ms"], "launches_per_step": int(prof["attn_launches"])},
             "model_tflops": fpp * total_pairs * args.steps / (total_ms / 1000.0) / 1e12,
