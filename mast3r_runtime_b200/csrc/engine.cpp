@@ -368,6 +368,7 @@ public:
         p.sec_rope[2] = r2;
         p.rope_cos = rope_cos;
         p.rope_sin = rope_sin;
+        p.rope_npos = std::max(d_.hg, d_.wg);
         const int b = (D % 256 == 0) ? 256 : 128;
         launch(kGemm, 2.0 * M * L.out * L.in, op,
                [&] { gemm_rows(stream_, d_.dt, b, EPI_HEADS, A, L.in, static_cast<int>(M), L.in, L.w, L.in, L.out, p); });
@@ -902,15 +903,16 @@ void Engine::load(const std::string& path) {
             H.lf2 = to16(dt, w2, groups * d.desc_dim, d.lf_hidden, b2);
         }
     }
-    // RoPE tables (rope2d.py:77-92): freq_i = 1 / 100^(i/16), angle = pos * freq_i in float32
+    // RoPE tables (rope2d.py:77-92): freq_i = 1 / 100^(i/16), angle = pos * freq_i in float32;
+    // frequency-major [16][maxpos] (the QKV epilogue reads a warp's consecutive tokens)
     const int maxpos = std::max(d.hg, d.wg);
     std::vector<float> rc(static_cast<size_t>(maxpos) * 16), rs(static_cast<size_t>(maxpos) * 16);
     for (int i = 0; i < 16; ++i) {
         const float freq = 1.0f / std::pow(100.0f, static_cast<float>(i) / 16.0f);
         for (int pos = 0; pos < maxpos; ++pos) {
             const float ang = static_cast<float>(pos) * freq;
-            rc[pos * 16 + i] = static_cast<float>(std::cos(static_cast<double>(ang)));
-            rs[pos * 16 + i] = static_cast<float>(std::sin(static_cast<double>(ang)));
+            rc[static_cast<size_t>(i) * maxpos + pos] = static_cast<float>(std::cos(static_cast<double>(ang)));
+            rs[static_cast<size_t>(i) * maxpos + pos] = static_cast<float>(std::sin(static_cast<double>(ang)));
         }
     }
 

@@ -60,8 +60,9 @@ struct GemmParams {
     int sec_len, n_tok, grid_w;
     void* sec_out[3];
     int sec_rope[3];
-    const float* rope_cos;  // [pos][16]
+    const float* rope_cos;  // [16 frequencies][rope_npos positions]
     const float* rope_sin;
+    int rope_npos;
     // EPI_DESC
     int patch, grid_h, desc_dim;
     // EPI_HEAD4
@@ -476,24 +477,18 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
             add_bias32(lo, p.bias, col0, p.N, true);
             add_bias32(hi, p.bias, col0 + 32, p.N, true);
             if (rope) {
-                // rope2d.py:133-146: pairs (i, i+32); i < 16 rotate by y*f_i, i >= 16 by x*f_(i-16)
-                const float4* cy = reinterpret_cast<const float4*>(p.rope_cos + py * 16);
-                const float4* sy = reinterpret_cast<const float4*>(p.rope_sin + py * 16);
-                const float4* cx = reinterpret_cast<const float4*>(p.rope_cos + px * 16);
-                const float4* sx = reinterpret_cast<const float4*>(p.rope_sin + px * 16);
+                // rope2d.py:133-146: pairs (i, i+32); i < 16 rotate by y*f_i, i >= 16 by x*f_(i-16).
+                // Tables are frequency-major [16][npos]: a warp's 32 rows are consecutive tokens,
+                // so their x lookups are one contiguous line and their y lookups mostly one value.
+                const float* ctab = p.rope_cos;
+                const float* stab = p.rope_sin;
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const float4 c4 = __ldg(q < 4 ? cy + q : cx + (q - 4));
-                    const float4 s4 = __ldg(q < 4 ? sy + q : sx + (q - 4));
-                    const float cc[4] = {c4.x, c4.y, c4.z, c4.w};
-                    const float ss[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int i = 4 * q + e;
-                        const float t1 = lo[i], t2 = hi[i];
-                        lo[i] = t1 * cc[e] - t2 * ss[e];
-                        hi[i] = t1 * ss[e] + t2 * cc[e];
-                    }
+                for (int i = 0; i < 32; ++i) {
+                    const int at = (i & 15) * p.rope_npos + (i < 16 ? py : px);
+                    const float cc = __ldg(ctab + at), ss = __ldg(stab + at);
+                    const float t1 = lo[i], t2 = hi[i];
+                    lo[i] = t1 * cc - t2 * ss;
+                    hi[i] = t1 * ss + t2 * cc;
                 }
             }
             uint4 o[8];
