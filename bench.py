@@ -154,6 +154,146 @@ def flops_per_pair(d, hw):
     return 2 * (enc + dec + lf + dpt)  # per view, two views
 
 
+# ---------------------------------------------------------------------------- matcher (config 4)
+MATCH_HW = (384, 512)       # one 512x384 descriptor map per set: N = 196,608
+MATCH_D = 24
+MATCH_TOP_K = 512
+MATCH_THR = 0.5
+FP32_LANES_PER_SM = 128     # FP32 lanes per SM per clock (B200: 148 SMs)
+N_SMS = 148
+
+
+def matcher_inputs(h, w, d, seed, dup_frac=0.3, sigma=0.05):
+    """Two [h, w, d] descriptor maps: set B has `dup_frac` of its rows as noisy (sigma)
+    copies of set-A rows at random positions, the rest fresh Gaussian (the matcher's
+    synthetic workload)."""
+    rng = np.random.default_rng(seed)
+    n = h * w
+    a = rng.standard_normal((n, d)).astype(np.float32)
+    b = rng.standard_normal((n, d)).astype(np.float32)
+    m = int(dup_frac * n)
+    dst = rng.permutation(n)[:m]
+    src = rng.permutation(n)[:m]
+    b[dst] = a[src] + np.float32(sigma) * rng.standard_normal((m, d)).astype(np.float32)
+    return a.reshape(h, w, d), b.reshape(h, w, d)
+
+
+def run_matcher(devices, steps, sm_mhz):
+    """engine.match at N = 196,608 x 24 (rows sharded over `devices`): device time per
+    phase (median over steps), host wall time, and a checksum of the result."""
+    import hashlib
+
+    from mast3r_runtime_b200 import NativeEngine, tiny_dims
+
+    a, b = matcher_inputs(*MATCH_HW, MATCH_D, 4)
+    eng = NativeEngine(tiny_dims(), (32, 32), devices, 1)  # the matcher needs no weights
+    r = eng.match(a, b, top_k=MATCH_TOP_K, reciprocal=True, confidence_threshold=MATCH_THR)  # warm-up
+    ph = {"normalize_ms": [], "argmax_ms": [], "select_ms": [], "kernel_ms": [], "wall_ms": []}
+    for _ in range(max(steps, 3)):
+        t0 = time.perf_counter()
+        r = eng.match(a, b, top_k=MATCH_TOP_K, reciprocal=True, confidence_threshold=MATCH_THR)
+        ph["wall_ms"].append(1000.0 * (time.perf_counter() - t0))
+        for k in ("normalize_ms", "argmax_ms", "select_ms", "kernel_ms"):
+            ph[k].append(r.timing[k])
+    eng.close()
+    med = {k: statistics.median(v) for k, v in ph.items()}
+    n = MATCH_HW[0] * MATCH_HW[1]
+    lane_ops = 2.0 * n * n * MATCH_D          # one multiply and one add per term, issued separately
+    peak = N_SMS * FP32_LANES_PER_SM * 1965e6 * len(devices)
+    argmax_rate = lane_ops / (med["argmax_ms"] * 1e-3)
+    norm_bytes = 2 * 2 * n * MATCH_D * 4       # both sets read and written
+    digest = hashlib.sha256(r.idx_1.tobytes() + r.idx_2.tobytes() + r.confidence.tobytes()).hexdigest()[:16]
+    return {
+        "workload": f"reciprocal top-{MATCH_TOP_K} matcher, N = {n} x {MATCH_D} fp32 per set, 30% noisy copies, "
+                    f"threshold {MATCH_THR}; rows of set A sharded over {len(devices)} GPU(s)",
+        "devices": len(devices), "matches": int(len(r.idx_1)), "checksum": digest,
+        "ms": med["kernel_ms"], "wall_ms": med["wall_ms"],
+        "phase_ms": {k[:-3]: med[k] for k in ("normalize_ms", "argmax_ms", "select_ms")},
+        "argmax": {"bound": "fp32 pipe", "achieved": argmax_rate / 1e12, "unit": "T lane-ops/s",
+                   "peak": peak / 1e12, "frac": argmax_rate / peak,
+                   "work": f"{lane_ops:.4g} lane-ops (N^2 D multiplies + N^2 D adds, not fused: the "
+                           f"reference's rounding)",
+                   "peak_source": f"nominal {N_SMS} SMs x {FP32_LANES_PER_SM} FP32 lanes x 1965 MHz per GPU"
+                                  + (f"; median SM clock under load {sm_mhz:.0f} MHz" if sm_mhz else "")},
+        "normalize": {"bound": "hbm", "bytes": norm_bytes,
+                      "achieved_gbs": norm_bytes / (med["normalize_ms"] * 1e-3) / 1e9},
+    }
+
+
+def cpu_baseline_matcher(rows=32768):
+    """The oracle's matcher (oracle/matcher.c, OpenMP on all host cores) on `rows` rows of
+    set A against all of set B, extrapolated to the full N x N arg-max."""
+    import oracle
+
+    a, b = matcher_inputs(*MATCH_HW, MATCH_D, 4)
+    n = MATCH_HW[0] * MATCH_HW[1]
+    an = oracle.normalize(a.reshape(n, MATCH_D))
+    bn = oracle.normalize(b.reshape(n, MATCH_D))
+    t0 = time.perf_counter()
+    oracle.argmax(an, bn, 0, rows)
+    t = time.perf_counter() - t0
+    return {"value": t * n / rows * 1000.0, "unit": "ms per match (arg-max, extrapolated)", "cores": oracle.cpu_count(),
+            "kind": "port", "sample": f"oracle/matcher.c arg-max of {rows} of {n} rows against all {n} columns "
+                                      f"({t:.1f} s), scaled by {n / rows:.0f}"}
+
+
+# ---------------------------------------------------------------------------- isolated attention (config 1)
+ATT_SEQS, ATT_HEADS, ATT_TOK = 128, 12, 576   # 64 pairs x 2 views, 24 x 24 grid, head dim 64
+
+
+def run_attention(dtype, iters=20):
+    """m3r_attention_fwd on [128 seqs, 12 heads, 576, 64] Q/K/V ~ N(0, 1): self (K, V of the
+    same view) and cross (K, V of the other view of the pair); mean kernel time per launch."""
+    import ctypes
+
+    from mast3r_runtime_b200 import _lib
+
+    lib = _lib.load()
+    rng = np.random.default_rng(9)
+    shape = (ATT_SEQS, ATT_HEADS, ATT_TOK, 64)
+
+    def bits(x):
+        if dtype == _lib.DTYPE_F16:
+            return x.astype(np.float16).view(np.uint16)
+        u = x.astype(np.float32).view(np.uint32).astype(np.uint64)
+        return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+    q = bits(rng.standard_normal(shape, dtype=np.float32))
+    k = bits(rng.standard_normal(shape, dtype=np.float32))
+    v = bits(rng.standard_normal(shape, dtype=np.float32))
+    other = np.concatenate([np.arange(64, 128), np.arange(0, 64)])  # view 1 <-> view 2 of each pair
+    kc, vc = np.ascontiguousarray(k[other]), np.ascontiguousarray(v[other])
+    out = np.empty((ATT_SEQS, ATT_TOK, ATT_HEADS * 64), np.uint16)
+    flop = 4.0 * ATT_TOK * ATT_TOK * 64 * ATT_SEQS * ATT_HEADS
+    res = {}
+    for name, kk, vv in (("self", k, v), ("cross", kc, vc)):
+        ms = ctypes.c_float(0)
+        _lib.check(lib.m3r_attention_fwd(0, dtype, _lib.ptr(q), _lib.ptr(kk), _lib.ptr(vv), _lib.ptr(out), ATT_SEQS,
+                                         ATT_HEADS, ATT_TOK, ATT_TOK, 0.125, iters, ctypes.byref(ms)))
+        res[name] = {"ms": ms.value, "tflops": flop / (ms.value * 1e-3) / 1e12}
+    return flop, res
+
+
+def cpu_baseline_attention(slices=24):
+    """The reference's own multi_head_attention (csrc/cpu/attention.cpp, OpenMP, compiled into
+    oracle/_ref) on `slices` of the 1536 (sequence, head) slices; GFLOP/s of that sample."""
+    import oracle
+
+    L = oracle.ref_lib()
+    if L is None:
+        return None
+    rng = np.random.default_rng(9)
+    q, k, v = (rng.standard_normal((1, slices, ATT_TOK, 64), dtype=np.float32) for _ in range(3))
+    o = np.empty_like(q)
+    t0 = time.perf_counter()
+    L.ref_multi_head_attention(q, k, v, o, 1, slices, ATT_TOK, 64)
+    t = time.perf_counter() - t0
+    flop = 4.0 * ATT_TOK * ATT_TOK * 64 * slices
+    return {"value": flop / t / 1e9, "unit": "GFLOP/s", "cores": oracle.cpu_count(), "kind": "reference",
+            "sample": f"{slices} of 1536 (sequence, head) slices through the reference's multi_head_attention "
+                      f"(oracle/_ref), {t:.1f} s"}
+
+
 def cpu_baseline_port(dims, hw, n_pairs=1, budget_s=60.0):
     """The oracle (numpy float32, all host cores) on one pair: a bounded sample of the workload."""
     from mast3r_runtime_b200 import make_weights
@@ -221,8 +361,6 @@ def run_reference(args):
 
 
 def run_ours(args):
-    import ctypes  # noqa: F401
-
     rank, local_rank, world = env_rank()
     dist = None
     if world > 1:
@@ -256,31 +394,44 @@ def run_ours(args):
     total_pairs = args.pairs
     per = total_pairs // world
     assert per * world == total_pairs, "global batch must divide over the GPUs"
+    dtypes = {"fp16": _lib.DTYPE_F16, "bf16": _lib.DTYPE_BF16}
+    main_dt = dtypes[args.dtype]
     path = weights_file(d, rank, dist)
-    eng = NativeEngine(d, IMAGE_HW, [local_rank], per)
-    eng.load(str(path))
     img1, img2 = make_inputs(rank * per, per, IMAGE_HW)
 
-    # ---------------- device-resident throughput (value)
-    eng.stage(img1, img2)
-    for _ in range(args.warmup):
+    def resident(eng, sample_clocks):
+        """W warm-up + K timed resident passes; (device ms summed over K, max over ranks), wall s, clocks."""
+        eng.stage(img1, img2)
+        for _ in range(args.warmup):
+            eng.run_resident(per)
+        barrier()
+        clocks = ClockSampler() if sample_clocks else None
+        if clocks:
+            clocks.start()
+        dev_ms = []
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            dev_ms.append(eng.run_resident(per))
+        wall = time.perf_counter() - t0
+        barrier()
+        clk = clocks.stop() if clocks else None
+        return allmax(sum(dev_ms)), allmax(wall), clk
+
+    def profiled(eng):
+        """One untimed resident pass with CUDA events around every launch."""
+        eng.set_profiling(True)
         eng.run_resident(per)
-    barrier()
-    clocks = ClockSampler() if rank == 0 else None
-    if clocks:
-        clocks.start()
-    dev_ms = []
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        dev_ms.append(eng.run_resident(per))
-    wall = time.perf_counter() - t0
-    barrier()
-    clk = clocks.stop() if clocks else None
-    total_ms = allmax(sum(dev_ms))
-    wall = allmax(wall)
+        prof, ops = eng.profile(), eng.profile_ops()
+        eng.set_profiling(False)
+        return prof, ops
+
+    # ---------------- device-resident throughput (value), operand type of the headline
+    eng = NativeEngine(d, IMAGE_HW, [local_rank], per, main_dt)
+    eng.load(str(path))
+    total_ms, wall, clk = resident(eng, rank == 0)
     value = total_pairs * args.steps / (total_ms / 1000.0)
 
-    # ---------------- end to end through the public batch API (pinned host buffers)
+    # ---------------- end to end through the public batch API
     e2e_line = None
     if not args.no_e2e:
         p1 = _lib.pinned_empty(img1.shape, np.uint8)
@@ -291,39 +442,89 @@ def run_ours(args):
         for _ in range(2):  # direct launches, then CUDA-graph capture of the sub-batch passes
             eng.infer_batch(p1, p2, out=outs)
         barrier()
+        h2d, d2h = [], []
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            eng.infer_batch(p1, p2, out=outs)
+            _, tm = eng.infer_batch(p1, p2, out=outs)
+            h2d.append(tm["h2d_ms"])
+            d2h.append(tm["d2h_ms"])
         e2e_s = allmax(time.perf_counter() - t0)
+        out_bytes = int(sum(o.nbytes for o in outs.values()))
         e2e_line = {"value": total_pairs * args.steps / e2e_s, "unit": "pairs/s",
                     "h2d_bytes_per_step": int(p1.nbytes + p2.nbytes) * world,
-                    "d2h_bytes_per_step": int(sum(o.nbytes for o in outs.values())) * world}
-
-    # ---------------- per-kernel-family device time (untimed run, events around every launch)
-    eng.set_profiling(True)
-    eng.run_resident(per)
-    prof = eng.profile()
-    ops = eng.profile_ops()
-    eng.set_profiling(False)
+                    "d2h_bytes_per_step": out_bytes * world,
+                    "host_buffers": "pinned (m3r_host_alloc)",
+                    "rank0_h2d_ms": statistics.median(h2d), "rank0_d2h_ms": statistics.median(d2h),
+                    "rank0_d2h_gbs": out_bytes / (statistics.median(d2h) * 1e-3) / 1e9 if d2h[0] > 0 else None}
+        # the same with ordinary (pageable) numpy arrays, as the drop-in engine.infer passes them
+        del outs
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(max(1, args.steps // 2)):
+            eng.infer_batch(img1, img2)
+        pg_s = allmax(time.perf_counter() - t0)
+        e2e_line["pageable"] = {"value": total_pairs * max(1, args.steps // 2) / pg_s, "unit": "pairs/s",
+                                "host_buffers": "pageable numpy arrays"}
+    prof, ops = profiled(eng)
+    eng.close()
     launches_per_step = int(prof["gemm_launches"] + prof["attn_launches"] + prof["other_launches"])
+
+    # ---------------- the other 16-bit operand type (same weights file, same workload)
+    other = None
+    if not args.no_other_dtype:
+        oname = "bf16" if args.dtype == "fp16" else "fp16"
+        eng = NativeEngine(d, IMAGE_HW, [local_rank], per, dtypes[oname])
+        eng.load(str(path))
+        o_ms, _, _ = resident(eng, False)
+        o_prof, o_ops = profiled(eng)
+        eng.close()
+        o_attn = o_prof["attn_flop"] / (o_prof["attn_ms"] * 1e-3) / 1e12 if o_prof["attn_ms"] > 0 else 0.0
+        other = {"dtype": oname, "value": total_pairs * args.steps / (o_ms / 1000.0), "unit": "pairs/s",
+                 "ms_per_step": o_ms / args.steps, "attention_tflops": o_attn,
+                 "ops": {k: [round(o["ms"], 3), round(o["flop"] / (o["ms"] * 1e-3) / 1e12, 1) if o["ms"] > 0 else 0.0]
+                         for k, o in o_ops.items()}}
+
+    # ---------------- matcher at N = 196,608 (rank 0 drives all N GPUs; the others wait)
+    matcher = None
+    barrier()
+    if rank == 0 and not args.no_matcher:
+        matcher = run_matcher(list(range(world)), args.steps, clk["sm_mhz"] if clk else None)
+    barrier()
+
+    # ---------------- isolated attention (128 seqs x 12 heads x 576 x 64), one GPU
+    attention_iso = None
+    if rank == 0 and not args.no_matcher:
+        flop, res = run_attention(main_dt)
+        attention_iso = {"workload": f"{ATT_SEQS} seqs (64 pairs x 2 views) x {ATT_HEADS} heads x {ATT_TOK} tokens "
+                                     f"(24x24 grid) x 64, {args.dtype}, Q/K/V ~ N(0,1) (RoPE is applied by the "
+                                     f"producing QKV GEMM's epilogue in this design)", "flop_per_launch": flop, **res}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and total_pairs == GLOBAL_PAIRS:
         cpu = cpu_baseline_port(d, IMAGE_HW)
+        if matcher is not None:
+            matcher["cpu_baseline"] = cpu_baseline_matcher()
+        if attention_iso is not None:
+            attention_iso["cpu_baseline"] = cpu_baseline_attention()
 
     if rank == 0:
         pk, src = peaks()
         gemm_tf = prof["gemm_flop"] / (prof["gemm_ms"] * 1e-3) / 1e12 if prof["gemm_ms"] > 0 else 0.0
         attn_tf = prof["attn_flop"] / (prof["attn_ms"] * 1e-3) / 1e12 if prof["attn_ms"] > 0 else 0.0
         peak_tc = float(pk["bf16_tflops_sustained"])
+        peak_burst = float(pk["bf16_tflops"])
         fc1 = ops.get("enc.fc1", {"ms": 0.0, "flop": 0.0, "launches": 1})
         fc1_tf = (fc1["flop"] / fc1["launches"]) / (fc1["ms"] / fc1["launches"] * 1e-3) / 1e12 if fc1["ms"] > 0 else 0.0
         fc1_rows = 2 * per * (IMAGE_HW[0] // d.patch) * (IMAGE_HW[1] // d.patch)
+        fc1_alg_bytes = fc1_rows * d.enc_dim * 2 + d.enc_mlp * d.enc_dim * 2 + fc1_rows * d.enc_mlp * 2
         fpp = flops_per_pair(d, IMAGE_HW)
+        if attention_iso is not None:
+            for k in ("self", "cross"):
+                attention_iso[k]["frac_of_burst"] = attention_iso[k]["tflops"] / peak_burst
         line = {
             "metric": METRIC, "value": value, "unit": "pairs/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": eng.dtype_name, "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": args.dtype, "data": "synthetic",
             "config": {"workload": "MASt3R ViT-L 512x384 two-view inference (enc 1024x24, dec 768x12, DPT + 24-d "
                                    "local-feature heads)", "global_batch": total_pairs, "pairs_per_gpu": per,
                        "image": "384x512", "parallelism": f"dp{world} (pairs sharded, no collectives)",
@@ -335,18 +536,24 @@ def run_ours(args):
                          "achieved": fc1_tf, "peak": peak_tc, "unit": "TFLOP/s", "frac": fc1_tf / peak_tc,
                          "peak_source": f"{src} bf16_tflops_sustained",
                          "traffic": FC1_DRAM_BYTES_PER_ROW * fc1_rows,
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one fc1 launch at "
-                                           "16 pairs, scaled by rows"},
+                         "traffic_source": "SCALED, not measured at this size: ncu dram__bytes_read.sum + "
+                                           "dram__bytes_write.sum of one fc1 launch at 16 pairs (24576 rows), "
+                                           "times the rows of this launch",
+                         "algorithmic_bytes": fc1_alg_bytes},
             "gemm_family": {"kernel": "gemm_tc_kernel (all GEMM/conv launches of a step)", "achieved": gemm_tf,
                             "peak": peak_tc, "unit": "TFLOP/s", "frac": gemm_tf / peak_tc,
                             "ms_per_step": prof["gemm_ms"], "launches_per_step": int(prof["gemm_launches"])},
             "attention": {"achieved": attn_tf, "peak": peak_tc, "unit": "TFLOP/s", "frac": attn_tf / peak_tc,
+                          "frac_of_burst": attn_tf / peak_burst,
                           "ms_per_step": prof["attn_ms"], "launches_per_step": int(prof["attn_launches"])},
+            "attention_isolated": attention_iso,
+            "matcher": matcher,
             "model_tflops": fpp * total_pairs * args.steps / (total_ms / 1000.0) / 1e12,
             "kernel_ms_per_step": {"gemm": prof["gemm_ms"], "attention": prof["attn_ms"], "other": prof["other_ms"]},
             # per operation of the model: [device ms per step, TFLOP/s (0 for non-contractions)]
             "ops": {k: [round(o["ms"], 3), round(o["flop"] / (o["ms"] * 1e-3) / 1e12, 1) if o["ms"] > 0 else 0.0]
                     for k, o in ops.items()},
+            "other_dtype": other,
             "e2e": e2e_line,
             "wall_ms_per_step": 1000.0 * wall / args.steps,
             "gpu_launches": launches_per_step * args.steps,
@@ -354,7 +561,6 @@ def run_ours(args):
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
-    eng.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -371,6 +577,9 @@ def main():
     ap.add_argument("--pairs", type=int, default=GLOBAL_PAIRS,
                     help="global batch (default: the 64 pairs of the benchmark; smaller for profiling runs)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end pass (profiling runs)")
+    ap.add_argument("--dtype", choices=("fp16", "bf16"), default="fp16", help="operand type of the headline line")
+    ap.add_argument("--no-other-dtype", action="store_true", help="skip the pass in the other 16-bit type")
+    ap.add_argument("--no-matcher", action="store_true", help="skip the matcher and isolated-attention lines")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

@@ -62,7 +62,10 @@ typedef struct m3r_config {
     int dtype;          /* M3R_DTYPE_F16 or M3R_DTYPE_BF16 */
 } m3r_config;
 
-/* Slots of the timing_ms array written by m3r_infer / m3r_match. */
+/* Slots of the timing_ms array written by m3r_infer / m3r_match.  m3r_match uses
+ * slots 0-2 for its device phases (max over devices): descriptor normalisation, the
+ * fused similarity arg-max, and the reciprocal test + threshold + top-k; slot 6 is
+ * the three together. */
 enum {
     M3R_T_PREPROCESS = 0, /* u8 -> normalised patches (device) */
     M3R_T_ENCODER = 1,
@@ -70,9 +73,12 @@ enum {
     M3R_T_HEADS = 3,
     M3R_T_H2D = 4,
     M3R_T_D2H = 5,
-    M3R_T_INFERENCE = 6, /* device time of the forward pass (max over devices) */
+    M3R_T_INFERENCE = 6, /* device time of the forward pass / the match (max over devices) */
     M3R_T_TOTAL = 7,     /* host wall time of the call */
-    M3R_T_COUNT = 8
+    M3R_T_COUNT = 8,
+    M3R_T_MATCH_NORMALIZE = 0,
+    M3R_T_MATCH_ARGMAX = 1,
+    M3R_T_MATCH_SELECT = 2
 };
 
 /* Opaque engine: weights replicated on every device of the config. */

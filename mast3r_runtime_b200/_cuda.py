@@ -235,7 +235,9 @@ class NativeEngine:
         return SimpleNamespace(
             idx_1=idx1[:k].copy(), idx_2=idx2[:k].copy(), pts2d_1=p1[:k].copy(), pts2d_2=p2[:k].copy(),
             pts3d_1=np.zeros((k, 3), np.float32), pts3d_2=np.zeros((k, 3), np.float32),
-            confidence=conf[:k].copy(), timing={"match_ms": float(t[-1]), "kernel_ms": float(t[6])},
+            confidence=conf[:k].copy(),
+            timing={"match_ms": float(t[7]), "kernel_ms": float(t[6]), "normalize_ms": float(t[0]),
+                    "argmax_ms": float(t[1]), "select_ms": float(t[2])},
         )
 
 

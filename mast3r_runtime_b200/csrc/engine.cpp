@@ -1148,47 +1148,65 @@ void Engine::profile(double* out) const {
 }
 
 // ---------------------------------------------------------------------------- match
+namespace {
+// Four events around the device phases of one match: normalize, arg-max, select.
+struct MatchEvents {
+    cudaEvent_t e[4] = {nullptr, nullptr, nullptr, nullptr};
+    MatchEvents() {
+        for (auto& x : e) M3R_CUDA(cudaEventCreate(&x));
+    }
+    ~MatchEvents() {
+        for (auto& x : e)
+            if (x) cudaEventDestroy(x);
+    }
+    MatchEvents(const MatchEvents&) = delete;
+    MatchEvents& operator=(const MatchEvents&) = delete;
+    // ms[0..2] per phase, ms[3] all three (the events must have completed)
+    void phases(float* ms) const {
+        for (int i = 0; i < 3; ++i) M3R_CUDA(cudaEventElapsedTime(&ms[i], e[i], e[i + 1]));
+        M3R_CUDA(cudaEventElapsedTime(&ms[3], e[0], e[3]));
+    }
+};
+}  // namespace
+
 int Engine::match(const float* d1, const float* d2, int hh, int ww, int dd, int top_k, int reciprocal, float thr,
                   int64_t* idx1, int64_t* idx2, float* conf, float* p1, float* p2, float* timing) {
     const auto t0 = std::chrono::steady_clock::now();
     M3R_REQUIRE(hh >= 0 && ww >= 0 && dd > 0 && top_k >= 0, "match: bad arguments");
     const long long n = static_cast<long long>(hh) * ww;
     M3R_REQUIRE(n < 0x7FFFFFFFLL, "match: too many descriptors");
-    M3R_REQUIRE(top_k <= 4096, "match: top_k must be <= 4096");
     if (n == 0 || top_k == 0) {
         if (timing) timing[M3R_T_TOTAL] = 0.0f;
         return 0;
     }
     int m = 0;
-    float kms = 0;
+    float phase_ms[4] = {0, 0, 0, 0};  // normalize, arg-max, select, all three (device time)
     if (devs_.size() > 1 && n >= static_cast<long long>(devs_.size()) * 128) {
-        m = match_multi(d1, d2, n, ww, dd, top_k, reciprocal, thr, idx1, idx2, conf, &kms);
+        m = match_multi(d1, d2, n, ww, dd, top_k, reciprocal, thr, idx1, idx2, conf, phase_ms);
     } else {
         // single device (device 0 of the engine)
         Device& D = *devs_[0];
         DeviceGuard g(D.dev());
         cudaStream_t s = D.stream();
         D.mws.reserve(n, dd);
-        cudaEvent_t e0, e1;
-        M3R_CUDA(cudaEventCreate(&e0));
-        M3R_CUDA(cudaEventCreate(&e1));
+        MatchEvents ev;
         M3R_CUDA(cudaMemcpyAsync(D.mws.a, d1, sizeof(float) * n * dd, cudaMemcpyHostToDevice, s));
         M3R_CUDA(cudaMemcpyAsync(D.mws.b, d2, sizeof(float) * n * dd, cudaMemcpyHostToDevice, s));
-        M3R_CUDA(cudaEventRecord(e0, s));
+        M3R_CUDA(cudaEventRecord(ev.e[0], s));
         match_normalize(s, D.mws.a, D.mws.a, n, dd);
         match_normalize(s, D.mws.b, D.mws.b, n, dd);
+        M3R_CUDA(cudaEventRecord(ev.e[1], s));
         match_argmax(s, D.mws.a, D.mws.b, 0, n, n, dd, D.mws.rowkey, D.mws.colkey, true);
+        M3R_CUDA(cudaEventRecord(ev.e[2], s));
         m = match_select(s, D.mws, n, 0, reciprocal, thr, top_k);
-        M3R_CUDA(cudaEventRecord(e1, s));
+        M3R_CUDA(cudaEventRecord(ev.e[3], s));
         if (m > 0) {
             M3R_CUDA(cudaMemcpyAsync(idx1, D.mws.idx1, sizeof(int64_t) * m, cudaMemcpyDeviceToHost, s));
             M3R_CUDA(cudaMemcpyAsync(idx2, D.mws.idx2, sizeof(int64_t) * m, cudaMemcpyDeviceToHost, s));
             M3R_CUDA(cudaMemcpyAsync(conf, D.mws.conf, sizeof(float) * m, cudaMemcpyDeviceToHost, s));
         }
         M3R_CUDA(cudaStreamSynchronize(s));
-        M3R_CUDA(cudaEventElapsedTime(&kms, e0, e1));
-        cudaEventDestroy(e0);
-        cudaEventDestroy(e1);
+        ev.phases(phase_ms);
     }
     for (int i = 0; i < m; ++i) {  // matching.cpp:216-222
         p1[2 * i] = static_cast<float>(idx1[i] % ww);
@@ -1198,7 +1216,10 @@ int Engine::match(const float* d1, const float* d2, int hh, int ww, int dd, int 
     }
     if (timing) {
         for (int i = 0; i < M3R_T_COUNT; ++i) timing[i] = 0.0f;
-        timing[M3R_T_INFERENCE] = kms;
+        timing[M3R_T_MATCH_NORMALIZE] = phase_ms[0];
+        timing[M3R_T_MATCH_ARGMAX] = phase_ms[1];
+        timing[M3R_T_MATCH_SELECT] = phase_ms[2];
+        timing[M3R_T_INFERENCE] = phase_ms[3];
         timing[M3R_T_TOTAL] =
             static_cast<float>(std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count());
     }
@@ -1212,7 +1233,7 @@ int Engine::match(const float* d1, const float* d2, int hh, int ww, int dd, int 
 // top-k on its own rows.  The per-device results (each <= top_k, exact top-k of its
 // rows) are merged on the host: the global top-k is inside their union.
 int Engine::match_multi(const float* d1, const float* d2, long long n, int ww, int dd, int top_k, int reciprocal,
-                        float thr, int64_t* idx1, int64_t* idx2, float* conf, float* kernel_ms) {
+                        float thr, int64_t* idx1, int64_t* idx2, float* conf, float* phase_ms) {
     const int nd = static_cast<int>(devs_.size());
     const NcclApi& api = nccl();
     if (nccl_comms_.empty()) {
@@ -1227,7 +1248,7 @@ int Engine::match_multi(const float* d1, const float* d2, long long n, int ww, i
         int m = 0, total = 0;
         std::vector<int64_t> i1, i2;
         std::vector<float> c;
-        cudaEvent_t e0 = nullptr, e1 = nullptr;
+        std::unique_ptr<MatchEvents> ev;  // created with the part's device current
     };
     std::vector<Part> parts(nd);
     for (int i = 0; i < nd; ++i) {
@@ -1242,15 +1263,16 @@ int Engine::match_multi(const float* d1, const float* d2, long long n, int ww, i
         cudaStream_t s = D.stream();
         const long long nr = P.r1 - P.r0;
         D.mws.reserve(n, dd);
-        M3R_CUDA(cudaEventCreate(&P.e0));
-        M3R_CUDA(cudaEventCreate(&P.e1));
+        P.ev.reset(new MatchEvents());
         M3R_CUDA(cudaMemcpyAsync(D.mws.a, d1 + P.r0 * dd, sizeof(float) * nr * dd, cudaMemcpyHostToDevice, s));
         M3R_CUDA(cudaMemcpyAsync(D.mws.b, d2, sizeof(float) * n * dd, cudaMemcpyHostToDevice, s));
-        M3R_CUDA(cudaEventRecord(P.e0, s));
+        M3R_CUDA(cudaEventRecord(P.ev->e[0], s));
         match_normalize(s, D.mws.a, D.mws.a, nr, dd);
         match_normalize(s, D.mws.b, D.mws.b, n, dd);
+        M3R_CUDA(cudaEventRecord(P.ev->e[1], s));
         // A is addressed by global row: rows [r0, r1) live at mws.a[0 .. nr)
         match_argmax(s, D.mws.a - P.r0 * dd, D.mws.b, P.r0, P.r1, n, dd, D.mws.rowkey, D.mws.colkey, true);
+        M3R_CUDA(cudaEventRecord(P.ev->e[2], s));
     });
     // phase 2: column keys max-reduced over the devices
     nccl_check(api.GroupStart(), "ncclGroupStart");
@@ -1269,7 +1291,7 @@ int Engine::match_multi(const float* d1, const float* d2, long long n, int ww, i
         DeviceGuard g(D.dev());
         cudaStream_t s = D.stream();
         P.m = match_select(s, D.mws, P.r1 - P.r0, P.r0, reciprocal, thr, top_k, &P.total);
-        M3R_CUDA(cudaEventRecord(P.e1, s));
+        M3R_CUDA(cudaEventRecord(P.ev->e[3], s));
         P.i1.resize(P.m);
         P.i2.resize(P.m);
         P.c.resize(P.m);
@@ -1280,18 +1302,17 @@ int Engine::match_multi(const float* d1, const float* d2, long long n, int ww, i
         }
         M3R_CUDA(cudaStreamSynchronize(s));
     });
-    float kms = 0;
+    // per phase, the slowest device (the phases end at the all-reduce / the host merge)
     long long total = 0;
+    for (int k = 0; k < 4; ++k) phase_ms[k] = 0.0f;
     for (int i = 0; i < nd; ++i) {
-        float t = 0;
-        M3R_CUDA(cudaSetDevice(devs_[i]->dev()));
-        M3R_CUDA(cudaEventElapsedTime(&t, parts[i].e0, parts[i].e1));
-        kms = std::max(kms, t);
-        cudaEventDestroy(parts[i].e0);
-        cudaEventDestroy(parts[i].e1);
+        DeviceGuard g(devs_[i]->dev());
+        float t[4];
+        parts[i].ev->phases(t);
+        for (int k = 0; k < 4; ++k) phase_ms[k] = std::max(phase_ms[k], t[k]);
+        parts[i].ev.reset();
         total += parts[i].total;
     }
-    if (kernel_ms) *kernel_ms = kms;
     // merge: all candidates in row order when they fit, else the top_k by (conf desc, idx_1 asc)
     struct C3 {
         float c;

@@ -77,7 +77,7 @@ private:
     std::vector<std::pair<int, int>> shards(int n_pairs) const;  // (first pair, count) per device
     // rows of desc_1 sharded over the devices; column keys max-reduced with NCCL
     int match_multi(const float* d1, const float* d2, long long n, int ww, int dd, int top_k, int reciprocal,
-                    float thr, int64_t* idx1, int64_t* idx2, float* conf, float* kernel_ms);
+                    float thr, int64_t* idx1, int64_t* idx2, float* conf, float* phase_ms);
     m3r_config cfg_;
     Dims d_;
     std::vector<std::unique_ptr<Device>> devs_;

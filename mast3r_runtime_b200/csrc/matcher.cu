@@ -33,6 +33,7 @@ namespace m3r {
 namespace {
 
 __device__ __forceinline__ uint32_t orderable(float f) {
+    if (f != f) return 0xFFFFFFFFu;  // NaN: only ever the seed of a row / column (see argmax_kernel)
     f = f + 0.0f;  // -0.0 -> +0.0: the reference's > comparison treats them as equal
     const uint32_t u = __float_as_uint(f);
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
@@ -48,7 +49,8 @@ __device__ __forceinline__ unsigned long long make_key(float v, uint32_t idx) {
 }
 
 // ------------------------------------------------------------------ normalize
-__global__ void normalize_kernel(const float* __restrict__ in, float* __restrict__ out, long long n, int d) {
+// (in and out may be the same buffer: no __restrict__)
+__global__ void normalize_kernel(const float* in, float* out, long long n, int d) {
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
         const float* r = in + i * d;
@@ -62,6 +64,38 @@ __global__ void normalize_kernel(const float* __restrict__ in, float* __restrict
         } else {
             for (int k = 0; k < d; ++k) o[k] = r[k];
         }
+    }
+}
+
+// 24-channel rows as six 16-byte loads / stores per thread (rows of 96 bytes keep
+// 16-byte alignment when the base is aligned); same operation order as above.
+__global__ void normalize24_kernel(const float4* in, float4* out, long long n) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        float4 x[6];
+#pragma unroll
+        for (int q = 0; q < 6; ++q) x[q] = in[i * 6 + q];
+        float s = 0.0f;
+#pragma unroll
+        for (int q = 0; q < 6; ++q) {
+            s = __fadd_rn(s, __fmul_rn(x[q].x, x[q].x));
+            s = __fadd_rn(s, __fmul_rn(x[q].y, x[q].y));
+            s = __fadd_rn(s, __fmul_rn(x[q].z, x[q].z));
+            s = __fadd_rn(s, __fmul_rn(x[q].w, x[q].w));
+        }
+        s = sqrtf(s);
+        if (s > 1e-8f) {
+            const float inv = 1.0f / s;
+#pragma unroll
+            for (int q = 0; q < 6; ++q) {
+                x[q].x = __fmul_rn(x[q].x, inv);
+                x[q].y = __fmul_rn(x[q].y, inv);
+                x[q].z = __fmul_rn(x[q].z, inv);
+                x[q].w = __fmul_rn(x[q].w, inv);
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 6; ++q) out[i * 6 + q] = x[q];
     }
 }
 
@@ -117,16 +151,17 @@ __global__ void __launch_bounds__(256, 2)
         for (int kc = 0; kc < D; kc += kKC) {
             const int kn = D - kc < kKC ? D - kc : kKC;
             __syncthreads();
-            // stage transposed chunks: thread t writes column (row t&127) for k in its half
+            // consecutive threads read consecutive floats of a row (row-major [n, D]), so
+            // a warp's loads are coalesced; the chunk is stored transposed ([k][row])
             if (!a_resident || jt == jt_begin) {
                 for (int e = tid; e < kTI * kn; e += 256) {
-                    const int rr = e % kTI, k = e / kTI;
+                    const int rr = e / kn, k = e - rr * kn;
                     const long long gi = i0 + rr;
                     sA[k][rr] = gi < row1 ? A[gi * D + kc + k] : 0.0f;
                 }
             }
             for (int e = tid; e < kTJ * kn; e += 256) {
-                const int cc = e % kTJ, k = e / kTJ;
+                const int cc = e / kn, k = e - cc * kn;
                 const long long gj = j0 + cc;
                 sB[k][cc] = gj < n2 ? B[gj * D + kc + k] : 0.0f;
             }
@@ -148,7 +183,11 @@ __global__ void __launch_bounds__(256, 2)
             }
         }
 
-        // ---- rows: first (lowest j) maximum over this thread's columns, in increasing j
+        // ---- rows: first (lowest j) maximum over this thread's columns, in increasing j.
+        // The reference seeds every row with column 0 and replaces it only on a strictly
+        // greater value (matching.cpp:128-139), so column 0 is taken even when it is NaN
+        // or -inf; a NaN seed is never replaced (its key, all ones, is the largest).
+        const bool seed_col0 = j0 == 0 && tc == 0;  // this thread holds column 0 (first tile of segment 0)
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
             float m = -INFINITY;
@@ -156,29 +195,38 @@ __global__ void __launch_bounds__(256, 2)
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
                 const long long j = j0 + (c < 4 ? tc * 4 + c : 64 + tc * 4 + c - 4);
-                if (j < n2 && s[r][c] > m) {
+                if (c == 0 && seed_col0) {
+                    m = s[r][0];
+                    mc = 0;
+                } else if (j < n2 && s[r][c] > m) {
                     m = s[r][c];
                     mc = c;
                 }
             }
-            if (mc >= 0 && m > rbest[r]) {
+            if (mc >= 0 && (seed_col0 || m > rbest[r])) {
                 rbest[r] = m;
                 ridx[r] = static_cast<uint32_t>(j0 + (mc < 4 ? tc * 4 + mc : 64 + tc * 4 + mc - 4));
             }
         }
 
-        // ---- columns: first (lowest i) maximum over this thread's rows, keyed
+        // ---- columns: first (lowest i) maximum over this thread's rows, keyed; row 0
+        // seeds every column as in matching.cpp:144-155
+        const bool seed_row0 = i0 == 0 && tr == 0;
         unsigned long long ck[8];
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
             float m = -INFINITY;
             int mr = -1;
 #pragma unroll
-            for (int r = 0; r < 8; ++r)
-                if (i0 + tr * 8 + r < row1 && s[r][c] > m) {
+            for (int r = 0; r < 8; ++r) {
+                if (r == 0 && seed_row0) {
+                    m = s[0][c];
+                    mr = 0;
+                } else if (i0 + tr * 8 + r < row1 && s[r][c] > m) {
                     m = s[r][c];
                     mr = r;
                 }
+            }
             ck[c] = mr >= 0 ? make_key(m, static_cast<uint32_t>(i0 + tr * 8 + mr)) : 0ull;
             // reduce over the 4 row groups of this warp (lanes differing in bits 3, 4)
 #pragma unroll
@@ -322,20 +370,62 @@ __global__ void radix_hist_kernel(const unsigned long long* __restrict__ keys, i
     }
 }
 
-// single thread: pick the digit bucket that holds the remaining-th largest key
-__global__ void radix_pick_kernel(unsigned* __restrict__ hist, unsigned long long* __restrict__ state) {
-    // state[0] = prefix, state[1] = remaining
-    unsigned long long remaining = state[1];
-    unsigned long long cum = 0;
-    int b = 65535;
-    for (; b >= 0; --b) {
-        if (cum + hist[b] >= remaining) break;
-        cum += hist[b];
+// One block of kPickThreads threads: finds the digit bucket that holds the
+// remaining-th largest key (buckets scanned from the highest digit down), appends
+// the digit to the prefix, and clears the histogram for the next pass.
+// state[0] = prefix of the digits chosen so far, state[1] = rank still to find.
+constexpr int kPickThreads = 1024;
+constexpr int kBinsPerThread = 65536 / kPickThreads;
+
+__global__ void __launch_bounds__(kPickThreads) radix_pick_kernel(unsigned* __restrict__ hist,
+                                                                  unsigned long long* __restrict__ state) {
+    __shared__ unsigned long long s_warp[kPickThreads / 32];
+    __shared__ int s_found;
+    const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+    // thread t owns bins [hi - kBinsPerThread, hi), hi = 65536 - t * kBinsPerThread: thread 0 the highest
+    const int hi = 65536 - t * kBinsPerThread;
+    unsigned local = 0;
+    for (int b = hi - 1; b >= hi - kBinsPerThread; --b) local += hist[b];
+    // exclusive prefix over threads (descending digits): warp scan, then over warps
+    unsigned long long incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
     }
-    if (b < 0) b = 0;
-    state[0] = (state[0] << 16) | static_cast<unsigned long long>(b);
-    state[1] = remaining - cum;
-    for (int i = 0; i < 65536; ++i) hist[i] = 0;
+    if (lane == 31) s_warp[w] = incl;
+    if (t == 0) s_found = 0;
+    __syncthreads();
+    if (w == 0) {
+        unsigned long long v = s_warp[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned long long u = __shfl_up_sync(0xffffffffu, v, o);
+            if (lane >= o) v += u;
+        }
+        s_warp[lane] = v;  // inclusive prefix of warp sums
+    }
+    __syncthreads();
+    const unsigned long long before = (w > 0 ? s_warp[w - 1] : 0ull) + incl - local;  // keys in higher bins
+    const unsigned long long remaining = state[1];
+    if (before < remaining && remaining <= before + local) {
+        // the remaining-th key lies in this thread's bins
+        unsigned long long cum = before;
+        int b = hi - 1;
+        for (; b > hi - kBinsPerThread; --b) {
+            if (cum + hist[b] >= remaining) break;
+            cum += hist[b];
+        }
+        state[0] = (state[0] << 16) | static_cast<unsigned long long>(b);
+        state[1] = remaining - cum;
+        s_found = 1;
+    }
+    __syncthreads();
+    if (t == 0 && !s_found) {  // fewer keys than `remaining` (not reached when total > top_k): lowest digit
+        state[0] = state[0] << 16;
+        state[1] = 1;
+    }
+    for (int b = hi - kBinsPerThread; b < hi; ++b) hist[b] = 0;
 }
 
 __global__ void select_ge_kernel(const unsigned long long* __restrict__ keys, const uint32_t* __restrict__ cj,
@@ -386,6 +476,32 @@ __global__ void sort_desc_kernel(unsigned long long* __restrict__ key, uint32_t*
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         key[i] = sk[i];
         val[i] = sv[i];
+    }
+}
+
+// Global-memory bitonic sort step (descending) for top_k > 4096: n is a power of two,
+// one launch per (size, stride) pair.
+__global__ void bitonic_step_kernel(unsigned long long* __restrict__ key, uint32_t* __restrict__ val, int n, int size,
+                                    int stride) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const int partner = i ^ stride;
+        if (partner <= i) continue;
+        const bool desc = (i & size) == 0;
+        const unsigned long long a = key[i], b = key[partner];
+        if (desc ? (a < b) : (a > b)) {
+            key[i] = b;
+            key[partner] = a;
+            const uint32_t t = val[i];
+            val[i] = val[partner];
+            val[partner] = t;
+        }
+    }
+}
+
+__global__ void fill_keys_kernel(unsigned long long* __restrict__ key, uint32_t* __restrict__ val, int from, int to) {
+    for (int i = from + blockIdx.x * blockDim.x + threadIdx.x; i < to; i += gridDim.x * blockDim.x) {
+        key[i] = 0ull;
+        val[i] = 0u;
     }
 }
 
@@ -445,8 +561,11 @@ void MatchWorkspace::reserve(long long n, int d) {
     M3R_CUDA(cudaMalloc(&cj, sizeof(uint32_t) * nn));
     M3R_CUDA(cudaMalloc(&hist, sizeof(unsigned) * 65536));
     M3R_CUDA(cudaMalloc(&state, sizeof(unsigned long long) * 2));
-    M3R_CUDA(cudaMalloc(&skey, sizeof(unsigned long long) * 4096));
-    M3R_CUDA(cudaMalloc(&sj, sizeof(uint32_t) * 4096));
+    // selected keys: room for a power-of-two bitonic sort of up to n entries
+    long long sel = 4096;
+    while (sel < nn) sel <<= 1;
+    M3R_CUDA(cudaMalloc(&skey, sizeof(unsigned long long) * sel));
+    M3R_CUDA(cudaMalloc(&sj, sizeof(uint32_t) * sel));
     M3R_CUDA(cudaMalloc(&misc, sizeof(int) * 4));
     M3R_CUDA(cudaMalloc(&idx1, sizeof(long long) * nn));
     M3R_CUDA(cudaMalloc(&idx2, sizeof(long long) * nn));
@@ -458,7 +577,12 @@ void MatchWorkspace::reserve(long long n, int d) {
 
 void match_normalize(cudaStream_t s, const float* in, float* out, long long n, int d) {
     if (n == 0) return;
-    normalize_kernel<<<blocks_for(n, 256), 256, 0, s>>>(in, out, n, d);
+    const bool aligned = (reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) % 16 == 0;
+    if (d == 24 && aligned)
+        normalize24_kernel<<<blocks_for(n, 256), 256, 0, s>>>(reinterpret_cast<const float4*>(in),
+                                                               reinterpret_cast<float4*>(out), n);
+    else
+        normalize_kernel<<<blocks_for(n, 256), 256, 0, s>>>(in, out, n, d);
     M3R_CUDA(cudaGetLastError());
 }
 
@@ -502,18 +626,26 @@ int match_select(cudaStream_t s, MatchWorkspace& ws, long long nrows, long long 
     if (total_out) *total_out = total;
     int m = total;
     if (total > top_k) {
-        M3R_REQUIRE(top_k <= 4096, "match: top_k must be <= 4096");
         unsigned long long st[2] = {0ull, static_cast<unsigned long long>(top_k)};
         M3R_CUDA(cudaMemcpyAsync(ws.state, st, sizeof(st), cudaMemcpyHostToDevice, s));
         for (int pass = 0; pass < 4; ++pass) {
             radix_hist_kernel<<<blocks_for(total, 256), 256, 0, s>>>(ws.ckey, total, 48 - 16 * pass, ws.state,
                                                                       16 * pass, ws.hist);
-            radix_pick_kernel<<<1, 1, 0, s>>>(ws.hist, ws.state);
+            radix_pick_kernel<<<1, kPickThreads, 0, s>>>(ws.hist, ws.state);
         }
         M3R_CUDA(cudaMemsetAsync(ws.misc + 1, 0, sizeof(int), s));
         select_ge_kernel<<<blocks_for(total, 256), 256, 0, s>>>(ws.ckey, ws.cj, total, ws.state, ws.skey, ws.sj,
                                                                  ws.misc + 1);
-        sort_desc_kernel<<<1, 1024, 0, s>>>(ws.skey, ws.sj, top_k);
+        if (top_k <= 4096) {
+            sort_desc_kernel<<<1, 1024, 0, s>>>(ws.skey, ws.sj, top_k);
+        } else {
+            int m2 = 1;
+            while (m2 < top_k) m2 <<= 1;
+            fill_keys_kernel<<<blocks_for(m2 - top_k, 256), 256, 0, s>>>(ws.skey, ws.sj, top_k, m2);
+            for (int size = 2; size <= m2; size <<= 1)
+                for (int stride = size >> 1; stride > 0; stride >>= 1)
+                    bitonic_step_kernel<<<blocks_for(m2, 256), 256, 0, s>>>(ws.skey, ws.sj, m2, size, stride);
+        }
         finalize_kernel<<<blocks_for(top_k, 256), 256, 0, s>>>(ws.skey, ws.sj, top_k, ws.idx1, ws.idx2, ws.conf);
         m = top_k;
     } else if (total > 0) {

@@ -76,12 +76,25 @@ def tiny_dims(patch: int = 16, enc_dim: int = 128, enc_depth: int = 2, enc_heads
 
 
 def _trunc_normal(rng: np.random.Generator, shape, std: float) -> np.ndarray:
-    x = rng.standard_normal(shape, dtype=np.float32)
-    bad = np.abs(x) > 2.0
-    while bad.any():
-        x[bad] = rng.standard_normal(int(bad.sum()), dtype=np.float32)
-        bad = np.abs(x) > 2.0
-    return x * np.float32(std)
+    x = rng.standard_normal(shape, dtype=np.float32).reshape(-1)
+    bad = np.flatnonzero(np.abs(x) > 2.0)
+    while bad.size:  # resample only the rejected entries
+        x[bad] = rng.standard_normal(bad.size, dtype=np.float32)
+        bad = bad[np.abs(x[bad]) > 2.0]
+    return (x * np.float32(std)).reshape(shape)
+
+
+def round_to_16bit(x: np.ndarray, dtype: str) -> np.ndarray:
+    """float32 values rounded (to nearest even) to the nearest fp16 / bf16 value, kept as
+    float32 (exactly representable in the 16-bit type)."""
+    x = np.ascontiguousarray(x, np.float32)
+    if dtype == "fp16":
+        return x.astype(np.float16).astype(np.float32)
+    if dtype == "bf16":
+        u = x.view(np.uint32).astype(np.uint64)
+        r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+        return r.astype(np.uint32).view(np.float32)
+    raise ValueError(f"unknown 16-bit type {dtype!r}")
 
 
 def weight_shapes(d: ModelDims) -> dict[str, tuple]:
@@ -163,12 +176,17 @@ def weight_shapes(d: ModelDims) -> dict[str, tuple]:
 
 
 def make_weights(d: ModelDims, seed: int = 0, std: float = 0.02,
-                 randomize_affine: bool = False) -> dict[str, np.ndarray]:
+                 randomize_affine: bool = False, checkpoint_dtype: str | None = None) -> dict[str, np.ndarray]:
     """Seeded float32 weights for every tensor of ``weight_shapes(d)``.
 
     Weight matrices: truncated normal (std ``std``, +-2 std).  Biases: 0, LayerNorm
     gamma 1 / beta 0 -- unless ``randomize_affine``, in which case biases ~ N(0, std^2)
     and gamma ~ 1 + N(0, 0.1^2), beta ~ N(0, 0.05^2).
+
+    ``checkpoint_dtype`` ("fp16" / "bf16"): a checkpoint stored in that 16-bit type --
+    every value rounded to it (the reference's checkpoints are 16-bit; its CPU path
+    upcasts them to float32), so a CPU model and a 16-bit GPU model read the same
+    weight values.
     """
     rng = np.random.default_rng(seed)
     out: dict[str, np.ndarray] = {}
@@ -187,6 +205,8 @@ def make_weights(d: ModelDims, seed: int = 0, std: float = 0.02,
                 out[key] = np.ones(shape, np.float32)
         else:
             out[key] = _trunc_normal(rng, shape, std)
+    if checkpoint_dtype is not None:
+        out = {k: round_to_16bit(v, checkpoint_dtype) for k, v in out.items()}
     return out
 
 

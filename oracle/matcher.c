@@ -113,9 +113,15 @@ void oracle_argmax(const float* a, const float* b, int64_t n1, int64_t n2, int d
                     if (dot[jj] > best) { best = dot[jj]; bj = (int32_t)(j0 + jj); }
                 best12[i] = best;
                 nn12[i] = bj;
+                /* matching.cpp:144-155 seeds every column with row 0 and replaces it
+                 * only on a strictly greater value: a thread's partial starts at the
+                 * global row 0 or at its first non-NaN value (a NaN elsewhere never wins) */
                 for (int jj = 0; jj < jn; ++jj) {
                     const int64_t j = j0 + jj;
-                    if (ci[j] < 0 || dot[jj] > cb[j]) { cb[j] = dot[jj]; ci[j] = (int32_t)i; }
+                    if ((ci[j] < 0 && (i == 0 || dot[jj] == dot[jj])) || (ci[j] >= 0 && dot[jj] > cb[j])) {
+                        cb[j] = dot[jj];
+                        ci[j] = (int32_t)i;
+                    }
                 }
             }
         }

@@ -1,9 +1,8 @@
 """Generate the golden fixtures in this directory by running the REFERENCE code.
 
-Run in a container where the reference tree is mounted (default /root/reference,
-override with M3R_REFERENCE):
+Run where the reference tree is available, naming it in M3R_REFERENCE:
 
-    python tests/golden/make_golden.py
+    M3R_REFERENCE=<reference tree> python tests/golden/make_golden.py [--large]
 
 It imports the reference's own numpy model classes
 (mast3r_runtime/backends/python/{croco_encoder,croco_decoder,rope2d,mast3r_model}.py)
@@ -18,6 +17,9 @@ Fixtures
                     on a seeded 64x96 image pair, plus RoPE2D of a seeded tensor
   matcher.npz       reference reciprocal_match (C++ and numpy) on seeded descriptor
                     maps, several (top_k, reciprocal, threshold) settings
+  matcher_large.npz (--large) the reference's C++ reciprocal_match on a 180 x 256
+                    map (N = 46,080, 24-d, the config-4 input recipe): the largest N
+                    its int-typed N * N similarity allocation accepts is 46,340
 """
 
 from __future__ import annotations
@@ -30,11 +32,12 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent.parent
-REF = Path(os.environ.get("M3R_REFERENCE", "/root/reference"))
+REF = Path(os.environ["M3R_REFERENCE"]) if os.environ.get("M3R_REFERENCE") else None
 
 MODEL_SEED = 1234
 IMAGE_SEED = (42, 43)
 IMAGE_HW = (64, 96)
+LARGE_CASE = (180, 256, 24, 5, 512, True, 0.5)  # (H, W, D, seed, top_k, reciprocal, threshold)
 MATCH_CASES = [  # (H, W, D, seed, top_k, reciprocal, threshold)
     (8, 8, 24, 7, 512, True, 0.5),
     (16, 24, 24, 8, 64, True, 0.0),
@@ -73,8 +76,27 @@ def matcher_inputs(h, w, d, seed):
     return a.reshape(h, w, d), b.reshape(h, w, d)
 
 
+def main_large():
+    """matcher_large.npz from the reference's own C++ matcher (oracle/_ref)."""
+    sys.path.insert(0, str(ROOT))
+    import oracle
+
+    if oracle.ref_lib() is None:
+        oracle.build()
+    h, w, d, seed, top_k, recip, thr = LARGE_CASE
+    a, b = matcher_inputs(h, w, d, seed)
+    r = oracle.ref_match(a, b, top_k=top_k, reciprocal=recip, confidence_threshold=thr)
+    if r is None:
+        raise SystemExit("oracle/_ref is not built: the reference tree is needed")
+    np.savez_compressed(HERE / "matcher_large.npz", case=np.array([h, w, d, seed, top_k, int(recip),
+                                                                    int(round(thr * 1000))]), **r)
+    print("wrote", HERE / "matcher_large.npz", len(r["idx_1"]), "matches")
+
+
 def main():
     sys.dont_write_bytecode = True
+    if REF is None:
+        raise SystemExit("set M3R_REFERENCE to the reference tree")
     sys.path.insert(0, str(REF))
     sys.path.insert(0, str(ROOT))
     from mast3r_runtime.backends.python.croco_decoder import CroCoDecoder
@@ -141,4 +163,7 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    if REF is None:
+        raise SystemExit("set M3R_REFERENCE to the reference tree")
+    os.environ.setdefault("M3R_REFERENCE", str(REF))
+    main_large() if "--large" in sys.argv[1:] else main()

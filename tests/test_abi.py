@@ -167,7 +167,7 @@ class FakeNative:
 
 
 def test_reference_wrapper_drives_cuda_engine(monkeypatch, tmp_path):
-    if not (REFERENCE / "mast3r_runtime").is_dir():
+    if REFERENCE is None or not (REFERENCE / "mast3r_runtime").is_dir():
         pytest.skip("reference tree not present")
     sys.dont_write_bytecode = True
     sys.path.insert(0, str(REFERENCE))

@@ -164,6 +164,33 @@ def test_match_argmax_bit_exact(lib, oracle_lib, n1, n2, d):
     assert gb.tobytes() == ob12.tobytes()
 
 
+@pytest.mark.parametrize("kind", ["a_row0", "b_row0", "a_row9", "inf"])
+def test_match_argmax_non_finite(lib, oracle_lib, kind):
+    """NaN / inf descriptors: row 0 (column 0) seeds every column (row) and a NaN seed
+    is never replaced; NaN elsewhere never wins (matching.cpp:128-155)."""
+    rng = np.random.default_rng(3)
+    a = rng.standard_normal((700, 24)).astype(np.float32)
+    b = rng.standard_normal((900, 24)).astype(np.float32)
+    if kind == "a_row0":
+        a[0, 5] = np.nan
+    elif kind == "b_row0":
+        b[0] = np.nan
+        a[300] = np.nan
+    elif kind == "a_row9":
+        a[9] = np.nan
+        b[400, 1] = np.nan
+    else:
+        a[4, 0] = np.inf
+        b[7, 3] = -np.inf
+    g12, g21, gb = _nn_gpu(lib, a, b)
+    o12, ob12, o21, _ = oracle_lib.argmax(oracle_lib.normalize(a), oracle_lib.normalize(b))
+    np.testing.assert_array_equal(g12, o12)
+    np.testing.assert_array_equal(g21, o21)
+    nan = np.isnan(ob12)
+    np.testing.assert_array_equal(np.isnan(gb), nan)
+    assert gb[~nan].tobytes() == ob12[~nan].tobytes()
+
+
 @pytest.fixture(scope="module")
 def matcher_engine(lib):
     from mast3r_runtime_b200 import NativeEngine, tiny_dims

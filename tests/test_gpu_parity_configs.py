@@ -1,0 +1,86 @@
+"""Parity of the two-view forward pass at the configurations that are timed.
+
+* MASt3R ViT-L, 384 x 512 (patch 16, 768 tokens, encoder 1024 x 24, decoder 768 x 12,
+  local-feature MLP 7168): the benchmark's model and weight recipe (seed 0, trunc-normal
+  0.02, zero biases, unit LayerNorm), in fp16 and bf16, and with random biases and
+  LayerNorm parameters in fp16;
+* DUNE ViT-B/14 encoder + MASt3R decoder, 336 x 336: random biases and LayerNorm, fp16
+  and bf16.
+
+The checkpoint is stored in the operand type (every weight rounded to fp16 / bf16), as
+the reference's 16-bit checkpoints are; the oracle (oracle/model.py, float32 -- the
+arithmetic type of the reference's numpy model) reads the same values.  Bar: pts3d and
+confidence relative L2 <= 1e-2, descriptor cosine >= 0.999 (mean over pixels).  With
+M3R_PARITY_REPORT=<file> the measured errors are appended to that file as JSON lines.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+
+import numpy as np
+import pytest
+
+from conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    ("mast3r_vit_large", (384, 512), "fp16", False),
+    ("mast3r_vit_large", (384, 512), "bf16", False),
+    ("mast3r_vit_large", (384, 512), "fp16", True),
+    ("dune_vit_base_336", (336, 336), "fp16", True),
+    ("dune_vit_base_336", (336, 336), "bf16", True),
+]
+
+_BASE = {}
+
+
+def _weights(variant, randomize_affine, dtype):
+    from mast3r_runtime_b200 import make_weights
+    from mast3r_runtime_b200.weights import VARIANTS, round_to_16bit
+
+    key = (variant, randomize_affine)
+    if key not in _BASE:
+        _BASE.clear()  # one full-precision set at a time (ViT-L: 2.7 GB)
+        _BASE[key] = make_weights(VARIANTS[variant], seed=0, randomize_affine=randomize_affine)
+    return {k: round_to_16bit(v, dtype) for k, v in _BASE[key].items()}
+
+
+@pytest.mark.parametrize("variant,hw,dtype,affine", CASES,
+                         ids=[f"{v}-{t}{'-affine' if a else ''}" for v, _, t, a in CASES])
+def test_timed_config_matches_oracle(tmp_path, variant, hw, dtype, affine):
+    from mast3r_runtime_b200 import NativeEngine, save_safetensors
+    from mast3r_runtime_b200._lib import DTYPE_BF16, DTYPE_F16
+    from mast3r_runtime_b200.weights import VARIANTS
+    from oracle.model import Model
+
+    d = VARIANTS[variant]
+    w = _weights(variant, affine, dtype)
+    path = save_safetensors(tmp_path / "unified.safetensors", w)
+    rng = np.random.default_rng(77)
+    img1 = rng.integers(0, 256, (1, *hw, 3), dtype=np.uint8)
+    img2 = rng.integers(0, 256, (1, *hw, 3), dtype=np.uint8)
+    eng = NativeEngine(d, hw, [0], 1, DTYPE_F16 if dtype == "fp16" else DTYPE_BF16)
+    eng.load(str(path))
+    out, _ = eng.infer_batch(img1, img2)
+    eng.close()
+    ref = Model(w, d, dtype=np.float32).forward(img1[0], img2[0])
+    rep = {"variant": variant, "image": list(hw), "dtype": dtype, "random_affine": affine}
+    for v in (1, 2):
+        rep[f"pts3d_{v}"] = rel_l2(out[f"pts3d_{v}"][0], ref[f"pts3d_{v}"])
+        rep[f"conf_{v}"] = rel_l2(out[f"conf_{v}"][0], ref[f"conf_{v}"])
+        g = out[f"desc_{v}"][0].astype(np.float64)
+        r = np.asarray(ref[f"desc_{v}"], np.float64)
+        cos = (g * r).sum(-1) / np.maximum(np.linalg.norm(g, axis=-1) * np.linalg.norm(r, axis=-1), 1e-30)
+        rep[f"desc_cos_mean_{v}"] = float(cos.mean())
+        rep[f"desc_cos_min_{v}"] = float(cos.min())
+    print(json.dumps(rep))
+    if os.environ.get("M3R_PARITY_REPORT"):
+        with open(os.environ["M3R_PARITY_REPORT"], "a") as f:
+            f.write(json.dumps(rep) + "\n")
+    for v in (1, 2):
+        assert rep[f"pts3d_{v}"] <= 1e-2, rep
+        assert rep[f"conf_{v}"] <= 1e-2, rep
+        assert rep[f"desc_cos_mean_{v}"] >= 0.999, rep

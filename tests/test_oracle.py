@@ -111,6 +111,18 @@ def test_matcher_golden_cpp_and_numpy(oracle_lib):
         np.testing.assert_array_equal(o["pts2d_1"][:, 1], o["idx_1"] // w)
 
 
+def test_matcher_large_golden(oracle_lib):
+    """The oracle at N = 46,080 against the reference C++ matcher's committed output."""
+    z = np.load(GOLDEN / "matcher_large.npz")
+    h, w, d, seed, top_k, recip, thr_m = (int(x) for x in z["case"])
+    a, b = matcher_inputs(h, w, d, seed)
+    o = oracle_lib.match(a, b, top_k=top_k, reciprocal=bool(recip), confidence_threshold=thr_m / 1000.0)
+    got = {(int(i), int(j)): c for i, j, c in zip(o["idx_1"], o["idx_2"], o["confidence"])}
+    want = {(int(i), int(j)): c for i, j, c in zip(z["idx_1"], z["idx_2"], z["confidence"])}
+    assert len(got) == top_k and got.keys() == want.keys()
+    assert all(np.float32(got[k]).tobytes() == np.float32(want[k]).tobytes() for k in got)
+
+
 def test_matcher_against_reference_cpp_live(oracle_lib):
     if oracle_lib.ref_lib() is None:
         pytest.skip("oracle/_ref not built (reference tree absent)")
@@ -120,6 +132,41 @@ def test_matcher_against_reference_cpp_live(oracle_lib):
             o = oracle_lib.match(a, b, top_k=64, reciprocal=recip, confidence_threshold=0.0)
             r = oracle_lib.ref_match(a, b, top_k=64, reciprocal=recip, confidence_threshold=0.0)
             assert set(zip(o["idx_1"], o["idx_2"])) == set(zip(r["idx_1"], r["idx_2"]))
+
+
+def _nan_cases():
+    """Descriptor sets with NaN / inf entries: a NaN in row 0 of either set seeds every
+    row (column) with a NaN that nothing replaces (matching.cpp:128-155); NaN elsewhere
+    never wins a comparison."""
+    cases = []
+    for kind in ("a_row7", "b_row0", "a_row0", "inf"):
+        a, b = matcher_inputs(6, 8, 24, 7)
+        a, b = a.reshape(48, 24).copy(), b.reshape(48, 24).copy()
+        if kind == "a_row7":
+            a[7] = np.nan
+        elif kind == "b_row0":
+            b[0, 3] = np.nan
+        elif kind == "a_row0":
+            a[0, 0] = np.nan
+            b[5] = np.nan
+        else:
+            a[3, 2] = np.inf
+            b[9, 0] = -np.inf
+        cases.append((kind, a.reshape(6, 8, 24), b.reshape(6, 8, 24)))
+    return cases
+
+
+@pytest.mark.parametrize("kind,a,b", _nan_cases(), ids=[c[0] for c in _nan_cases()])
+def test_matcher_non_finite_matches_reference_cpp(oracle_lib, kind, a, b):
+    if oracle_lib.ref_lib() is None:
+        pytest.skip("oracle/_ref not built (reference tree absent)")
+    for recip in (True, False):
+        o = oracle_lib.match(a, b, top_k=64, reciprocal=recip, confidence_threshold=0.0)
+        r = oracle_lib.ref_match(a, b, top_k=64, reciprocal=recip, confidence_threshold=0.0)
+        got = {(int(i), int(j)): c for i, j, c in zip(o["idx_1"], o["idx_2"], o["confidence"])}
+        want = {(int(i), int(j)): c for i, j, c in zip(r["idx_1"], r["idx_2"], r["confidence"])}
+        assert got.keys() == want.keys(), kind
+        assert all(np.float32(got[k]).tobytes() == np.float32(want[k]).tobytes() for k in got)
 
 
 def test_matcher_kats(oracle_lib):
