@@ -56,6 +56,31 @@ constexpr bool kHalfExp = false;
 template <>
 constexpr bool kHalfExp<__half> = true;
 
+#ifndef M3R_ATTN_POLY_PAIRS_F16
+#define M3R_ATTN_POLY_PAIRS_F16 4
+#endif
+#ifndef M3R_ATTN_POLY_PAIRS_BF16
+#define M3R_ATTN_POLY_PAIRS_BF16 4
+#endif
+template <class T>
+constexpr int kPolyPairs = M3R_ATTN_POLY_PAIRS_BF16;
+template <>
+constexpr int kPolyPairs<__half> = M3R_ATTN_POLY_PAIRS_F16;
+
+// the 16-bit pattern layout: mantissa bits and exponent bias + 0.5
+template <class T>
+struct Bits16;
+template <>
+struct Bits16<__half> {
+    static constexpr float kScale = 1024.0f, kBias = 15.5f, kMin = -15.5f;  // 2^(v+0.5) < 2^-14 -> (near) 0
+};
+template <>
+struct Bits16<__nv_bfloat16> {
+    static constexpr float kScale = 128.0f, kBias = 127.5f, kMin = -60.0f;
+};
+constexpr float kShifter = 12582912.0f;  // 1.5 * 2^23: x + kShifter rounds x to an integer
+constexpr float kG0 = -0.085893214f, kG1 = -0.01980106f, kG2 = 0.3431447f, kG3 = 0.07920424f;
+
 __device__ __forceinline__ float max3(float a, float b, float c) {
     float d;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
@@ -72,6 +97,53 @@ __device__ __forceinline__ float2 fma2(float a, float b, float s, float t) {
     float2 o;
     asm("mov.b64 {%0, %1}, %2;" : "=f"(o.x), "=f"(o.y) : "l"(r));
     return o;
+}
+
+__device__ __forceinline__ unsigned long long pk2(float a, float b) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ unsigned long long fma2v(unsigned long long a, unsigned long long b, unsigned long long c) {
+    unsigned long long r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ unsigned long long add2v(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ unsigned long long sub2v(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+// 16-bit pair (low half first) of 2^(s0 * sl2 - mh + 0.5), 2^(s1 * sl2 - mh + 0.5) on
+// the FMA pipe (see the comment on kPolyPairs); mh = the row's offset + 0.5.
+template <class T>
+__device__ __forceinline__ uint32_t exp2_poly2(float s0, float s1, float sl2, float mh) {
+    float v0, v1;
+    {
+        const unsigned long long v = fma2v(pk2(s0, s1), pk2(sl2, sl2), pk2(-mh, -mh));
+        asm("mov.b64 {%0, %1}, %2;" : "=f"(v0), "=f"(v1) : "l"(v));
+    }
+    v0 = fmaxf(v0, Bits16<T>::kMin);
+    v1 = fmaxf(v1, Bits16<T>::kMin);
+    const unsigned long long v = pk2(v0, v1);
+    const unsigned long long sh = pk2(kShifter, kShifter);
+    const unsigned long long n = sub2v(add2v(v, sh), sh);  // round(v)
+    const unsigned long long f = sub2v(v, n);               // in [-0.5, 0.5]
+    unsigned long long q = fma2v(f, pk2(kG3, kG3), pk2(kG2, kG2));
+    q = fma2v(q, f, pk2(kG1, kG1));
+    q = fma2v(q, f, pk2(kG0, kG0));                         // g(f + 0.5)
+    const unsigned long long t = add2v(v, q);
+    constexpr float kC = kShifter + Bits16<T>::kScale * Bits16<T>::kBias;
+    const unsigned long long y = fma2v(t, pk2(Bits16<T>::kScale, Bits16<T>::kScale), pk2(kC, kC));
+    uint32_t y0, y1;
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(y0), "=r"(y1) : "l"(y));
+    return __byte_perm(y0, y1, 0x5410);  // low 16 bits of each
 }
 
 // fp16 pair (low half = x0) of 2^x0, 2^x1
@@ -326,8 +398,12 @@ __global__ void __launch_bounds__(kThreads, 2)
                 for (int c = 0; c < 2; ++c)
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
-                        const float2 x = fma2(__uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1]), sl2, -m_new);
-                        pk[c][i] = ex2_h2(x.x, x.y);
+                        if (i < kPolyPairs<T>) {
+                            pk[c][i] = exp2_poly2<T>(__uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1]), sl2, m_new + 0.5f);
+                        } else {
+                            const float2 x = fma2(__uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1]), sl2, -m_new);
+                            pk[c][i] = ex2_h2(x.x, x.y);
+                        }
                         const int u = 2 * (i & 3);
                         add_h2_f32(rs[u], rs[u + 1], pk[c][i]);
                     }
@@ -341,6 +417,14 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         const int c0 = c * 32 + 2 * i;
+                        if (full_half && i < kPolyPairs<T>) {  // bf16: exponentials on the FMA pipe
+                            pk[c][i] = exp2_poly2<T>(__uint_as_float(v[c][2 * i]), __uint_as_float(v[c][2 * i + 1]), sl2,
+                                                     m_new + 0.5f);
+                            const float2 pf = Elem<T>::unpack(pk[c][i]);
+                            rs[2 * (i & 3)] += pf.x;
+                            rs[2 * (i & 3) + 1] += pf.y;
+                            continue;
+                        }
                         float p0 = ex2_approx(__uint_as_float(v[c][2 * i]) * sl2 - m_new);
                         float p1 = ex2_approx(__uint_as_float(v[c][2 * i + 1]) * sl2 - m_new);
                         if (!full_half) {
