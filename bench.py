@@ -484,6 +484,29 @@ def run_ours(args):
                  "ops": {k: [round(o["ms"], 3), round(o["flop"] / (o["ms"] * 1e-3) / 1e12, 1) if o["ms"] > 0 else 0.0]
                          for k, o in o_ops.items()}}
 
+    # ---------------- one pair per call through the object NativeEngineWrapper drives
+    latency = None
+    if rank == 0 and not args.no_e2e:
+        from mast3r_runtime_b200 import CUDAEngine
+
+        ce = CUDAEngine(variant=VARIANT, precision=args.dtype, image_size=IMAGE_HW, devices=[local_rank])
+        ce.load(str(path))
+        ce.warmup(3)
+        lat = []
+        for i in range(10):
+            t0 = time.perf_counter()
+            r = ce.infer(img1[i % per], img2[i % per])
+            lat.append(1000.0 * (time.perf_counter() - t0))
+        t0 = time.perf_counter()
+        m = ce.match(r.desc_1, r.desc_2, top_k=MATCH_TOP_K, reciprocal=True, confidence_threshold=MATCH_THR)
+        match_ms = 1000.0 * (time.perf_counter() - t0)
+        latency = {"infer_ms_per_pair": statistics.median(lat), "match_ms": match_ms, "matches": int(len(m.idx_1)),
+                   "path": "CUDAEngine.infer(img1, img2) -> numpy (the call NativeEngineWrapper.infer makes, "
+                           "native_wrapper.py:84-97), one 384x512 pair, host wall time, median of 10"}
+        for e in list(ce._engines.values()) + ([ce._matcher] if ce._matcher is not None else []):
+            e.close()
+    barrier()
+
     # ---------------- matcher at N = 196,608 (rank 0 drives all N GPUs; the others wait)
     matcher = None
     barrier()
@@ -555,6 +578,7 @@ def run_ours(args):
                     for k, o in ops.items()},
             "other_dtype": other,
             "e2e": e2e_line,
+            "latency": latency,
             "wall_ms_per_step": 1000.0 * wall / args.steps,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,

@@ -134,6 +134,12 @@ int m3r_fetch_outputs(m3r_engine* engine, int n_pairs, float* pts3d_1, float* pt
  * out[4] other kernels ms, out[5] GEMM launches, out[6] attention launches,
  * out[7] other launches.  Values are for device 0 of the engine. */
 int m3r_set_profiling(m3r_engine* engine, int on);
+
+/* Limit (ns) of every bounded device-side wait of the engine's kernels (0 = the default,
+ * two seconds).  A kernel whose wait runs out stops, and the call that launched it
+ * returns M3R_ERR_TIMEOUT; the CUDA context stays usable.  No reference counterpart:
+ * the reference's CUDA backend has no device-side pipeline waits. */
+int m3r_set_wait_timeout(m3r_engine* engine, unsigned long long ns);
 int m3r_get_profile(const m3r_engine* engine, double* out8);
 
 /* The same profile per operation of the model ("enc.qkv", "enc.attn", "dec.fc2",
@@ -171,6 +177,19 @@ int m3r_conv3_test(int device, int dtype, const uint16_t* x, const uint16_t* w, 
  * normalised descriptors, and the row maxima best_12 [n1]. */
 int m3r_match_nn(int device, const float* desc_1, const float* desc_2, int64_t n1, int64_t n2, int desc_dim,
                  int32_t* nn_12, int32_t* nn_21, float* best_12, float* kernel_ms);
+
+/* Self-test of the bounded device waits: a kernel waits on a barrier that nothing
+ * signals, with the wait limit limit_ns (0 < limit_ns <= 10 s).  Returns M3R_ERR_TIMEOUT
+ * (the expected outcome) with *device_code = the code the wait recorded, after which the
+ * device is usable as before.  Errors: m3r_global_error(). */
+int m3r_wait_selftest(int device, unsigned long long limit_ns, int* device_code);
+
+/* Validates a checkpoint against a model configuration on the host only (no GPU): every
+ * tensor the engine loads is present, F32 / F16 / BF16, with the expected shape, and the
+ * file is a well-formed safetensors file.  Returns M3R_OK or M3R_ERR_IO / M3R_ERR_ARG
+ * with the reason in m3r_global_error().  Same checks as m3r_load (native_wrapper.py:57
+ * loads through it). */
+int m3r_check_checkpoint(const m3r_config* cfg, const char* safetensors_path);
 
 /* m3r_match_nn without any device allocation (no counterpart in the reference).
  * For callers that must not allocate GPU memory while running -- a real-time loop

@@ -87,6 +87,9 @@ SIGNATURES = {
     "m3r_conv3_test": (_I, [_I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I]),
     "m3r_match_nn": (_I, [_I, _P, _P, _I64, _I64, _I, _P, _P, _P, ctypes.POINTER(_F)]),
     "m3r_match_nn_static": (_I, [_I, _P, _P, _I64, _I64, _I, _P, _P, _P, _P]),
+    "m3r_set_wait_timeout": (_I, [_P, ctypes.c_ulonglong]),
+    "m3r_wait_selftest": (_I, [_I, ctypes.c_ulonglong, ctypes.POINTER(_I)]),
+    "m3r_check_checkpoint": (_I, [ctypes.POINTER(M3RConfig), ctypes.c_char_p]),
 }
 
 _lib = None

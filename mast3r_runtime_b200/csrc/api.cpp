@@ -7,6 +7,7 @@
 
 #include "../../include/m3r_cuda.h"
 #include "attention.h"
+#include "common.cuh"
 #include "engine.h"
 #include "gemm.h"
 #include "matcher.h"
@@ -24,7 +25,7 @@ template <class F>
 int guarded(m3r_engine* e, F&& fn) {
     try {
         fn();
-        if (e) e->err.clear();
+        (e ? e->err : g_err).clear();
         return M3R_OK;
     } catch (const m3r::Error& x) {
         (e ? e->err : g_err) = x.what();
@@ -147,6 +148,13 @@ int m3r_load(m3r_engine* engine, const char* path) {
     });
 }
 
+int m3r_check_checkpoint(const m3r_config* cfg, const char* path) {
+    return guarded(nullptr, [&] {
+        M3R_REQUIRE(cfg != nullptr && path != nullptr, "null argument");
+        m3r::check_checkpoint(path, m3r::Dims::from(*cfg));
+    });
+}
+
 int m3r_is_ready(const m3r_engine* engine) { return engine && engine->impl && engine->impl->ready() ? 1 : 0; }
 
 int m3r_infer(m3r_engine* engine, const uint8_t* img1, const uint8_t* img2, int n_pairs, float* pts3d_1,
@@ -205,6 +213,11 @@ int m3r_set_profiling(m3r_engine* engine, int on) {
     return M3R_OK;
 }
 
+int m3r_set_wait_timeout(m3r_engine* engine, unsigned long long ns) {
+    if (!engine) return M3R_ERR_ARG;
+    return guarded(engine, [&] { engine->impl->set_wait_timeout(ns); });
+}
+
 int m3r_get_profile(const m3r_engine* engine, double* out8) {
     if (!engine || !out8) return M3R_ERR_ARG;
     engine->impl->profile(out8);
@@ -243,11 +256,11 @@ int m3r_attention_fwd(int device, int dtype, const uint16_t* q, const uint16_t* 
         M3R_REQUIRE(q && k && v && out && n_seq > 0 && heads > 0 && nq > 0 && nk > 0, "attention: bad arguments");
         m3r::DeviceGuard g(device);
         const size_t qn = static_cast<size_t>(n_seq) * heads * nq * 64, kn = static_cast<size_t>(n_seq) * heads * nk * 64;
-        DBuf dq(qn * 2), dk(kn * 2), dv(kn * 2), dout(qn * 2), derr(sizeof(int));
+        DBuf dq(qn * 2), dk(kn * 2), dv(kn * 2), dout(qn * 2), derr(sizeof(m3r::DevStatus));
         M3R_CUDA(cudaMemcpy(dq.p, q, qn * 2, cudaMemcpyHostToDevice));
         M3R_CUDA(cudaMemcpy(dk.p, k, kn * 2, cudaMemcpyHostToDevice));
         M3R_CUDA(cudaMemcpy(dv.p, v, kn * 2, cudaMemcpyHostToDevice));
-        M3R_CUDA(cudaMemset(derr.p, 0, sizeof(int)));
+        M3R_CUDA(cudaMemset(derr.p, 0, sizeof(m3r::DevStatus)));
         const int it = iters < 1 ? 1 : iters;
         Events ev;
         m3r::attention_fwd(nullptr, dtype, dq.p, dk.p, dv.p, dout.p, n_seq, heads, nq, nk, scale, derr.as<int>());
@@ -268,11 +281,11 @@ int m3r_gemm_test(int device, int dtype, const uint16_t* a, const uint16_t* w, c
         M3R_REQUIRE(a && w && c && M > 0 && N > 0 && K > 0 && K % 8 == 0 && N % 4 == 0, "gemm_test: bad arguments");
         m3r::DeviceGuard g(device);
         DBuf da(static_cast<size_t>(M) * K * 2), dw(static_cast<size_t>(N) * K * 2), dc(static_cast<size_t>(M) * N * 4),
-            db(static_cast<size_t>(N) * 4), derr(sizeof(int));
+            db(static_cast<size_t>(N) * 4), derr(sizeof(m3r::DevStatus));
         M3R_CUDA(cudaMemcpy(da.p, a, static_cast<size_t>(M) * K * 2, cudaMemcpyHostToDevice));
         M3R_CUDA(cudaMemcpy(dw.p, w, static_cast<size_t>(N) * K * 2, cudaMemcpyHostToDevice));
         if (bias) M3R_CUDA(cudaMemcpy(db.p, bias, static_cast<size_t>(N) * 4, cudaMemcpyHostToDevice));
-        M3R_CUDA(cudaMemset(derr.p, 0, sizeof(int)));
+        M3R_CUDA(cudaMemset(derr.p, 0, sizeof(m3r::DevStatus)));
         m3r::GemmParams p = m3r::gemm_params();
         p.bias = bias ? db.as<float>() : nullptr;
         p.out = dc.p;
@@ -300,11 +313,11 @@ int m3r_conv3_test(int device, int dtype, const uint16_t* x, const uint16_t* w, 
         const int cpad = (c + 63) / 64 * 64;
         const size_t xn = static_cast<size_t>(n) * h * wd * c, wn = static_cast<size_t>(cout) * 9 * cpad,
                      yn = static_cast<size_t>(n) * h * wd * cout;
-        DBuf dx(xn * 2), dw(wn * 2), dy(yn * 4), db(static_cast<size_t>(cout) * 4), derr(sizeof(int));
+        DBuf dx(xn * 2), dw(wn * 2), dy(yn * 4), db(static_cast<size_t>(cout) * 4), derr(sizeof(m3r::DevStatus));
         M3R_CUDA(cudaMemcpy(dx.p, x, xn * 2, cudaMemcpyHostToDevice));
         M3R_CUDA(cudaMemcpy(dw.p, w, wn * 2, cudaMemcpyHostToDevice));
         if (bias) M3R_CUDA(cudaMemcpy(db.p, bias, static_cast<size_t>(cout) * 4, cudaMemcpyHostToDevice));
-        M3R_CUDA(cudaMemset(derr.p, 0, sizeof(int)));
+        M3R_CUDA(cudaMemset(derr.p, 0, sizeof(m3r::DevStatus)));
         m3r::GemmParams p = m3r::gemm_params();
         p.bias = bias ? db.as<float>() : nullptr;
         p.out = dy.p;

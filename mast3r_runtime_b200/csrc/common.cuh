@@ -15,6 +15,8 @@ namespace m3r {
 // ---------------------------------------------------------------- error flag
 // A kernel whose bounded wait runs out records a code in the int the host
 // passed it (err) and returns; the host reads that int after synchronising.
+// `err` points at a 16-byte device status block (DevStatus): the code, and the
+// wait limit in ns that every bounded wait of the launch uses (0: kWaitTimeoutNs).
 enum DeviceError : int {
     kDevOk = 0,
     kDevTimeoutProducer = 1,
@@ -24,9 +26,16 @@ enum DeviceError : int {
     kDevBadSmemAlign = 5,  // dynamic shared memory not at the alignment the kernel declares
 };
 
-// Spin budget for every mbarrier wait: the wait gives up after about two
+// Default spin budget of every mbarrier wait: the wait gives up after about two
 // seconds of global time, far above any legitimate wait in these kernels.
 constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;
+
+struct DevStatus {
+    int code;                   // DeviceError of the first wait that ran out (0: none)
+    int reserved;
+    unsigned long long wait_ns;  // limit of every bounded wait (0: kWaitTimeoutNs)
+};
+static_assert(sizeof(DevStatus) == 16, "device status block layout");
 
 __device__ __forceinline__ unsigned long long global_timer_ns() {
     unsigned long long t;
@@ -77,7 +86,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // role of the CTA has already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int code, int* err) {
     if (mbar_try_wait(bar, parity)) return true;
-    unsigned long long t0 = 0;
+    unsigned long long t0 = 0, limit = kWaitTimeoutNs;
     uint32_t it = 0;
     while (!mbar_try_wait(bar, parity)) {
         if ((++it & 255u) == 0) {
@@ -85,7 +94,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
             const unsigned long long now = global_timer_ns();
             if (t0 == 0) {
                 t0 = now;
-            } else if (now - t0 > kWaitTimeoutNs) {
+                if (err) {
+                    const unsigned long long w = reinterpret_cast<const volatile DevStatus*>(err)->wait_ns;
+                    if (w != 0) limit = w;
+                }
+            } else if (now - t0 > limit) {
                 if (err) atomicCAS(err, 0, code);
                 *abort = 1;
                 return false;

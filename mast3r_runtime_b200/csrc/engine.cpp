@@ -13,6 +13,7 @@
 #include "engine.h"
 
 #include <algorithm>
+#include <cstddef>
 #include <array>
 #include <map>
 #include <mutex>
@@ -94,6 +95,26 @@ uint16_t to16bits(float f, int dt) {
     return r;
 }
 
+// memcpy split over host threads (large copies between pinned staging and pageable
+// caller memory run at several times one thread's bandwidth)
+void parallel_memcpy(void* dst, const void* src, size_t n) {
+    constexpr size_t kChunk = size_t(16) << 20;
+    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    const size_t nt = std::min<size_t>(std::min<size_t>(8, hw), (n + kChunk - 1) / kChunk);
+    if (nt <= 1) {
+        std::memcpy(dst, src, n);
+        return;
+    }
+    std::vector<std::thread> th;
+    const size_t per = (n + nt - 1) / nt;
+    for (size_t t = 0; t < nt; ++t) {
+        const size_t b = t * per, e = std::min(n, b + per);
+        if (b >= e) break;
+        th.emplace_back([=] { std::memcpy(static_cast<char*>(dst) + b, static_cast<const char*>(src) + b, e - b); });
+    }
+    for (auto& x : th) x.join();
+}
+
 struct HostLin {
     std::vector<uint16_t> w;  // 16-bit operand bits [out, in]
     std::vector<float> b;     // may be empty
@@ -142,8 +163,8 @@ public:
         DeviceGuard g(dev_);
         M3R_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
         M3R_CUDA(cudaStreamCreateWithFlags(&copy_stream_, cudaStreamNonBlocking));
-        err_ = static_cast<int*>(alloc(sizeof(int)));
-        M3R_CUDA(cudaMemset(err_, 0, sizeof(int)));
+        err_ = static_cast<int*>(alloc(sizeof(DevStatus)));
+        M3R_CUDA(cudaMemset(err_, 0, sizeof(DevStatus)));
         for (int i = 0; i < 8; ++i) M3R_CUDA(cudaEventCreate(&stage_ev_[i]));
         alloc_activations();
     }
@@ -162,6 +183,8 @@ public:
         }
         for (void* p : allocs_) cudaFree(p);
         if (stream_) cudaStreamDestroy(stream_);
+        for (void* p : {stage_in_, stage_out_[0], stage_out_[1]})
+            if (p) cudaFreeHost(p);
     }
 
     int dev() const { return dev_; }
@@ -403,22 +426,26 @@ public:
     // embedding, encoder, decoder, heads) with a timing event (ev[0..4]) before and
     // after each.  The first pass for a given (n, slot) launches directly (it also sets
     // the kernels' attributes); later passes replay one CUDA graph per stage, captured
-    // on the second pass.  Profiled passes always launch directly (events around every
-    // launch).  enqueue_forward only enqueues; forward also waits and reads the timings.
+    // on the second pass.  Only the patch stage (reads the input slot) and the heads
+    // (write the output slot) depend on the slot: the encoder and decoder graphs are
+    // shared by every slot of a pair count.  Profiled passes always launch directly
+    // (events around every launch).  enqueue_forward only enqueues; forward also waits
+    // and reads the timings.
     static constexpr int kStages = 4;
     void enqueue_forward(int n, int slot, const cudaEvent_t* ev) {
         DeviceGuard g(dev_);
         profiling_reset();
         const std::pair<int, int> key(n, slot);
         const bool use_graph = !profiling && direct_runs_[key]++ > 0;
-        auto& gs = graphs_[key];
         M3R_CUDA(cudaEventRecord(ev[0], stream_));
         for (int st = 0; st < kStages; ++st) {
             if (!use_graph) {
                 enqueue_stage(st, n, slot);
             } else {
-                if (gs[st] == nullptr) gs[st] = capture_stage(st, n, slot);
-                M3R_CUDA(cudaGraphLaunch(gs[st], stream_));
+                const bool slotted = st == 0 || st == kStages - 1;
+                cudaGraphExec_t& ge = graphs_[std::make_pair(n, slotted ? slot : -1)][st];
+                if (ge == nullptr) ge = capture_stage(st, n, slot);
+                M3R_CUDA(cudaGraphLaunch(ge, stream_));
             }
             M3R_CUDA(cudaEventRecord(ev[st + 1], stream_));
         }
@@ -651,6 +678,11 @@ public:
     // device's first pair.  stage_ms[5] (summed over sub-batches), *h2d_ms (input
     // copies), *d2h_ms (output copies, summed) are device times.  Afterwards the input
     // slots hold these n pairs, as after stage().
+    // Pageable (not page-locked) caller buffers would make every copy synchronous with
+    // the host thread and serialise copies and compute, so they pass through this
+    // device's pinned staging slots instead: the inputs in one multi-threaded host copy,
+    // the outputs of sub-batch k into slot k % 2, copied on to the caller's arrays by
+    // host threads while the GPU computes and copies the next sub-batches.
     static constexpr int kChunkEvents = 8;
     void infer_pipelined(const uint8_t* img1, const uint8_t* img2, int n, float* const outs[6], float* stage_ms,
                          float* h2d_ms, float* d2h_ms) {
@@ -668,52 +700,120 @@ public:
         const size_t px = static_cast<size_t>(d_.H) * d_.W;
         const int per_px[3] = {3, d_.desc_dim, 1};
         const float* bases[3] = {o_pts, o_desc, o_conf};
+        const bool in_pageable = is_pageable(img1) || is_pageable(img2);
+        bool out_pageable = false;
+        for (int i = 0; i < 6; ++i) out_pageable = out_pageable || (outs[i] && is_pageable(outs[i]));
+        const size_t pair_out_bytes = sizeof(float) * px * (3 + d_.desc_dim + 1) * 2;
         const bool prof = profiling;
         profiling = false;  // per-launch profiling is a run_resident feature
-        M3R_CUDA(cudaEventRecord(chunk_ev_[0], copy_stream_));
-        for (int k = 0; k < nsub; ++k) {
-            const int slot = k * c, nk = std::min(c, n - slot);
-            if (nk <= 0) break;
-            M3R_CUDA(cudaMemcpyAsync(img_slot(0, slot), img1 + slot * ib, nk * ib, cudaMemcpyHostToDevice, copy_stream_));
-            M3R_CUDA(cudaMemcpyAsync(img_slot(1, slot), img2 + slot * ib, nk * ib, cudaMemcpyHostToDevice, copy_stream_));
-            M3R_CUDA(cudaEventRecord(ev(k, 5), copy_stream_));
+        try {
+            const uint8_t* src1 = img1;
+            const uint8_t* src2 = img2;
+            if (in_pageable) {
+                uint8_t* st = static_cast<uint8_t*>(pinned(stage_in_, stage_in_cap_, 2 * n * ib));
+                parallel_memcpy(st, img1, n * ib);
+                parallel_memcpy(st + n * ib, img2, n * ib);
+                src1 = st;
+                src2 = st + n * ib;
+            }
+            if (out_pageable)
+                for (int sslot = 0; sslot < 2; ++sslot) pinned(stage_out_[sslot], stage_out_cap_[sslot], c * pair_out_bytes);
+            M3R_CUDA(cudaEventRecord(chunk_ev_[0], copy_stream_));
+            for (int k = 0; k < nsub; ++k) {
+                const int slot = k * c, nk = std::min(c, n - slot);
+                if (nk <= 0) break;
+                M3R_CUDA(cudaMemcpyAsync(img_slot(0, slot), src1 + slot * ib, nk * ib, cudaMemcpyHostToDevice, copy_stream_));
+                M3R_CUDA(cudaMemcpyAsync(img_slot(1, slot), src2 + slot * ib, nk * ib, cudaMemcpyHostToDevice, copy_stream_));
+                M3R_CUDA(cudaEventRecord(ev(k, 5), copy_stream_));
+            }
+            // destination of output kind/view of sub-batch k: the caller's array, or the
+            // staging slot k % 2 (laid out as the caller's arrays for nk pairs)
+            auto out_dst = [&](int k, int kind, int view, int nk) -> float* {
+                const int slot = k * c;
+                if (!out_pageable) return outs[2 * kind + view] + slot * px * per_px[kind];
+                float* base = static_cast<float*>(stage_out_[k % 2]);
+                size_t off = 0;
+                for (int q = 0; q < 2 * kind + view; ++q) off += static_cast<size_t>(nk) * px * per_px[q / 2];
+                return base + off;
+            };
+            // staged sub-batch k -> the caller's arrays (host threads)
+            auto unstage = [&](int k) {
+                const int slot = k * c, nk = std::min(c, n - slot);
+                M3R_CUDA(cudaEventSynchronize(ev(k, 7)));
+                for (int kind = 0; kind < 3; ++kind)
+                    for (int view = 0; view < 2; ++view)
+                        if (outs[2 * kind + view])
+                            parallel_memcpy(outs[2 * kind + view] + slot * px * per_px[kind], out_dst(k, kind, view, nk),
+                                            sizeof(float) * nk * px * per_px[kind]);
+            };
+            int last = 0;
+            for (int k = 0; k < nsub; ++k) {
+                const int slot = k * c, nk = std::min(c, n - slot);
+                if (nk <= 0) break;
+                last = k;
+                M3R_CUDA(cudaStreamWaitEvent(stream_, ev(k, 5), 0));
+                const cudaEvent_t sev[5] = {ev(k, 0), ev(k, 1), ev(k, 2), ev(k, 3), ev(k, 4)};
+                enqueue_forward(nk, slot, sev);
+                if (out_pageable && k >= 2) unstage(k - 2);  // frees staging slot k % 2
+                M3R_CUDA(cudaStreamWaitEvent(copy_stream_, ev(k, 4), 0));
+                M3R_CUDA(cudaEventRecord(ev(k, 6), copy_stream_));
+                for (int kind = 0; kind < 3; ++kind)
+                    for (int view = 0; view < 2; ++view) {
+                        if (!outs[2 * kind + view]) continue;
+                        M3R_CUDA(cudaMemcpyAsync(out_dst(k, kind, view, nk), out_slot(bases[kind], per_px[kind], view, slot),
+                                                 sizeof(float) * nk * px * per_px[kind], cudaMemcpyDeviceToHost,
+                                                 copy_stream_));
+                    }
+                M3R_CUDA(cudaEventRecord(ev(k, 7), copy_stream_));
+            }
+            if (out_pageable)
+                for (int k = std::max(0, last - 1); k <= last; ++k) unstage(k);
+            profiling = prof;
+            M3R_CUDA(cudaStreamSynchronize(copy_stream_));
+            M3R_CUDA(cudaStreamSynchronize(stream_));
+            staged = n;
+            check_error();
+            for (int i = 0; i < 5; ++i) stage_ms[i] = 0.0f;
+            *d2h_ms = 0.0f;
+            for (int k = 0; k <= last; ++k) {
+                float sm[5];
+                const cudaEvent_t sev[5] = {ev(k, 0), ev(k, 1), ev(k, 2), ev(k, 3), ev(k, 4)};
+                stage_times(sev, sm);
+                for (int i = 0; i < 5; ++i) stage_ms[i] += sm[i];
+                float ms;
+                M3R_CUDA(cudaEventElapsedTime(&ms, ev(k, 6), ev(k, 7)));
+                *d2h_ms += ms;
+            }
+            M3R_CUDA(cudaEventElapsedTime(h2d_ms, chunk_ev_[0], ev(last, 5)));
+        } catch (...) {
+            // no copy may still read or write the caller's buffers once the call returns
+            profiling = prof;
+            cudaStreamSynchronize(copy_stream_);
+            cudaStreamSynchronize(stream_);
+            cudaGetLastError();
+            throw;
         }
-        int last = 0;
-        for (int k = 0; k < nsub; ++k) {
-            const int slot = k * c, nk = std::min(c, n - slot);
-            if (nk <= 0) break;
-            last = k;
-            M3R_CUDA(cudaStreamWaitEvent(stream_, ev(k, 5), 0));
-            const cudaEvent_t sev[5] = {ev(k, 0), ev(k, 1), ev(k, 2), ev(k, 3), ev(k, 4)};
-            enqueue_forward(nk, slot, sev);
-            M3R_CUDA(cudaStreamWaitEvent(copy_stream_, ev(k, 4), 0));
-            M3R_CUDA(cudaEventRecord(ev(k, 6), copy_stream_));
-            for (int kind = 0; kind < 3; ++kind)
-                for (int view = 0; view < 2; ++view) {
-                    float* dst = outs[2 * kind + view];
-                    if (!dst) continue;
-                    M3R_CUDA(cudaMemcpyAsync(dst + slot * px * per_px[kind], out_slot(bases[kind], per_px[kind], view, slot),
-                                             sizeof(float) * nk * px * per_px[kind], cudaMemcpyDeviceToHost, copy_stream_));
-                }
-            M3R_CUDA(cudaEventRecord(ev(k, 7), copy_stream_));
+    }
+
+    static bool is_pageable(const void* p) {
+        cudaPointerAttributes a;
+        if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+            cudaGetLastError();
+            return true;
         }
-        profiling = prof;
-        M3R_CUDA(cudaStreamSynchronize(copy_stream_));
-        M3R_CUDA(cudaStreamSynchronize(stream_));
-        staged = n;
-        check_error();
-        for (int i = 0; i < 5; ++i) stage_ms[i] = 0.0f;
-        *d2h_ms = 0.0f;
-        for (int k = 0; k <= last; ++k) {
-            float sm[5];
-            const cudaEvent_t sev[5] = {ev(k, 0), ev(k, 1), ev(k, 2), ev(k, 3), ev(k, 4)};
-            stage_times(sev, sm);
-            for (int i = 0; i < 5; ++i) stage_ms[i] += sm[i];
-            float ms;
-            M3R_CUDA(cudaEventElapsedTime(&ms, ev(k, 6), ev(k, 7)));
-            *d2h_ms += ms;
+        return a.type == cudaMemoryTypeUnregistered;
+    }
+
+    // pinned staging block of at least `need` bytes (kept and grown as needed)
+    static void* pinned(void*& p, size_t& cap, size_t need) {
+        if (cap < need) {
+            if (p) M3R_CUDA(cudaFreeHost(p));
+            p = nullptr;
+            cap = 0;
+            M3R_CUDA(cudaHostAlloc(&p, need, cudaHostAllocPortable));
+            cap = need;
         }
-        M3R_CUDA(cudaEventElapsedTime(h2d_ms, chunk_ev_[0], ev(last, 5)));
+        return p;
     }
 
     void check_error() {
@@ -727,6 +827,14 @@ public:
 
     int* err_ptr() const { return err_; }
 
+    // limit of every bounded device wait of this device's launches (0: the default)
+    void set_wait_limit(unsigned long long ns) {
+        DeviceGuard g(dev_);
+        M3R_CUDA(cudaStreamSynchronize(stream_));
+        M3R_CUDA(cudaMemcpy(reinterpret_cast<char*>(err_) + offsetof(DevStatus, wait_ns), &ns, sizeof(ns),
+                            cudaMemcpyHostToDevice));
+    }
+
 private:
     void profiling_reset() { prof_rec_.clear(); }
 
@@ -735,11 +843,16 @@ private:
     int max_pairs_;
     cudaStream_t stream_ = nullptr;
     cudaStream_t copy_stream_ = nullptr;  // host <-> device copies of pipelined infer
+    void* stage_in_ = nullptr;            // pinned staging of pageable caller buffers
+    size_t stage_in_cap_ = 0;
+    void* stage_out_[2] = {nullptr, nullptr};
+    size_t stage_out_cap_[2] = {0, 0};
     std::vector<cudaEvent_t> chunk_ev_;   // per sub-batch: 5 stage events, input, 2 output-copy events
     int* err_ = nullptr;
     cudaEvent_t stage_ev_[8];
     std::vector<void*> allocs_;
-    std::map<std::pair<int, int>, std::array<cudaGraphExec_t, 4>> graphs_;  // forward stages per (pairs, slot)
+    // forward-stage graphs per (pairs, slot); slot -1 holds the slot-independent stages
+    std::map<std::pair<int, int>, std::array<cudaGraphExec_t, 4>> graphs_;
     std::map<std::pair<int, int>, int> direct_runs_;
 };
 
@@ -768,10 +881,39 @@ Engine::~Engine() {
     }
 }
 
-void Engine::load(const std::string& path) {
+namespace {
+// ---------------------------------------------------------------------------- host-side checkpoint
+// Every tensor the engine uploads, read from a checkpoint and converted on the host
+// (16-bit operand bits, tap-major conv weights, folded norm_y, RoPE tables).
+struct HostEnc {
+    std::vector<float> n1g, n1b, n2g, n2b;
+    HostLin qkv, proj, fc1, fc2;
+};
+struct HostDec {
+    std::vector<float> n[8];
+    HostLin qkv, proj, q, kv, cproj, fc1, fc2;
+};
+struct HostHead {
+    HostLin ap0_0, ap0_1t, ap1_0, ap1_1t, ap2_0, ap3_0, ap3_1, rn[4], hd0, hd2, lf1, lf2;
+    std::vector<float> w4, b4;
+};
+struct HostModel {
+    HostLin patch;
+    std::vector<HostEnc> enc;
+    std::vector<float> eng, enb;
+    HostLin dembed;
+    std::vector<HostDec> dec[2];
+    std::vector<float> dng, dnb;
+    HostHead hh[2];
+    std::vector<float> rope_cos, rope_sin;
+};
+
+// Reads and converts a checkpoint for the model `d` (host only; throws Error(kErrIo)
+// on a missing, malformed or wrongly-shaped tensor).
+HostModel read_model(const std::string& path, const Dims& d) {
     SafetensorsFile f(path);
-    const int dt = d_.dt;
-    const Dims& d = d_;
+    const int dt = d.dt;
+    HostModel M;
     auto L = [&](const std::string& name, int out, int in, bool bias = true) {
         auto w = f.load_f32(name + ".weight", {out, in});
         std::vector<float> b;
@@ -782,7 +924,7 @@ void Engine::load(const std::string& path) {
 
     // patch embedding [D, 3, p, p] -> [D, kpad]
     const int p = d.patch, kp = 3 * p * p;
-    HostLin patch;
+    HostLin& patch = M.patch;
     {
         auto w = f.load_f32("patch_embed.proj.weight", {d.enc_dim, 3, p, p});
         std::vector<float> t(static_cast<size_t>(d.enc_dim) * d.kpad, 0.0f);
@@ -790,11 +932,8 @@ void Engine::load(const std::string& path) {
             for (int kk = 0; kk < kp; ++kk) t[static_cast<size_t>(o) * d.kpad + kk] = w[static_cast<size_t>(o) * kp + kk];
         patch = to16(dt, t, d.enc_dim, d.kpad, V("patch_embed.proj.bias", d.enc_dim));
     }
-    struct HostEnc {
-        std::vector<float> n1g, n1b, n2g, n2b;
-        HostLin qkv, proj, fc1, fc2;
-    };
-    std::vector<HostEnc> enc(d.enc_depth);
+    std::vector<HostEnc>& enc = M.enc;
+    enc.resize(d.enc_depth);
     for (int i = 0; i < d.enc_depth; ++i) {
         const std::string b = "enc_blocks." + std::to_string(i) + ".";
         HostEnc& e = enc[i];
@@ -807,13 +946,10 @@ void Engine::load(const std::string& path) {
         e.fc1 = L(b + "mlp.fc1", d.enc_mlp, d.enc_dim);
         e.fc2 = L(b + "mlp.fc2", d.enc_dim, d.enc_mlp);
     }
-    const auto eng = V("enc_norm.weight", d.enc_dim), enb = V("enc_norm.bias", d.enc_dim);
-    const HostLin dembed = L("decoder_embed", d.dec_dim, d.enc_dim);
-    struct HostDec {
-        std::vector<float> n[8];
-        HostLin qkv, proj, q, kv, cproj, fc1, fc2;
-    };
-    std::vector<HostDec> dec[2];
+    M.eng = V("enc_norm.weight", d.enc_dim);
+    M.enb = V("enc_norm.bias", d.enc_dim);
+    M.dembed = L("decoder_embed", d.dec_dim, d.enc_dim);
+    std::vector<HostDec>* dec = M.dec;
     const int Dd = d.dec_dim;
     for (int view = 0; view < 2; ++view) {
         dec[view].resize(d.dec_depth);
@@ -854,12 +990,9 @@ void Engine::load(const std::string& path) {
             e.fc2 = L(b + "mlp.fc2", Dd, d.dec_mlp);
         }
     }
-    const auto dng = V("dec_norm.weight", Dd), dnb = V("dec_norm.bias", Dd);
-    struct HostHead {
-        HostLin ap0_0, ap0_1t, ap1_0, ap1_1t, ap2_0, ap3_0, ap3_1, rn[4], hd0, hd2, lf1, lf2;
-        std::vector<float> w4, b4;
-    };
-    HostHead hh[2];
+    M.dng = V("dec_norm.weight", Dd);
+    M.dnb = V("dec_norm.bias", Dd);
+    HostHead* hh = M.hh;
     const int dpt[4] = {96, 192, 384, 768};
     for (int view = 0; view < 2; ++view) {
         const std::string t = std::string(view == 0 ? "downstream_head1" : "downstream_head2") + ".dpt.";
@@ -906,7 +1039,10 @@ void Engine::load(const std::string& path) {
     // RoPE tables (rope2d.py:77-92): freq_i = 1 / 100^(i/16), angle = pos * freq_i in float32;
     // frequency-major [16][maxpos] (the QKV epilogue reads a warp's consecutive tokens)
     const int maxpos = std::max(d.hg, d.wg);
-    std::vector<float> rc(static_cast<size_t>(maxpos) * 16), rs(static_cast<size_t>(maxpos) * 16);
+    std::vector<float>& rc = M.rope_cos;
+    std::vector<float>& rs = M.rope_sin;
+    rc.assign(static_cast<size_t>(maxpos) * 16, 0.0f);
+    rs.assign(static_cast<size_t>(maxpos) * 16, 0.0f);
     for (int i = 0; i < 16; ++i) {
         const float freq = 1.0f / std::pow(100.0f, static_cast<float>(i) / 16.0f);
         for (int pos = 0; pos < maxpos; ++pos) {
@@ -916,6 +1052,23 @@ void Engine::load(const std::string& path) {
         }
     }
 
+    return M;
+}
+}  // namespace
+
+void check_checkpoint(const std::string& path, const Dims& d) { (void)read_model(path, d); }
+
+void Engine::load(const std::string& path) {
+    const HostModel M = read_model(path, d_);
+    const Dims& d = d_;
+    const int Dd = d.dec_dim;
+    const HostLin& patch = M.patch;
+    const std::vector<HostEnc>& enc = M.enc;
+    const std::vector<float>&eng = M.eng, &enb = M.enb, &dng = M.dng, &dnb = M.dnb;
+    const HostLin& dembed = M.dembed;
+    const std::vector<HostDec>* dec = M.dec;
+    const HostHead* hh = M.hh;
+    const std::vector<float>&rc = M.rope_cos, &rs = M.rope_sin;
     // upload to every device
     for (auto& dp : devs_) {
         Device& D = *dp;
@@ -1133,6 +1286,10 @@ std::string Engine::profile_ops() const {
         t += line;
     }
     return t;
+}
+
+void Engine::set_wait_timeout(unsigned long long ns) {
+    for (auto& d : devs_) d->set_wait_limit(ns);
 }
 
 void Engine::profile(double* out) const {

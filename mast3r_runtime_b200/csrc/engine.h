@@ -66,6 +66,7 @@ public:
     int match(const float* d1, const float* d2, int h, int w, int d, int top_k, int reciprocal, float thr,
               int64_t* idx1, int64_t* idx2, float* conf, float* p1, float* p2, float* timing);
     void set_profiling(bool on) { profiling_ = on; }
+    void set_wait_timeout(unsigned long long ns);  // bounded device waits of every device (0: default)
     void profile(double* out8) const;
     std::string profile_ops() const;  // "<op>\t<ms>\t<flop>\t<launches>\n" per operation
 
@@ -86,6 +87,10 @@ private:
     bool profiling_ = false;
     int staged_pairs_ = 0;
 };
+
+// Reads a checkpoint for the model `d` on the host and discards it: the checks of
+// Engine::load without a device (throws Error(kErrIo) / Error(kErrArg)).
+void check_checkpoint(const std::string& path, const Dims& d);
 
 // Per-device helpers used by the test entry points.
 struct DeviceGuard {

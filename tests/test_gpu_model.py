@@ -162,7 +162,9 @@ def test_profile_per_operation(tmp_path):
 def test_pipelined_infer_matches_resident(tmp_path):
     """infer_batch runs a device's pairs in sub-batches whose output copies overlap the
     next sub-batch's compute; the outputs equal one resident pass over all pairs, and
-    the staged inputs afterwards are the pairs of that call."""
+    the staged inputs afterwards are the pairs of that call.  Ordinary numpy arrays go
+    through the pinned staging slots (four sub-batches: both slots reused), page-locked
+    ones are copied directly."""
     from mast3r_runtime_b200 import NativeEngine, make_weights, save_safetensors
     from mast3r_runtime_b200.weights import tiny_dims
 
@@ -182,6 +184,17 @@ def test_pipelined_infer_matches_resident(tmp_path):
         for k in ref:
             np.testing.assert_array_equal(got[k], ref[k])
     assert timing["encoder_ms"] > 0 and timing["d2h_ms"] > 0
+    # page-locked caller buffers take the direct copies (no staging): same results
+    from mast3r_runtime_b200 import _lib
+
+    p1 = _lib.pinned_empty(img1.shape, np.uint8)
+    p2 = _lib.pinned_empty(img2.shape, np.uint8)
+    p1[...] = img1
+    p2[...] = img2
+    pinned_out = eng._out_arrays(n, alloc=_lib.pinned_empty)
+    got, _ = eng.infer_batch(p1, p2, out=pinned_out)
+    for k in ref:
+        np.testing.assert_array_equal(np.asarray(got[k]), ref[k])
     eng.run_resident(n)  # the slots still hold the call's pairs
     again = eng.fetch(n)
     for k in ref:

@@ -52,10 +52,16 @@ def test_match_nn_static_equals_match_nn_on_two_calls():
         o21 = torch.full((n2,), -1, dtype=torch.int32, device=dev)
         ob = torch.zeros(n1, dtype=torch.float32, device=dev)
         stream = torch.cuda.current_stream(dev).cuda_stream
+        torch.cuda.synchronize(dev)
+        free_before = torch.cuda.mem_get_info(dev)[0]
         rc = lib.m3r_match_nn_static(0, ta.data_ptr(), tb.data_ptr(), n1, n2, d, o12.data_ptr(), o21.data_ptr(),
                                      ob.data_ptr(), stream)
         _lib.check(rc)
         torch.cuda.synchronize(dev)
+        if seed > 1:
+            # past its first (set-up) call the entry point allocates no device memory:
+            # the device's free memory is unchanged (allocations come in >= 2 MiB pages)
+            assert torch.cuda.mem_get_info(dev)[0] == free_before
         np.testing.assert_array_equal(o12.cpu().numpy(), want12)
         np.testing.assert_array_equal(o21.cpu().numpy(), want21)
         assert ob.cpu().numpy().tobytes() == wantb.tobytes()
