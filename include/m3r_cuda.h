@@ -121,6 +121,20 @@ int m3r_match(m3r_engine* engine, const float* desc_1, const float* desc_2, int 
               int top_k, int reciprocal, float confidence_threshold, int64_t* idx_1, int64_t* idx_2,
               float* confidence, float* pts2d_1, float* pts2d_2, int* n_matches, float* timing_ms);
 
+/* ---- match(desc_1, desc_2, conf_1, conf_2, pts3d_1, pts3d_2): the full signature of the
+ * reference matcher, reciprocal_match(desc_1, desc_2, conf_1, conf_2, pts3d_1, pts3d_2, ...)
+ * (mast3r_runtime/backends/matching.py:53-63; csrc/cpu/matching.cpp:85-90).  As m3r_match,
+ * plus: conf_1 / conf_2 ([height*width], both or neither) weight every similarity by
+ * conf_1[i] * conf_2[j] before the arg-max, threshold and top-k (matching.cpp:110-119);
+ * match_pts3d_1 / _2 ([n, 3], both or neither) receive pts3d_1[idx_1] / pts3d_2[idx_2]
+ * ([height*width, 3] maps, matching.py:144-152), or zeros when the maps are NULL (the
+ * C++ path's result, matching.cpp:231-232). */
+int m3r_match_ex(m3r_engine* engine, const float* desc_1, const float* desc_2, const float* conf_1,
+                 const float* conf_2, const float* pts3d_1, const float* pts3d_2, int height, int width, int desc_dim,
+                 int top_k, int reciprocal, float confidence_threshold, int64_t* idx_1, int64_t* idx_2,
+                 float* confidence, float* pts2d_1, float* pts2d_2, float* match_pts3d_1, float* match_pts3d_2,
+                 int* n_matches, float* timing_ms);
+
 /* ---- device-resident stages of m3r_infer (throughput measurement and callers that
  * keep outputs on the device): copy inputs in, run, copy outputs out. */
 int m3r_stage_inputs(m3r_engine* engine, const uint8_t* img1, const uint8_t* img2, int n_pairs);

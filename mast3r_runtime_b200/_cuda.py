@@ -204,7 +204,11 @@ class NativeEngine:
             ops[name] = {"ms": float(ms), "flop": float(flop), "launches": int(launches)}
         return ops
 
-    def match(self, desc_1, desc_2, top_k=512, reciprocal=True, confidence_threshold=0.5):
+    def match(self, desc_1, desc_2, top_k=512, reciprocal=True, confidence_threshold=0.5, conf_1=None, conf_2=None,
+              pts3d_1=None, pts3d_2=None):
+        """reciprocal_match (backends/matching.py:53-165): conf_1 / conf_2 [H, W] weight every
+        similarity by conf_1[i] * conf_2[j] (both needed); pts3d_1 / pts3d_2 [H, W, 3] give the
+        3-D points of the matches (zeros without them)."""
         d1 = np.ascontiguousarray(desc_1, dtype=np.float32)
         d2 = np.ascontiguousarray(desc_2, dtype=np.float32)
         if d1.ndim != 3 or d2.ndim != 3:
@@ -212,6 +216,12 @@ class NativeEngine:
         if d1.shape != d2.shape:
             raise ValueError(f"descriptor maps differ in shape: {d1.shape} vs {d2.shape}")
         H, W, D = d1.shape
+        weighted = conf_1 is not None and conf_2 is not None
+        c1 = np.ascontiguousarray(conf_1, dtype=np.float32).reshape(H * W) if weighted else None
+        c2 = np.ascontiguousarray(conf_2, dtype=np.float32).reshape(H * W) if weighted else None
+        have3 = pts3d_1 is not None and pts3d_2 is not None
+        q1 = np.ascontiguousarray(pts3d_1, dtype=np.float32).reshape(H * W, 3) if have3 else None
+        q2 = np.ascontiguousarray(pts3d_2, dtype=np.float32).reshape(H * W, 3) if have3 else None
         n = H * W
         top_k = int(top_k)
         if top_k < 0:
@@ -222,19 +232,22 @@ class NativeEngine:
         conf = np.zeros(cap, np.float32)
         p1 = np.zeros((cap, 2), np.float32)
         p2 = np.zeros((cap, 2), np.float32)
+        o1 = np.zeros((cap, 3), np.float32)
+        o2 = np.zeros((cap, 3), np.float32)
         m = ctypes.c_int(0)
         t = np.zeros(len(_lib.TIMING_KEYS), np.float32)
         if n == 0 or D == 0:
             m.value = 0
         else:
-            rc = self.lib.m3r_match(self.h, _lib.ptr(d1), _lib.ptr(d2), H, W, D, top_k, int(bool(reciprocal)),
-                                    float(confidence_threshold), _lib.ptr(idx1), _lib.ptr(idx2), _lib.ptr(conf),
-                                    _lib.ptr(p1), _lib.ptr(p2), ctypes.byref(m), _lib.ptr(t))
+            rc = self.lib.m3r_match_ex(self.h, _lib.ptr(d1), _lib.ptr(d2), _lib.ptr(c1), _lib.ptr(c2), _lib.ptr(q1),
+                                       _lib.ptr(q2), H, W, D, top_k, int(bool(reciprocal)), float(confidence_threshold),
+                                       _lib.ptr(idx1), _lib.ptr(idx2), _lib.ptr(conf), _lib.ptr(p1), _lib.ptr(p2),
+                                       _lib.ptr(o1), _lib.ptr(o2), ctypes.byref(m), _lib.ptr(t))
             _lib.check(rc, self.h)
         k = m.value
         return SimpleNamespace(
             idx_1=idx1[:k].copy(), idx_2=idx2[:k].copy(), pts2d_1=p1[:k].copy(), pts2d_2=p2[:k].copy(),
-            pts3d_1=np.zeros((k, 3), np.float32), pts3d_2=np.zeros((k, 3), np.float32),
+            pts3d_1=o1[:k].copy(), pts3d_2=o2[:k].copy(),
             confidence=conf[:k].copy(),
             timing={"match_ms": float(t[7]), "kernel_ms": float(t[6]), "normalize_ms": float(t[0]),
                     "argmax_ms": float(t[1]), "select_ms": float(t[2])},
@@ -313,14 +326,19 @@ class CUDAEngine:
         eng = self._engine(tuple(img1.shape[1:3]), per_dev)
         return eng.infer_batch(img1, img2)
 
-    def match(self, desc_1, desc_2, top_k: int = 512, reciprocal: bool = True, confidence_threshold: float = 0.5):
+    def match(self, desc_1, desc_2, top_k: int = 512, reciprocal: bool = True, confidence_threshold: float = 0.5,
+              conf_1=None, conf_2=None, pts3d_1=None, pts3d_2=None):
+        """The wrapper's match (native_wrapper.py:99-140); also takes the reference matcher's
+        optional conf_* / pts3d_* maps (backends/matching.py:53-63), which the wrapper itself
+        does not pass on."""
         if self._matcher is None:
             # matching needs no weights: a minimal engine provides the device context
             self._matcher = next(iter(self._engines.values()), None) or NativeEngine(
                 self.dims, (self.dims.patch * 2, self.dims.patch * 2), self.devices[:1], 1, self.dtype)
         t0 = time.perf_counter()
         r = self._matcher.match(desc_1, desc_2, top_k=top_k, reciprocal=reciprocal,
-                                confidence_threshold=confidence_threshold)
+                                confidence_threshold=confidence_threshold, conf_1=conf_1, conf_2=conf_2,
+                                pts3d_1=pts3d_1, pts3d_2=pts3d_2)
         r.timing["match_ms"] = (time.perf_counter() - t0) * 1000.0
         return r
 

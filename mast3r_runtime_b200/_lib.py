@@ -74,6 +74,8 @@ SIGNATURES = {
     "m3r_is_ready": (_I, [_P]),
     "m3r_infer": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P]),
     "m3r_match": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, ctypes.POINTER(_I), _P]),
+    "m3r_match_ex": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _P,
+                          ctypes.POINTER(_I), _P]),
     "m3r_stage_inputs": (_I, [_P, _P, _P, _I]),
     "m3r_run_resident": (_I, [_P, _I, ctypes.POINTER(_F)]),
     "m3r_fetch_outputs": (_I, [_P, _I, _P, _P, _P, _P, _P, _P]),

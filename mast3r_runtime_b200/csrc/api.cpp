@@ -182,6 +182,33 @@ int m3r_match(m3r_engine* engine, const float* desc_1, const float* desc_2, int 
     });
 }
 
+int m3r_match_ex(m3r_engine* engine, const float* desc_1, const float* desc_2, const float* conf_1,
+                 const float* conf_2, const float* pts3d_1, const float* pts3d_2, int height, int width, int desc_dim,
+                 int top_k, int reciprocal, float confidence_threshold, int64_t* idx_1, int64_t* idx_2,
+                 float* confidence, float* pts2d_1, float* pts2d_2, float* match_pts3d_1, float* match_pts3d_2,
+                 int* n_matches, float* timing_ms) {
+    if (!engine) return M3R_ERR_ARG;
+    return guarded(engine, [&] {
+        M3R_REQUIRE(n_matches != nullptr, "n_matches is null");
+        *n_matches = 0;
+        const long long n = static_cast<long long>(height) * width;
+        M3R_REQUIRE(n == 0 || (desc_1 && desc_2 && idx_1 && idx_2 && confidence && pts2d_1 && pts2d_2),
+                    "match: null buffer");
+        M3R_REQUIRE((conf_1 == nullptr) == (conf_2 == nullptr), "match: give both confidence maps or neither");
+        M3R_REQUIRE((match_pts3d_1 == nullptr) == (match_pts3d_2 == nullptr), "match: give both pts3d outputs or neither");
+        m3r::MatchExtras ex;
+        ex.conf_1 = conf_1;
+        ex.conf_2 = conf_2;
+        ex.pts3d_1 = pts3d_1;
+        ex.pts3d_2 = pts3d_2;
+        ex.out3_1 = match_pts3d_1;
+        ex.out3_2 = match_pts3d_2;
+        *n_matches = engine->impl->match(desc_1, desc_2, height, width, desc_dim, top_k, reciprocal,
+                                         confidence_threshold, idx_1, idx_2, confidence, pts2d_1, pts2d_2, timing_ms,
+                                         &ex);
+    });
+}
+
 int m3r_stage_inputs(m3r_engine* engine, const uint8_t* img1, const uint8_t* img2, int n_pairs) {
     if (!engine) return M3R_ERR_ARG;
     return guarded(engine, [&] {

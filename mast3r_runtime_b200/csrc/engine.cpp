@@ -1327,7 +1327,9 @@ struct MatchEvents {
 }  // namespace
 
 int Engine::match(const float* d1, const float* d2, int hh, int ww, int dd, int top_k, int reciprocal, float thr,
-                  int64_t* idx1, int64_t* idx2, float* conf, float* p1, float* p2, float* timing) {
+                  int64_t* idx1, int64_t* idx2, float* conf, float* p1, float* p2, float* timing,
+                  const MatchExtras* ex) {
+    const bool weighted = ex && ex->conf_1 && ex->conf_2;
     const auto t0 = std::chrono::steady_clock::now();
     M3R_REQUIRE(hh >= 0 && ww >= 0 && dd > 0 && top_k >= 0, "match: bad arguments");
     const long long n = static_cast<long long>(hh) * ww;
@@ -1339,7 +1341,8 @@ int Engine::match(const float* d1, const float* d2, int hh, int ww, int dd, int 
     int m = 0;
     float phase_ms[4] = {0, 0, 0, 0};  // normalize, arg-max, select, all three (device time)
     if (devs_.size() > 1 && n >= static_cast<long long>(devs_.size()) * 128) {
-        m = match_multi(d1, d2, n, ww, dd, top_k, reciprocal, thr, idx1, idx2, conf, phase_ms);
+        m = match_multi(d1, d2, weighted ? ex->conf_1 : nullptr, weighted ? ex->conf_2 : nullptr, n, ww, dd, top_k,
+                        reciprocal, thr, idx1, idx2, conf, phase_ms);
     } else {
         // single device (device 0 of the engine)
         Device& D = *devs_[0];
@@ -1349,11 +1352,16 @@ int Engine::match(const float* d1, const float* d2, int hh, int ww, int dd, int 
         MatchEvents ev;
         M3R_CUDA(cudaMemcpyAsync(D.mws.a, d1, sizeof(float) * n * dd, cudaMemcpyHostToDevice, s));
         M3R_CUDA(cudaMemcpyAsync(D.mws.b, d2, sizeof(float) * n * dd, cudaMemcpyHostToDevice, s));
+        if (weighted) {
+            M3R_CUDA(cudaMemcpyAsync(D.mws.c1, ex->conf_1, sizeof(float) * n, cudaMemcpyHostToDevice, s));
+            M3R_CUDA(cudaMemcpyAsync(D.mws.c2, ex->conf_2, sizeof(float) * n, cudaMemcpyHostToDevice, s));
+        }
         M3R_CUDA(cudaEventRecord(ev.e[0], s));
         match_normalize(s, D.mws.a, D.mws.a, n, dd);
         match_normalize(s, D.mws.b, D.mws.b, n, dd);
         M3R_CUDA(cudaEventRecord(ev.e[1], s));
-        match_argmax(s, D.mws.a, D.mws.b, 0, n, n, dd, D.mws.rowkey, D.mws.colkey, true);
+        match_argmax(s, D.mws.a, D.mws.b, 0, n, n, dd, D.mws.rowkey, D.mws.colkey, true,
+                     weighted ? D.mws.c1 : nullptr, weighted ? D.mws.c2 : nullptr);
         M3R_CUDA(cudaEventRecord(ev.e[2], s));
         m = match_select(s, D.mws, n, 0, reciprocal, thr, top_k);
         M3R_CUDA(cudaEventRecord(ev.e[3], s));
@@ -1370,6 +1378,16 @@ int Engine::match(const float* d1, const float* d2, int hh, int ww, int dd, int 
         p1[2 * i + 1] = static_cast<float>(idx1[i] / ww);
         p2[2 * i] = static_cast<float>(idx2[i] % ww);
         p2[2 * i + 1] = static_cast<float>(idx2[i] / ww);
+    }
+    // 3-D points of the matches (matching.py:144-152; zeros without pts3d maps, as the
+    // C++ path returns, matching.cpp:231-232)
+    if (ex && ex->out3_1 && ex->out3_2) {
+        const bool have = ex->pts3d_1 && ex->pts3d_2;
+        for (int i = 0; i < m; ++i)
+            for (int q = 0; q < 3; ++q) {
+                ex->out3_1[3 * i + q] = have ? ex->pts3d_1[3 * idx1[i] + q] : 0.0f;
+                ex->out3_2[3 * i + q] = have ? ex->pts3d_2[3 * idx2[i] + q] : 0.0f;
+            }
     }
     if (timing) {
         for (int i = 0; i < M3R_T_COUNT; ++i) timing[i] = 0.0f;
@@ -1389,8 +1407,9 @@ int Engine::match(const float* d1, const float* d2, int hh, int ww, int dd, int 
 // every device then holds the exact nn_21 and runs the reciprocal test, threshold and
 // top-k on its own rows.  The per-device results (each <= top_k, exact top-k of its
 // rows) are merged on the host: the global top-k is inside their union.
-int Engine::match_multi(const float* d1, const float* d2, long long n, int ww, int dd, int top_k, int reciprocal,
-                        float thr, int64_t* idx1, int64_t* idx2, float* conf, float* phase_ms) {
+int Engine::match_multi(const float* d1, const float* d2, const float* c1, const float* c2, long long n, int ww, int dd,
+                        int top_k, int reciprocal, float thr, int64_t* idx1, int64_t* idx2, float* conf,
+                        float* phase_ms) {
     const int nd = static_cast<int>(devs_.size());
     const NcclApi& api = nccl();
     if (nccl_comms_.empty()) {
@@ -1423,12 +1442,17 @@ int Engine::match_multi(const float* d1, const float* d2, long long n, int ww, i
         P.ev.reset(new MatchEvents());
         M3R_CUDA(cudaMemcpyAsync(D.mws.a, d1 + P.r0 * dd, sizeof(float) * nr * dd, cudaMemcpyHostToDevice, s));
         M3R_CUDA(cudaMemcpyAsync(D.mws.b, d2, sizeof(float) * n * dd, cudaMemcpyHostToDevice, s));
+        if (c1 && c2) {  // whole maps: conf_1 is addressed by global row
+            M3R_CUDA(cudaMemcpyAsync(D.mws.c1, c1, sizeof(float) * n, cudaMemcpyHostToDevice, s));
+            M3R_CUDA(cudaMemcpyAsync(D.mws.c2, c2, sizeof(float) * n, cudaMemcpyHostToDevice, s));
+        }
         M3R_CUDA(cudaEventRecord(P.ev->e[0], s));
         match_normalize(s, D.mws.a, D.mws.a, nr, dd);
         match_normalize(s, D.mws.b, D.mws.b, n, dd);
         M3R_CUDA(cudaEventRecord(P.ev->e[1], s));
         // A is addressed by global row: rows [r0, r1) live at mws.a[0 .. nr)
-        match_argmax(s, D.mws.a - P.r0 * dd, D.mws.b, P.r0, P.r1, n, dd, D.mws.rowkey, D.mws.colkey, true);
+        match_argmax(s, D.mws.a - P.r0 * dd, D.mws.b, P.r0, P.r1, n, dd, D.mws.rowkey, D.mws.colkey, true,
+                     c1 && c2 ? D.mws.c1 : nullptr, c1 && c2 ? D.mws.c2 : nullptr);
         M3R_CUDA(cudaEventRecord(P.ev->e[2], s));
     });
     // phase 2: column keys max-reduced over the devices

@@ -53,6 +53,18 @@ struct Head {
 
 class Device;
 
+// Optional inputs / outputs of a match: confidence maps that weight every similarity
+// (conf_1[i] * conf_2[j], csrc/cpu/matching.cpp:110-119), and 3-D point maps whose
+// entries at the matched pixels are returned (matching.py:144-152).  Any may be null.
+struct MatchExtras {
+    const float* conf_1 = nullptr;   // [n]
+    const float* conf_2 = nullptr;   // [n]
+    const float* pts3d_1 = nullptr;  // [n, 3]
+    const float* pts3d_2 = nullptr;  // [n, 3]
+    float* out3_1 = nullptr;         // [<= top_k, 3]
+    float* out3_2 = nullptr;
+};
+
 class Engine {
 public:
     explicit Engine(const m3r_config& cfg);
@@ -64,7 +76,8 @@ public:
     float run_resident(int n_pairs, float* stage_ms);
     void fetch(int n_pairs, float* const outs[6]);
     int match(const float* d1, const float* d2, int h, int w, int d, int top_k, int reciprocal, float thr,
-              int64_t* idx1, int64_t* idx2, float* conf, float* p1, float* p2, float* timing);
+              int64_t* idx1, int64_t* idx2, float* conf, float* p1, float* p2, float* timing,
+              const MatchExtras* ex = nullptr);
     void set_profiling(bool on) { profiling_ = on; }
     void set_wait_timeout(unsigned long long ns);  // bounded device waits of every device (0: default)
     void profile(double* out8) const;
@@ -77,8 +90,8 @@ public:
 private:
     std::vector<std::pair<int, int>> shards(int n_pairs) const;  // (first pair, count) per device
     // rows of desc_1 sharded over the devices; column keys max-reduced with NCCL
-    int match_multi(const float* d1, const float* d2, long long n, int ww, int dd, int top_k, int reciprocal,
-                    float thr, int64_t* idx1, int64_t* idx2, float* conf, float* phase_ms);
+    int match_multi(const float* d1, const float* d2, const float* c1, const float* c2, long long n, int ww, int dd,
+                    int top_k, int reciprocal, float thr, int64_t* idx1, int64_t* idx2, float* conf, float* phase_ms);
     m3r_config cfg_;
     Dims d_;
     std::vector<std::unique_ptr<Device>> devs_;

@@ -12,7 +12,8 @@
 // Pipeline (one device, rows [row0, row1) of set A against all of set B):
 //   normalize      one thread per row
 //   argmax         128 x 128 tiles, 8 x 8 per thread; row and column maxima of
-//                  every similarity, fused -- the N x N matrix never exists.
+//                  every similarity (times conf_1[i] * conf_2[j] when confidence
+//                  maps are given), fused -- the N x N matrix never exists.
 //                  Partial maxima are merged with 64-bit atomicMax on keys
 //                  (orderable(value) << 32) | (0xFFFFFFFF - index): the maximum
 //                  key is the maximum value with the lowest index, which is the
@@ -110,8 +111,9 @@ constexpr int kPitch = 128 + 4;
 // tr in [4*(w/2), +4), tc in [8*(w%2), +8): lane = tr_l * 8 + tc_l.
 template <int DFIX>
 __global__ void __launch_bounds__(256, 2)
-    argmax_kernel(const float* __restrict__ A, const float* __restrict__ B, long long row0, long long row1, long long n2,
-                  int dyn_d, int n_seg, unsigned long long* __restrict__ rowkey, unsigned long long* __restrict__ colkey) {
+    argmax_kernel(const float* __restrict__ A, const float* __restrict__ B, const float* __restrict__ C1,
+                  const float* __restrict__ C2, long long row0, long long row1, long long n2, int dyn_d, int n_seg,
+                  unsigned long long* __restrict__ rowkey, unsigned long long* __restrict__ colkey) {
     const int D = DFIX > 0 ? DFIX : dyn_d;
     __shared__ __align__(16) float sA[kKC][kPitch];
     __shared__ __align__(16) float sB[kKC][kPitch];
@@ -139,6 +141,15 @@ __global__ void __launch_bounds__(256, 2)
     }
 
     const bool a_resident = D <= kKC;
+    // confidence weighting (matching.cpp:110-119): sim * (conf_1[i] * conf_2[j]); the
+    // row confidences of this thread's 8 rows stay in registers
+    const bool weighted = C1 != nullptr && C2 != nullptr;
+    float cr[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+        const long long gi = i0 + tr * 8 + r;
+        cr[r] = (weighted && gi < row1) ? C1[gi] : 1.0f;
+    }
     for (long long jt = jt_begin; jt < jt_end; ++jt) {
         const long long j0 = jt * kTJ;
         // s[r][c]: similarity of row tr*8 + r and column (c < 4 ? tc*4 + c : 64 + tc*4 + c - 4)
@@ -180,6 +191,16 @@ __global__ void __launch_bounds__(256, 2)
                 for (int r = 0; r < 8; ++r)
 #pragma unroll
                     for (int c = 0; c < 8; ++c) s[r][c] = __fadd_rn(s[r][c], __fmul_rn(av[r], bv[c]));
+            }
+        }
+
+        if (weighted) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const long long j = j0 + (c < 4 ? tc * 4 + c : 64 + tc * 4 + c - 4);
+                const float cc = j < n2 ? C2[j] : 1.0f;
+#pragma unroll
+                for (int r = 0; r < 8; ++r) s[r][c] = __fmul_rn(s[r][c], __fmul_rn(cr[r], cc));
             }
         }
 
@@ -539,7 +560,8 @@ void MatchWorkspace::release() {
                      reinterpret_cast<void**>(&hist), reinterpret_cast<void**>(&state),
                      reinterpret_cast<void**>(&skey), reinterpret_cast<void**>(&sj), reinterpret_cast<void**>(&misc),
                      reinterpret_cast<void**>(&idx1), reinterpret_cast<void**>(&idx2),
-                     reinterpret_cast<void**>(&conf)}) {
+                     reinterpret_cast<void**>(&conf), reinterpret_cast<void**>(&c1),
+                     reinterpret_cast<void**>(&c2)}) {
         if (*p) cudaFree(*p);
         *p = nullptr;
     }
@@ -570,6 +592,8 @@ void MatchWorkspace::reserve(long long n, int d) {
     M3R_CUDA(cudaMalloc(&idx1, sizeof(long long) * nn));
     M3R_CUDA(cudaMalloc(&idx2, sizeof(long long) * nn));
     M3R_CUDA(cudaMalloc(&conf, sizeof(float) * nn));
+    M3R_CUDA(cudaMalloc(&c1, sizeof(float) * nn));
+    M3R_CUDA(cudaMalloc(&c2, sizeof(float) * nn));
     M3R_CUDA(cudaMemset(hist, 0, sizeof(unsigned) * 65536));
     cap_n = n;
     cap_d = d;
@@ -587,7 +611,8 @@ void match_normalize(cudaStream_t s, const float* in, float* out, long long n, i
 }
 
 void match_argmax(cudaStream_t s, const float* a_norm, const float* b_norm, long long row0, long long row1,
-                  long long n2, int d, unsigned long long* rowkey, unsigned long long* colkey, bool clear_colkey) {
+                  long long n2, int d, unsigned long long* rowkey, unsigned long long* colkey, bool clear_colkey,
+                  const float* conf_1, const float* conf_2) {
     const long long nrows = row1 - row0;
     if (nrows > 0) M3R_CUDA(cudaMemsetAsync(rowkey, 0, sizeof(unsigned long long) * nrows, s));
     if (clear_colkey && n2 > 0) M3R_CUDA(cudaMemsetAsync(colkey, 0, sizeof(unsigned long long) * n2, s));
@@ -602,10 +627,11 @@ void match_argmax(cudaStream_t s, const float* a_norm, const float* b_norm, long
     M3R_REQUIRE(row_blocks <= 0x7FFFFFFFLL, "match: too many rows");
     dim3 grid(static_cast<unsigned>(row_blocks), static_cast<unsigned>(seg));
     if (d == 24)
-        argmax_kernel<24><<<grid, 256, 0, s>>>(a_norm, b_norm, row0, row1, n2, d, static_cast<int>(seg), rowkey,
-                                               colkey);
+        argmax_kernel<24><<<grid, 256, 0, s>>>(a_norm, b_norm, conf_1, conf_2, row0, row1, n2, d,
+                                               static_cast<int>(seg), rowkey, colkey);
     else
-        argmax_kernel<0><<<grid, 256, 0, s>>>(a_norm, b_norm, row0, row1, n2, d, static_cast<int>(seg), rowkey, colkey);
+        argmax_kernel<0><<<grid, 256, 0, s>>>(a_norm, b_norm, conf_1, conf_2, row0, row1, n2, d, static_cast<int>(seg),
+                                              rowkey, colkey);
     M3R_CUDA(cudaGetLastError());
 }
 

@@ -23,6 +23,8 @@ struct MatchWorkspace {
     long long* idx1 = nullptr;
     long long* idx2 = nullptr;
     float* conf = nullptr;
+    float* c1 = nullptr;              // confidence maps (weighted matching)
+    float* c2 = nullptr;
     long long cap_n = 0;
     int cap_d = 0;
 
@@ -35,9 +37,12 @@ struct MatchWorkspace {
 void match_normalize(cudaStream_t s, const float* in, float* out, long long n, int d);
 
 // Row keys of rows [row0, row1) of A (rowkey[i - row0]) and column keys of all n2
-// columns of B (colkey[j], merged with atomicMax; cleared first when asked).
+// columns of B (colkey[j], merged with atomicMax; cleared first when asked).  With
+// conf_1 (indexed by global row) and conf_2 (by column) both given, every similarity
+// is weighted by conf_1[i] * conf_2[j] (csrc/cpu/matching.cpp:110-119).
 void match_argmax(cudaStream_t s, const float* a_norm, const float* b_norm, long long row0, long long row1,
-                  long long n2, int d, unsigned long long* rowkey, unsigned long long* colkey, bool clear_colkey);
+                  long long n2, int d, unsigned long long* rowkey, unsigned long long* colkey, bool clear_colkey,
+                  const float* conf_1 = nullptr, const float* conf_2 = nullptr);
 
 // Reciprocal / threshold / top-k over rows [row0, row0 + nrows) with keys in ws;
 // results in ws.idx1 / ws.idx2 / ws.conf.  Returns the match count (<= top_k);

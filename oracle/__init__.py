@@ -54,6 +54,15 @@ def lib() -> ctypes.CDLL:
                                    ctypes.c_int, ctypes.c_int, ctypes.c_float,
                                    _i64p, _i64p, _f32p, _f32p, _f32p, ctypes.c_void_p, ctypes.c_void_p]
         L.oracle_match.restype = ctypes.c_int64
+        _opt = ctypes.c_void_p  # optional float arrays (None = absent)
+        L.oracle_match_w.argtypes = [_f32p, _f32p, _opt, _opt, _opt, _opt, ctypes.c_int64, ctypes.c_int,
+                                     ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                     _i64p, _i64p, _f32p, _f32p, _f32p, _opt, _opt, ctypes.c_void_p,
+                                     ctypes.c_void_p]
+        L.oracle_match_w.restype = ctypes.c_int64
+        L.oracle_argmax_w.argtypes = [_f32p, _f32p, _opt, _opt, ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
+                                      ctypes.c_int64, ctypes.c_int64, _i32p, _f32p, _i32p, _f32p]
+        L.oracle_argmax_w.restype = None
         L.oracle_attention.argtypes = [_f32p, _f32p, _f32p, _f32p, ctypes.c_int64, ctypes.c_int,
                                        ctypes.c_int, ctypes.c_int, ctypes.c_float]
         L.oracle_attention.restype = None
@@ -73,6 +82,10 @@ def ref_lib() -> ctypes.CDLL | None:
                                            ctypes.c_int, ctypes.c_int, ctypes.c_float,
                                            _i64p, _i64p, _f32p, _f32p, _f32p]
         L.ref_reciprocal_match.restype = ctypes.c_int64
+        L.ref_reciprocal_match_conf.argtypes = [_f32p, _f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_int,
+                                                ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                                _i64p, _i64p, _f32p, _f32p, _f32p]
+        L.ref_reciprocal_match_conf.restype = ctypes.c_int64
         L.ref_normalize.argtypes = [_f32p, ctypes.c_int, ctypes.c_int]
         L.ref_normalize.restype = None
         L.ref_multi_head_attention.argtypes = [_f32p, _f32p, _f32p, _f32p, ctypes.c_int,
@@ -90,7 +103,8 @@ def normalize(desc: np.ndarray) -> np.ndarray:
     return out.reshape(desc.shape)
 
 
-def argmax(a_norm: np.ndarray, b_norm: np.ndarray, row0: int = 0, row1: int | None = None):
+def argmax(a_norm: np.ndarray, b_norm: np.ndarray, row0: int = 0, row1: int | None = None, conf_1=None,
+           conf_2=None):
     """Row/column arg-max of a_norm . b_norm^T (already normalised), lowest index on ties.
 
     Returns (nn12, best12, nn21, best21); nn12/best12 are only filled in [row0, row1).
@@ -104,16 +118,30 @@ def argmax(a_norm: np.ndarray, b_norm: np.ndarray, row0: int = 0, row1: int | No
     b12 = np.zeros(n1, np.float32)
     nn21 = np.zeros(n2, np.int32)
     b21 = np.zeros(n2, np.float32)
-    lib().oracle_argmax(a, b, n1, n2, d, row0, row1, nn12, b12, nn21, b21)
+    c1 = None if conf_1 is None else np.ascontiguousarray(conf_1, np.float32).reshape(n1)
+    c2 = None if conf_2 is None else np.ascontiguousarray(conf_2, np.float32).reshape(n2)
+    lib().oracle_argmax_w(a, b, None if c1 is None else c1.ctypes.data_as(ctypes.c_void_p),
+                          None if c2 is None else c2.ctypes.data_as(ctypes.c_void_p), n1, n2, d, row0, row1,
+                          nn12, b12, nn21, b21)
     return nn12, b12, nn21, b21
 
 
-def match(desc_1: np.ndarray, desc_2: np.ndarray, top_k: int = 512, reciprocal: bool = True,
-          confidence_threshold: float = 0.5, with_nn: bool = False):
-    """Restated reciprocal_match on [H, W, D] maps (csrc/cpu/matching.cpp:85-237).
+def _opt32(x, n):
+    if x is None:
+        return None, None
+    a = np.ascontiguousarray(x, dtype=np.float32).reshape(n, -1)
+    return a, a.ctypes.data_as(ctypes.c_void_p)
 
-    Returns a dict with idx_1, idx_2 (int64), confidence, pts2d_1, pts2d_2 (float32)
-    and, when ``with_nn``, nn_12 / nn_21 (int32).
+
+def match(desc_1: np.ndarray, desc_2: np.ndarray, top_k: int = 512, reciprocal: bool = True,
+          confidence_threshold: float = 0.5, with_nn: bool = False, conf_1=None, conf_2=None,
+          pts3d_1=None, pts3d_2=None):
+    """Restated reciprocal_match on [H, W, D] maps (csrc/cpu/matching.cpp:85-237), with the
+    confidence weighting of :110-119 when conf_1 and conf_2 ([H, W]) are given and the
+    pts3d gather of matching.py:144-152 when pts3d_1 and pts3d_2 ([H, W, 3]) are.
+
+    Returns a dict with idx_1, idx_2 (int64), confidence, pts2d_1, pts2d_2, pts3d_1,
+    pts3d_2 (float32) and, when ``with_nn``, nn_12 / nn_21 (int32).
     """
     h, w, d = desc_1.shape
     n = h * w
@@ -127,15 +155,24 @@ def match(desc_1: np.ndarray, desc_2: np.ndarray, top_k: int = 512, reciprocal: 
     p2 = np.zeros(cap * 2, np.float32)
     nn12 = np.zeros(max(n, 1), np.int32)
     nn21 = np.zeros(max(n, 1), np.int32)
-    m = lib().oracle_match(a, b, n, d, w, top_k, int(bool(reciprocal)), float(confidence_threshold),
-                           idx1, idx2, conf, p1, p2,
-                           nn12.ctypes.data if with_nn else None,
-                           nn21.ctypes.data if with_nn else None)
+    weighted = conf_1 is not None and conf_2 is not None
+    c1, c1p = _opt32(conf_1 if weighted else None, n)
+    c2, c2p = _opt32(conf_2 if weighted else None, n)
+    q1, q1p = _opt32(pts3d_1 if pts3d_2 is not None else None, n)
+    q2, q2p = _opt32(pts3d_2 if pts3d_1 is not None else None, n)
+    o1 = np.zeros(cap * 3, np.float32)
+    o2 = np.zeros(cap * 3, np.float32)
+    m = lib().oracle_match_w(a, b, c1p, c2p, q1p, q2p, n, d, w, top_k, int(bool(reciprocal)),
+                             float(confidence_threshold), idx1, idx2, conf, p1, p2,
+                             o1.ctypes.data_as(ctypes.c_void_p), o2.ctypes.data_as(ctypes.c_void_p),
+                             nn12.ctypes.data if with_nn else None,
+                             nn21.ctypes.data if with_nn else None)
     if m < 0:
         raise ValueError("oracle_match: bad arguments")
     out = {
         "idx_1": idx1[:m].copy(), "idx_2": idx2[:m].copy(), "confidence": conf[:m].copy(),
         "pts2d_1": p1[: 2 * m].reshape(m, 2).copy(), "pts2d_2": p2[: 2 * m].reshape(m, 2).copy(),
+        "pts3d_1": o1[: 3 * m].reshape(m, 3).copy(), "pts3d_2": o2[: 3 * m].reshape(m, 3).copy(),
     }
     if with_nn:
         out["nn_12"] = nn12[:n].copy()
@@ -144,7 +181,7 @@ def match(desc_1: np.ndarray, desc_2: np.ndarray, top_k: int = 512, reciprocal: 
 
 
 def ref_match(desc_1: np.ndarray, desc_2: np.ndarray, top_k: int = 512, reciprocal: bool = True,
-              confidence_threshold: float = 0.5):
+              confidence_threshold: float = 0.5, conf_1=None, conf_2=None):
     """The reference's own reciprocal_match (oracle/_ref), or None when unavailable.
 
     It materialises the N x N similarity matrix: keep N small.
@@ -162,8 +199,14 @@ def ref_match(desc_1: np.ndarray, desc_2: np.ndarray, top_k: int = 512, reciproc
     conf = np.zeros(cap, np.float32)
     p1 = np.zeros(cap * 2, np.float32)
     p2 = np.zeros(cap * 2, np.float32)
-    m = L.ref_reciprocal_match(a, b, h, w, d, top_k, int(bool(reciprocal)),
-                               float(confidence_threshold), idx1, idx2, conf, p1, p2)
+    if conf_1 is not None and conf_2 is not None:
+        c1 = np.ascontiguousarray(conf_1, np.float32).reshape(n)
+        c2 = np.ascontiguousarray(conf_2, np.float32).reshape(n)
+        m = L.ref_reciprocal_match_conf(a, b, c1, c2, h, w, d, top_k, int(bool(reciprocal)),
+                                        float(confidence_threshold), idx1, idx2, conf, p1, p2)
+    else:
+        m = L.ref_reciprocal_match(a, b, h, w, d, top_k, int(bool(reciprocal)),
+                                   float(confidence_threshold), idx1, idx2, conf, p1, p2)
     return {
         "idx_1": idx1[:m].copy(), "idx_2": idx2[:m].copy(), "confidence": conf[:m].copy(),
         "pts2d_1": p1[: 2 * m].reshape(m, 2).copy(), "pts2d_2": p2[: 2 * m].reshape(m, 2).copy(),

@@ -18,6 +18,11 @@
  *   top-k       matching.cpp:189-213 conf descending; ties (unspecified in the
  *                                    reference's partial_sort) by idx_1 ascending
  *   pts2d       matching.cpp:216-222 (idx % W, idx / W) as float
+ *   confidence  matching.cpp:110-119 (when conf_1 and conf_2 are given) every
+ *   weighting   similarity becomes sim * (conf_1[i] * conf_2[j]), the product
+ *               of the two confidences rounded first
+ *   pts3d       matching.py:144-152 (the numpy path; the C++ path leaves zeros):
+ *               pts3d_1[idx_1], pts3d_2[idx_2] when pts3d maps are given
  * Unlike the reference this never materialises the N1 x N2 similarity matrix
  * (154.6 GB at N = 196,608): rows are processed in blocks and the column
  * maxima are merged across threads in row order, which gives the same
@@ -59,9 +64,9 @@ void oracle_normalize(float* desc, int64_t n, int d) {
  * nn21[j] = lowest i with the maximum of column j, best21[j] that maximum.
  * Rows [row0, row1) only (for sharded baselines); columns always all of B.
  */
-void oracle_argmax(const float* a, const float* b, int64_t n1, int64_t n2, int d,
-                   int64_t row0, int64_t row1,
-                   int32_t* nn12, float* best12, int32_t* nn21, float* best21) {
+void oracle_argmax_w(const float* a, const float* b, const float* c1, const float* c2, int64_t n1, int64_t n2,
+                     int d, int64_t row0, int64_t row1,
+                     int32_t* nn12, float* best12, int32_t* nn21, float* best21) {
     int nt = 1;
 #ifdef _OPENMP
     nt = omp_get_max_threads();
@@ -103,6 +108,13 @@ void oracle_argmax(const float* a, const float* b, int64_t n1, int64_t n2, int d
                     for (int jj = 0; jj < jn; ++jj) {
                         float p = ak * br[jj];
                         dot[jj] = dot[jj] + p;
+                    }
+                }
+                if (c1 && c2) {
+                    const float ci = c1[i];
+                    for (int jj = 0; jj < jn; ++jj) {
+                        const float w = ci * c2[j0 + jj];
+                        dot[jj] = dot[jj] * w;
                     }
                 }
                 float best = best12[i];
@@ -147,6 +159,12 @@ void oracle_argmax(const float* a, const float* b, int64_t n1, int64_t n2, int d
     free(touched);
 }
 
+void oracle_argmax(const float* a, const float* b, int64_t n1, int64_t n2, int d,
+                   int64_t row0, int64_t row1,
+                   int32_t* nn12, float* best12, int32_t* nn21, float* best21) {
+    oracle_argmax_w(a, b, NULL, NULL, n1, n2, d, row0, row1, nn12, best12, nn21, best21);
+}
+
 typedef struct { float c; int64_t i; int64_t j; } cand_t;
 
 static int cand_cmp(const void* x, const void* y) {
@@ -162,10 +180,11 @@ static int cand_cmp(const void* x, const void* y) {
  * d2 [n, d] of an H x W map (n = H * W).  Outputs are sized top_k (or n when
  * top_k >= n).  Returns the number of matches written, or -1 on bad input.
  */
-int64_t oracle_match(const float* d1, const float* d2, int64_t n, int d, int width,
-                     int top_k, int reciprocal, float thr,
-                     int64_t* idx1, int64_t* idx2, float* conf, float* pts2d_1, float* pts2d_2,
-                     int32_t* nn12_out, int32_t* nn21_out) {
+int64_t oracle_match_w(const float* d1, const float* d2, const float* c1, const float* c2,
+                       const float* p3_1, const float* p3_2, int64_t n, int d, int width,
+                       int top_k, int reciprocal, float thr,
+                       int64_t* idx1, int64_t* idx2, float* conf, float* pts2d_1, float* pts2d_2,
+                       float* pts3d_1, float* pts3d_2, int32_t* nn12_out, int32_t* nn21_out) {
     if (n < 0 || d <= 0 || top_k < 0 || (n > 0 && width <= 0)) return -1;
     if (n == 0) return 0;
     float* a = (float*)malloc(sizeof(float) * (size_t)n * d);
@@ -178,7 +197,7 @@ int64_t oracle_match(const float* d1, const float* d2, int64_t n, int d, int wid
     int32_t* nn21 = (int32_t*)malloc(sizeof(int32_t) * (size_t)n);
     float* b12 = (float*)malloc(sizeof(float) * (size_t)n);
     float* b21 = (float*)malloc(sizeof(float) * (size_t)n);
-    oracle_argmax(a, b, n, n, d, 0, n, nn12, b12, nn21, b21);
+    oracle_argmax_w(a, b, c1, c2, n, n, d, 0, n, nn12, b12, nn21, b21);
     cand_t* cand = (cand_t*)malloc(sizeof(cand_t) * (size_t)n);
     int64_t m = 0;
     for (int64_t i = 0; i < n; ++i) {
@@ -199,11 +218,23 @@ int64_t oracle_match(const float* d1, const float* d2, int64_t n, int d, int wid
         pts2d_1[2 * k + 1] = (float)(cand[k].i / width);
         pts2d_2[2 * k + 0] = (float)(cand[k].j % width);
         pts2d_2[2 * k + 1] = (float)(cand[k].j / width);
+        for (int q = 0; q < 3; ++q) {
+            if (pts3d_1) pts3d_1[3 * k + q] = p3_1 ? p3_1[3 * cand[k].i + q] : 0.0f;
+            if (pts3d_2) pts3d_2[3 * k + q] = p3_2 ? p3_2[3 * cand[k].j + q] : 0.0f;
+        }
     }
     if (nn12_out) memcpy(nn12_out, nn12, sizeof(int32_t) * (size_t)n);
     if (nn21_out) memcpy(nn21_out, nn21, sizeof(int32_t) * (size_t)n);
     free(a); free(b); free(nn12); free(nn21); free(b12); free(b21); free(cand);
     return m;
+}
+
+int64_t oracle_match(const float* d1, const float* d2, int64_t n, int d, int width,
+                     int top_k, int reciprocal, float thr,
+                     int64_t* idx1, int64_t* idx2, float* conf, float* pts2d_1, float* pts2d_2,
+                     int32_t* nn12_out, int32_t* nn21_out) {
+    return oracle_match_w(d1, d2, NULL, NULL, NULL, NULL, n, d, width, top_k, reciprocal, thr, idx1, idx2, conf,
+                          pts2d_1, pts2d_2, NULL, NULL, nn12_out, nn21_out);
 }
 
 /*

@@ -5,7 +5,8 @@
 //
 // The reference declares these functions in no header, so their signatures
 // are restated here exactly as they are defined:
-//   csrc/cpu/matching.cpp:85-90   mast3r::cpu::reciprocal_match
+//   csrc/cpu/matching.cpp:85-90   mast3r::cpu::reciprocal_match (with and without
+//                                 the confidence maps, :110-119)
 //   csrc/cpu/matching.cpp:22      mast3r::cpu::normalize_descriptors
 //   csrc/cpu/attention.cpp:118    mast3r::cpu::multi_head_attention
 #include <cstdint>
@@ -38,6 +39,26 @@ int64_t ref_reciprocal_match(const float* d1, const float* d2, int height, int w
     cfg.confidence_threshold = thr;
     mast3r::MatchResult r =
         mast3r::cpu::reciprocal_match(d1, d2, nullptr, nullptr, height, width, d, cfg);
+    const int64_t n = static_cast<int64_t>(r.num_matches());
+    if (n > 0) {
+        std::memcpy(idx1, r.idx_1.data(), sizeof(int64_t) * n);
+        std::memcpy(idx2, r.idx_2.data(), sizeof(int64_t) * n);
+        std::memcpy(conf, r.confidence.data(), sizeof(float) * n);
+        std::memcpy(pts2d_1, r.pts2d_1.data(), sizeof(float) * 2 * n);
+        std::memcpy(pts2d_2, r.pts2d_2.data(), sizeof(float) * 2 * n);
+    }
+    return n;
+}
+
+// The same with confidence weighting (conf_1, conf_2 [height*width]).
+int64_t ref_reciprocal_match_conf(const float* d1, const float* d2, const float* c1, const float* c2, int height,
+                                  int width, int d, int top_k, int reciprocal, float thr, int64_t* idx1,
+                                  int64_t* idx2, float* conf, float* pts2d_1, float* pts2d_2) {
+    mast3r::MatchingConfig cfg;
+    cfg.top_k = top_k;
+    cfg.reciprocal = reciprocal != 0;
+    cfg.confidence_threshold = thr;
+    mast3r::MatchResult r = mast3r::cpu::reciprocal_match(d1, d2, c1, c2, height, width, d, cfg);
     const int64_t n = static_cast<int64_t>(r.num_matches());
     if (n > 0) {
         std::memcpy(idx1, r.idx_1.data(), sizeof(int64_t) * n);

@@ -155,7 +155,8 @@ class FakeNative:
              "conf_1": np.ones((n, H, W), np.float32), "conf_2": np.ones((n, H, W), np.float32)}
         return o, {"inference_ms": 1.0, "total_ms": 2.0}
 
-    def match(self, d1, d2, top_k=512, reciprocal=True, confidence_threshold=0.5):
+    def match(self, d1, d2, top_k=512, reciprocal=True, confidence_threshold=0.5, conf_1=None, conf_2=None,
+              pts3d_1=None, pts3d_2=None):
         k = 3
         return SimpleNamespace(idx_1=np.arange(k, dtype=np.int64), idx_2=np.arange(k, dtype=np.int64),
                                pts2d_1=np.zeros((k, 2), np.float32), pts2d_2=np.zeros((k, 2), np.float32),

@@ -216,6 +216,34 @@ def test_match_bit_exact_vs_oracle(matcher_engine, oracle_lib, h, w, d, top_k, r
     np.testing.assert_array_equal(r.pts2d_2, o["pts2d_2"])
 
 
+@pytest.mark.parametrize("h,w,d,top_k,recip,thr", [
+    (48, 64, 24, 512, True, 1.5),      # top-k cut of the weighted similarities
+    (40, 64, 24, 4096, True, 0.0),     # all candidates
+    (32, 32, 24, 200, False, 1.0),
+])
+def test_match_confidence_weighted_bit_exact_vs_oracle(matcher_engine, oracle_lib, h, w, d, top_k, recip, thr):
+    """conf_1[i] * conf_2[j] weighting (matching.cpp:110-119) and the pts3d gather
+    (matching.py:144-152), bit for bit."""
+    a, b = matcher_inputs(h, w, d, h + w + 1)
+    rng = np.random.default_rng(h * w)
+    c1 = (1.0 + 2.0 * rng.random((h, w))).astype(np.float32)
+    c2 = (1.0 + 2.0 * rng.random((h, w))).astype(np.float32)
+    q1 = rng.standard_normal((h, w, 3)).astype(np.float32)
+    q2 = rng.standard_normal((h, w, 3)).astype(np.float32)
+    kw = dict(top_k=top_k, reciprocal=recip, confidence_threshold=thr, conf_1=c1, conf_2=c2, pts3d_1=q1, pts3d_2=q2)
+    r = matcher_engine.match(a, b, **kw)
+    o = oracle_lib.match(a, b, **kw)
+    assert len(o["idx_1"]) > 0
+    np.testing.assert_array_equal(r.idx_1, o["idx_1"])
+    np.testing.assert_array_equal(r.idx_2, o["idx_2"])
+    assert r.confidence.tobytes() == o["confidence"].tobytes()
+    np.testing.assert_array_equal(r.pts3d_1, o["pts3d_1"])
+    np.testing.assert_array_equal(r.pts3d_2, o["pts3d_2"])
+    # weighting changes the result (the test is not vacuous)
+    u = matcher_engine.match(a, b, top_k=top_k, reciprocal=recip, confidence_threshold=thr)
+    assert len(u.idx_1) != len(r.idx_1) or not np.array_equal(u.confidence, r.confidence)
+
+
 def test_match_kats_gpu(matcher_engine):
     rng = np.random.default_rng(0)
     desc = rng.random((8, 8, 64)).astype(np.float32)

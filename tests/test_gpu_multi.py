@@ -44,6 +44,23 @@ def test_sharded_match_bit_exact(two_gpus, oracle_lib, h, w, d, top_k, recip, th
     eng.close()
 
 
+def test_sharded_confidence_weighted_match_bit_exact(two_gpus, oracle_lib):
+    from mast3r_runtime_b200 import NativeEngine, tiny_dims
+
+    eng = NativeEngine(tiny_dims(), (32, 32), two_gpus, 1)
+    a, b = matcher_inputs(96, 128, 24, 91)
+    rng = np.random.default_rng(4)
+    c1 = (1.0 + rng.random((96, 128))).astype(np.float32)
+    c2 = (1.0 + rng.random((96, 128))).astype(np.float32)
+    kw = dict(top_k=512, reciprocal=True, confidence_threshold=1.0, conf_1=c1, conf_2=c2)
+    r = eng.match(a, b, **kw)
+    o = oracle_lib.match(a, b, **kw)
+    np.testing.assert_array_equal(r.idx_1, o["idx_1"])
+    np.testing.assert_array_equal(r.idx_2, o["idx_2"])
+    assert r.confidence.tobytes() == o["confidence"].tobytes()
+    eng.close()
+
+
 def test_pairs_sharded_over_devices_match_single_device(two_gpus, tmp_path):
     from mast3r_runtime_b200 import NativeEngine, make_weights, save_safetensors, tiny_dims
 

@@ -169,6 +169,42 @@ def test_matcher_non_finite_matches_reference_cpp(oracle_lib, kind, a, b):
         assert all(np.float32(got[k]).tobytes() == np.float32(want[k]).tobytes() for k in got)
 
 
+def _conf_case(seed, h=12, w=16, d=24):
+    a, b = matcher_inputs(h, w, d, seed)
+    rng = np.random.default_rng(seed + 1)
+    c1 = (1.0 + rng.random((h, w))).astype(np.float32)      # confidences >= 1, as the head's 1 + exp
+    c2 = (1.0 + rng.random((h, w))).astype(np.float32)
+    p1 = rng.standard_normal((h, w, 3)).astype(np.float32)
+    p2 = rng.standard_normal((h, w, 3)).astype(np.float32)
+    return a, b, c1, c2, p1, p2
+
+
+@pytest.mark.parametrize("recip", [True, False])
+def test_matcher_confidence_weighted_matches_reference_cpp(oracle_lib, recip):
+    """conf_1 / conf_2 weighting (matching.cpp:110-119) against the reference's own C++."""
+    if oracle_lib.ref_lib() is None:
+        pytest.skip("oracle/_ref not built (reference tree absent)")
+    for seed in (3, 4):
+        a, b, c1, c2, _, _ = _conf_case(seed)
+        for thr in (0.0, 1.5):
+            o = oracle_lib.match(a, b, top_k=64, reciprocal=recip, confidence_threshold=thr, conf_1=c1, conf_2=c2)
+            r = oracle_lib.ref_match(a, b, top_k=64, reciprocal=recip, confidence_threshold=thr, conf_1=c1, conf_2=c2)
+            got = {(int(i), int(j)): c for i, j, c in zip(o["idx_1"], o["idx_2"], o["confidence"])}
+            want = {(int(i), int(j)): c for i, j, c in zip(r["idx_1"], r["idx_2"], r["confidence"])}
+            assert got.keys() == want.keys() and len(got) > 0
+            assert all(np.float32(got[k]).tobytes() == np.float32(want[k]).tobytes() for k in got)
+
+
+def test_matcher_pts3d_gather_as_numpy_path(oracle_lib):
+    """pts3d of the matches: pts3d_1[idx_1], pts3d_2[idx_2] (matching.py:144-152)."""
+    a, b, c1, c2, p1, p2 = _conf_case(5)
+    o = oracle_lib.match(a, b, top_k=64, confidence_threshold=0.0, conf_1=c1, conf_2=c2, pts3d_1=p1, pts3d_2=p2)
+    np.testing.assert_array_equal(o["pts3d_1"], p1.reshape(-1, 3)[o["idx_1"]])
+    np.testing.assert_array_equal(o["pts3d_2"], p2.reshape(-1, 3)[o["idx_2"]])
+    z = oracle_lib.match(a, b, top_k=64, confidence_threshold=0.0)
+    assert not z["pts3d_1"].any()
+
+
 def test_matcher_kats(oracle_lib):
     # tests/unit/test_matching.py:27-35: [3, 4] -> [0.6, 0.8]
     n = oracle_lib.normalize(np.array([[3.0, 4.0], [1.0, 0.0]], np.float32))
