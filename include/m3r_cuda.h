@@ -28,7 +28,7 @@ extern "C" {
 #pragma GCC visibility push(default)
 #endif
 
-#define M3R_ABI_VERSION 1
+#define M3R_ABI_VERSION 2
 
 #define M3R_OK 0
 #define M3R_ERR_ARG (-1)     /* bad argument, shape or size */
@@ -47,6 +47,16 @@ extern "C" {
 #define M3R_DTYPE_BF16 0
 #define M3R_DTYPE_F16 1
 
+/* Output heads.  M3R_HEAD_MAST3R24: the MASt3R DPT + local-feature head, 24-d
+ * L2-normalised descriptors (csrc/mps/mpsgraph_engine.mm:383-437; desc_dim 24).
+ * M3R_HEAD_REF_SIMPLE: the reference's CPU head MASt3RDPTHead
+ * (mast3r_runtime/backends/python/mast3r_model.py:86-156): 3x3 / 3x3 / 1x1 convs of the
+ * first 256 decoder channels at patch-grid resolution, bilinear upsampling
+ * (dpt_head.py:72-116), and the first 256 local-feature channels as unnormalised
+ * descriptors (desc_dim 256). */
+#define M3R_HEAD_MAST3R24 0
+#define M3R_HEAD_REF_SIMPLE 1
+
 /* Model architecture + runtime shape.  Dimensions follow the reference's model
  * table (csrc/common/types.hpp:51-69, csrc/mps/graph_builder.hpp:67-77). */
 typedef struct m3r_config {
@@ -54,12 +64,13 @@ typedef struct m3r_config {
     int enc_dim, enc_depth, enc_heads, enc_mlp;
     int dec_dim, dec_depth, dec_heads, dec_mlp;
     int lf_hidden;  /* local-feature MLP width */
-    int desc_dim;   /* 24 */
+    int desc_dim;   /* output descriptor channels: 24 (M3R_HEAD_MAST3R24) or 256 (M3R_HEAD_REF_SIMPLE) */
     int img_h, img_w;   /* input image size, multiples of `patch` */
     int n_devices;      /* 0 = device 0 only */
     int devices[M3R_MAX_DEVICES];
     int max_pairs;      /* image pairs per device per launch (activation buffers) */
     int dtype;          /* M3R_DTYPE_F16 or M3R_DTYPE_BF16 */
+    int head;           /* M3R_HEAD_MAST3R24 or M3R_HEAD_REF_SIMPLE */
 } m3r_config;
 
 /* Slots of the timing_ms array written by m3r_infer / m3r_match.  m3r_match uses

@@ -74,12 +74,14 @@ def get_compute_capability(device: int = 0) -> tuple[int, int]:
 
 
 def make_config(dims: ModelDims, image_hw: tuple[int, int], devices=(0,), max_pairs: int = 1,
-                dtype: int = _lib.DTYPE_F16) -> _lib.M3RConfig:
+                dtype: int = _lib.DTYPE_F16, head: int = _lib.HEAD_MAST3R24) -> _lib.M3RConfig:
     c = _lib.M3RConfig()
     c.patch = dims.patch
     c.enc_dim, c.enc_depth, c.enc_heads, c.enc_mlp = dims.enc_dim, dims.enc_depth, dims.enc_heads, dims.enc_mlp
     c.dec_dim, c.dec_depth, c.dec_heads, c.dec_mlp = dims.dec_dim, dims.dec_depth, dims.dec_heads, dims.dec_mlp
-    c.lf_hidden, c.desc_dim = dims.lf_hidden, dims.desc_dim
+    c.lf_hidden = dims.lf_hidden
+    c.desc_dim = _lib.HEAD_DESC_DIM[int(head)]
+    c.head = int(head)
     c.img_h, c.img_w = int(image_hw[0]), int(image_hw[1])
     devices = list(devices)
     if len(devices) > _lib.M3R_MAX_DEVICES:
@@ -102,7 +104,8 @@ def _env_devices() -> list[int]:
 class NativeEngine:
     """One libm3r_cuda engine: fixed model dims, image size, device list and launch size."""
 
-    def __init__(self, dims: ModelDims, image_hw, devices=(0,), max_pairs: int = 1, dtype: int = _lib.DTYPE_F16):
+    def __init__(self, dims: ModelDims, image_hw, devices=(0,), max_pairs: int = 1, dtype: int = _lib.DTYPE_F16,
+                 head: int = _lib.HEAD_MAST3R24):
         self.lib = _lib.load()
         self.dims = dims
         self.image_hw = (int(image_hw[0]), int(image_hw[1]))
@@ -110,7 +113,9 @@ class NativeEngine:
         self.max_pairs = int(max_pairs)
         self.dtype = int(dtype)
         self.dtype_name = _lib.DTYPE_NAMES[self.dtype]
-        cfg = make_config(dims, self.image_hw, self.devices, self.max_pairs, self.dtype)
+        self.head = int(head)
+        self.desc_dim = _lib.HEAD_DESC_DIM[self.head]  # output descriptor channels
+        cfg = make_config(dims, self.image_hw, self.devices, self.max_pairs, self.dtype, self.head)
         h = ctypes.c_void_p()
         _lib.check(self.lib.m3r_create(ctypes.byref(cfg), ctypes.byref(h)))
         self.h = h
@@ -134,7 +139,7 @@ class NativeEngine:
 
     def _out_arrays(self, n: int, alloc=np.empty):
         H, W = self.image_hw
-        D = self.dims.desc_dim
+        D = self.desc_dim
         return {
             "pts3d_1": alloc((n, H, W, 3), np.float32), "pts3d_2": alloc((n, H, W, 3), np.float32),
             "desc_1": alloc((n, H, W, D), np.float32), "desc_2": alloc((n, H, W, D), np.float32),
@@ -262,10 +267,15 @@ class CUDAEngine:
     ``resolution`` x ``resolution`` (the reference engines' convention) or of any other
     size that is a multiple of the patch: an engine for a new size is created on first
     use with the already-loaded weights file.  Devices: M3R_CUDA_DEVICES (default "0").
+    ``head``: "mast3r24" (the MASt3R DPT + local-feature head, 24-d L2-normalised
+    descriptors) or "ref_simple" (the reference's CPU head MASt3RDPTHead,
+    backends/python/mast3r_model.py:86-156: 256-d raw descriptors, convs at patch-grid
+    resolution, bilinear upsampling).
     """
 
     def __init__(self, variant: str = "dune_vit_small_336", resolution: int = 336, precision: str = "fp16",
-                 num_threads: int = 4, image_size: tuple[int, int] | None = None, devices=None):
+                 num_threads: int = 4, image_size: tuple[int, int] | None = None, devices=None,
+                 head: str = "mast3r24"):
         if variant not in VARIANTS:
             raise RuntimeError(f"Unknown model variant: {variant}")
         self.variant = variant
@@ -275,6 +285,9 @@ class CUDAEngine:
         self.num_threads = int(num_threads)
         self.image_hw = tuple(image_size) if image_size is not None else (int(resolution), int(resolution))
         self.devices = list(devices) if devices is not None else _env_devices()
+        if head not in _lib.HEADS:
+            raise RuntimeError(f"Unknown head: {head} (mast3r24 or ref_simple)")
+        self.head = _lib.HEADS[head]
         self._engines: dict[tuple, NativeEngine] = {}
         self._path: str | None = None
         self._matcher: NativeEngine | None = None
@@ -352,7 +365,7 @@ class CUDAEngine:
             # drop engines of the same size but another launch size, to bound memory
             for k in [k for k in self._engines if k[0] == tuple(hw)]:
                 self._engines.pop(k).close()
-            eng = NativeEngine(self.dims, hw, self.devices, max_pairs, self.dtype)
+            eng = NativeEngine(self.dims, hw, self.devices, max_pairs, self.dtype, self.head)
             eng.load(self._path)
             self._engines[key] = eng
         return eng

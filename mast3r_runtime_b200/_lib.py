@@ -37,9 +37,14 @@ class M3RConfig(ctypes.Structure):
         ("dec_mlp", ctypes.c_int), ("lf_hidden", ctypes.c_int), ("desc_dim", ctypes.c_int),
         ("img_h", ctypes.c_int), ("img_w", ctypes.c_int),
         ("n_devices", ctypes.c_int), ("devices", ctypes.c_int * M3R_MAX_DEVICES),
-        ("max_pairs", ctypes.c_int), ("dtype", ctypes.c_int),
+        ("max_pairs", ctypes.c_int), ("dtype", ctypes.c_int), ("head", ctypes.c_int),
     ]
 
+
+HEAD_MAST3R24 = 0     # 24-d MASt3R DPT + local-feature head
+HEAD_REF_SIMPLE = 1   # the reference's CPU head (256-d raw descriptors)
+HEADS = {"mast3r24": HEAD_MAST3R24, "ref_simple": HEAD_REF_SIMPLE}
+HEAD_DESC_DIM = {HEAD_MAST3R24: 24, HEAD_REF_SIMPLE: 256}
 
 DTYPE_BF16 = 0
 DTYPE_F16 = 1

@@ -47,6 +47,7 @@ Dims Dims::from(const m3r_config& c) {
     d.dec_mlp = c.dec_mlp;
     d.lf_hidden = c.lf_hidden;
     d.desc_dim = c.desc_dim;
+    d.head = c.head;
     d.H = c.img_h;
     d.W = c.img_w;
     M3R_REQUIRE(d.patch > 0 && d.H > 0 && d.W > 0 && d.H % d.patch == 0 && d.W % d.patch == 0,
@@ -66,7 +67,9 @@ Dims Dims::from(const m3r_config& c) {
     M3R_REQUIRE(d.enc_dim % 128 == 0 && d.dec_dim % 128 == 0, "model dims must be multiples of 128");
     M3R_REQUIRE(d.enc_mlp % 64 == 0 && d.dec_mlp % 64 == 0 && d.lf_hidden % 64 == 0, "MLP widths must be multiples of 64");
     M3R_REQUIRE(d.enc_dim <= 1024 && d.dec_dim <= 1024, "model dims above 1024 are not supported");
-    M3R_REQUIRE(d.desc_dim == 24, "descriptor dim must be 24");
+    M3R_REQUIRE(d.head == M3R_HEAD_MAST3R24 || d.head == M3R_HEAD_REF_SIMPLE, "unknown head");
+    M3R_REQUIRE(d.desc_dim == (d.head == M3R_HEAD_MAST3R24 ? 24 : 256),
+                "descriptor dim must be 24 (MASt3R head) or 256 (reference CPU head)");
     M3R_REQUIRE((d.patch * d.patch) % 8 == 0 || (d.patch * d.patch) % 4 == 0, "unsupported patch size");
     M3R_REQUIRE(d.hg % 2 == 0 && d.wg % 2 == 0, "patch grid must have even height and width");
     M3R_REQUIRE(d.dec_depth >= 4, "decoder depth must be >= 4");
@@ -235,6 +238,8 @@ public:
                   *f2 = nullptr, *rn2 = nullptr, *f3a = nullptr, *col3 = nullptr, *f3 = nullptr, *rn3 = nullptr,
                   *fused = nullptr, *up1 = nullptr, *hd0 = nullptr, *up2 = nullptr, *lf1 = nullptr;
     float* out4 = nullptr;
+    uint16_t* hdg = nullptr;  // reference CPU head: first conv's output at grid resolution
+    float* rawd = nullptr;    // reference CPU head: first 256 local-feature channels [tokens, 256]
     float *o_pts = nullptr, *o_conf = nullptr, *o_desc = nullptr;
     MatchWorkspace mws;
 
@@ -264,6 +269,17 @@ public:
         hook1 = bf(T * d_.dec_dim);
         hook2 = bf(T * d_.dec_dim);
         dec_out = bf(T * d_.dec_dim);
+        lf1 = bf(Tv * d_.lf_hidden);
+        o_pts = f32(2 * P * d_.H * d_.W * 3);
+        o_conf = f32(2 * P * d_.H * d_.W);
+        o_desc = f32(2 * P * d_.H * d_.W * d_.desc_dim);
+        if (d_.head == M3R_HEAD_REF_SIMPLE) {
+            // the reference CPU head works at patch-grid resolution, one view at a time
+            hdg = bf(Tv * 128);
+            out4 = f32(Tv * 4);
+            rawd = f32(Tv * 256);
+            return;
+        }
         // DPT / local features, one view at a time
         f0a = bf(Tv * 96);
         f0 = bf(P * 16 * hg * wg * 96);
@@ -282,10 +298,6 @@ public:
         hd0 = bf(P * 64 * hg * wg * 128);
         up2 = bf(P * 256 * hg * wg * 128);
         out4 = f32(P * 256 * hg * wg * 4);
-        lf1 = bf(Tv * d_.lf_hidden);
-        o_pts = f32(2 * P * d_.H * d_.W * 3);
-        o_conf = f32(2 * P * d_.H * d_.W);
-        o_desc = f32(2 * P * d_.H * d_.W * d_.desc_dim);
     }
 
     // ------------------------------------------------------------ profiling
@@ -505,7 +517,12 @@ public:
             case 2: stage_decoder(n); break;
             default:
                 // heads, one view at a time (downstream_head1 / downstream_head2)
-                for (int view = 0; view < 2; ++view) heads(view, n, slot);
+                for (int view = 0; view < 2; ++view) {
+                    if (d_.head == M3R_HEAD_REF_SIMPLE)
+                        heads_ref(view, n, slot);
+                    else
+                        heads(view, n, slot);
+                }
         }
     }
 
@@ -669,6 +686,53 @@ public:
                 gemm_rows(stream_, d_.dt, bn, EPI_DESC, lf1, d.lf_hidden, static_cast<int>(Tv), d.lf_hidden, Hh.lf2.w, d.lf_hidden, Hh.lf2.out, p);
             });
         }
+    }
+
+    // The reference's CPU head (mast3r_model.py:86-156), per view: local features =
+    // MLP(dec || enc) (the decoder features first, :106-110), of which the first 256
+    // channels are the descriptors; pts3d / confidence = conv3x3 + ReLU, conv3x3 + ReLU,
+    // conv1x1 of the first 256 decoder channels (:118-131) at patch-grid resolution;
+    // both bilinearly upsampled to the image (dpt_head.py:72-116).
+    void heads_ref(int view, int n, int slot) {
+        const Dims& d = d_;
+        const Head& Hh = head[view];
+        const long long N = d.ntok, Tv = static_cast<long long>(n) * N;
+        const uint16_t* he = enc_out + view * Tv * d.enc_dim;
+        const uint16_t* hd = dec_out + view * Tv * d.dec_dim;
+        {
+            GemmParams p = gp();
+            p.bias = Hh.lf1.b;
+            p.act = ACT_GELU;
+            p.out = lf1;
+            p.ldo = d.lf_hidden;
+            launch(kGemm, 2.0 * Tv * Hh.lf1.out * Hh.lf1.in, "lf.fc1", [&] {
+                gemm_concat(stream_, d_.dt, 256, EPI_BF16, hd, d.dec_dim, d.dec_dim, he, d.enc_dim, d.enc_dim,
+                            static_cast<int>(Tv), Hh.lf1.w, Hh.lf1.in, Hh.lf1.out, p);
+            });
+        }
+        linear("lf.fc2", lf1, Tv, Hh.lf2, EPI_F32, rawd, 256);
+        // head convs on the first min(256, dec_dim) decoder channels (the tiling of a
+        // narrower decoder is folded into the first conv's weights at load time)
+        const int c0 = std::min(256, d.dec_dim);
+        {
+            GemmParams p = gp();
+            p.bias = Hh.hd0.b;
+            p.act = ACT_RELU;
+            p.out = hdg;
+            p.ldo = 128;
+            const double fl = 2.0 * Tv * 128.0 * 9 * c0;
+            launch(kGemm, fl, "head.conv0", [&] {
+                gemm_conv3(stream_, d_.dt, 128, EPI_BF16, hd, n, d.hg, d.wg, c0, d.dec_dim, Hh.hd0.w, 128, p);
+            });
+        }
+        conv3("head.conv_out", hdg, n, d.hg, d.wg, 128, Hh.hd2, EPI_HEAD4, out4, ACT_RELU, 128, Hh.w4, Hh.b4);
+        float* pts = out_slot(o_pts, 3, view, slot);
+        float* conf = out_slot(o_conf, 1, view, slot);
+        float* desc = out_slot(o_desc, 256, view, slot);
+        launch(kOther, 0, "head.upsample", [&] {
+            upsample_ref_split(stream_, out4, n, d.hg, d.wg, d.H, d.W, pts, conf);
+            upsample_ref(stream_, rawd, n, d.hg, d.wg, 256, d.H, d.W, desc);
+        });
     }
 
     // Whole inference of n pairs on this device with host buffers: the pairs run in
@@ -997,6 +1061,33 @@ HostModel read_model(const std::string& path, const Dims& d) {
     for (int view = 0; view < 2; ++view) {
         const std::string t = std::string(view == 0 ? "downstream_head1" : "downstream_head2") + ".dpt.";
         HostHead& H = hh[view];
+        const std::string lf = std::string(view == 0 ? "downstream_head1" : "downstream_head2") + ".head_local_features.";
+        if (d.head == M3R_HEAD_REF_SIMPLE) {
+            // mast3r_model.py:86-156: head.0 / head.2 / head.4 on the first 256 decoder
+            // channels (a decoder narrower than 256 is tiled, :120-125: its tiling is folded
+            // into head.0's weights); descriptors = the first 256 outputs of the local
+            // features' fc2 (:139-146), whose fc1 reads (decoder || encoder) (:106-110)
+            const int c0 = std::min(256, Dd);
+            auto w0 = f.load_f32(t + "head.0.weight", {128, 256, 3, 3});
+            std::vector<float> folded(static_cast<size_t>(128) * c0 * 9, 0.0f);
+            for (int o = 0; o < 128; ++o)
+                for (int k = 0; k < 256; ++k)
+                    for (int tap = 0; tap < 9; ++tap)
+                        folded[(static_cast<size_t>(o) * c0 + k % Dd) * 9 + tap] += w0[(static_cast<size_t>(o) * 256 + k) * 9 + tap];
+            H.hd0 = conv3_weights(dt, folded, 128, c0, V(t + "head.0.bias", 128));
+            H.hd2 = conv3_weights(dt, f.load_f32(t + "head.2.weight", {128, 128, 3, 3}), 128, 128, V(t + "head.2.bias", 128));
+            H.w4 = f.load_f32(t + "head.4.weight", {4, 128, 1, 1});
+            H.b4 = V(t + "head.4.bias", 4);
+            H.lf1 = L(lf + "fc1", d.lf_hidden, Dd + d.enc_dim);
+            const int rows = 25 * p * p;  // the checkpoint's fc2: (24 + 1) p^2 outputs
+            M3R_REQUIRE(rows >= 256, "local-feature head has fewer than 256 outputs");
+            auto w = f.load_f32(lf + "fc2.weight", {rows, d.lf_hidden});
+            auto b = V(lf + "fc2.bias", rows);
+            w.resize(static_cast<size_t>(256) * d.lf_hidden);
+            b.resize(256);
+            H.lf2 = to16(dt, w, 256, d.lf_hidden, b);
+            continue;
+        }
         auto conv1 = [&](const std::string& name, int out, int in) {
             auto w = f.load_f32(name + ".weight", {out, in, 1, 1});
             return to16(dt, w, out, in, V(name + ".bias", out));
@@ -1018,7 +1109,6 @@ HostModel read_model(const std::string& path, const Dims& d) {
         H.hd2 = conv3_weights(dt, f.load_f32(t + "head.2.weight", {128, 128, 3, 3}), 128, 128, V(t + "head.2.bias", 128));
         H.w4 = f.load_f32(t + "head.4.weight", {4, 128, 1, 1});
         H.b4 = V(t + "head.4.bias", 4);
-        const std::string lf = std::string(view == 0 ? "downstream_head1" : "downstream_head2") + ".head_local_features.";
         H.lf1 = L(lf + "fc1", d.lf_hidden, d.enc_dim + Dd);
         {
             // keep the desc_dim descriptor channels of every (dy, dx) group of desc_dim + 1

@@ -16,7 +16,8 @@ namespace m3r {
 struct Dims {
     int patch, enc_dim, enc_depth, enc_heads, enc_mlp;
     int dec_dim, dec_depth, dec_heads, dec_mlp;
-    int lf_hidden, desc_dim;
+    int lf_hidden, desc_dim;  // desc_dim: output descriptor channels (24, or 256 for the reference CPU head)
+    int head;                 // M3R_HEAD_MAST3R24 or M3R_HEAD_REF_SIMPLE
     int H, W, hg, wg, ntok;
     int kpad;  // patch-embed K (3 p^2) rounded up to 64
     int hook1, hook2;

@@ -269,6 +269,67 @@ __global__ void im2col_s2_kernel(const uint16_t* __restrict__ x, int n, int h, i
     }
 }
 
+// Source rows / columns of output index i under the reference CPU head's bilinear
+// resize (backends/python/dpt_head.py:72-116): src = i * in / out (no half-pixel
+// offset), i0 = floor(src), i1 = min(i0 + 1, in - 1), f = src - i0; the rational src
+// is formed exactly in integers.
+__device__ __forceinline__ void ref_coord(int i, int in, int out, int& i0, int& i1, float& f) {
+    const long long num = static_cast<long long>(i) * in;
+    i0 = static_cast<int>(num / out);
+    f = static_cast<float>(num - static_cast<long long>(i0) * out) / static_cast<float>(out);
+    i1 = min(i0 + 1, in - 1);
+}
+
+// the four-term blend in the reference's order: (1-fh)(1-fw) a + (1-fh) fw b + fh (1-fw) c + fh fw d
+__device__ __forceinline__ float ref_blend(float a, float b, float c, float d, float fh, float fw) {
+    return (1.0f - fh) * (1.0f - fw) * a + (1.0f - fh) * fw * b + fh * (1.0f - fw) * c + fh * fw * d;
+}
+
+// [n, hi, wi, C] fp32 -> [n, ho, wo, C] fp32, four channels per thread (C % 4 == 0)
+__global__ void upsample_ref_kernel(const float4* __restrict__ x, int n, int hi, int wi, int C4, int ho, int wo,
+                                    float4* __restrict__ y) {
+    const long long total = static_cast<long long>(n) * ho * wo * C4;
+    for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
+         e += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int c = static_cast<int>(e % C4);
+        const long long pix = e / C4;
+        const int ox = static_cast<int>(pix % wo);
+        const int oy = static_cast<int>((pix / wo) % ho);
+        const int im = static_cast<int>(pix / (static_cast<long long>(wo) * ho));
+        int y0, y1, x0, x1;
+        float fh, fw;
+        ref_coord(oy, hi, ho, y0, y1, fh);
+        ref_coord(ox, wi, wo, x0, x1, fw);
+        const float4* base = x + static_cast<long long>(im) * hi * wi * C4 + c;
+        const float4 a = base[(static_cast<long long>(y0) * wi + x0) * C4], b = base[(static_cast<long long>(y0) * wi + x1) * C4];
+        const float4 q = base[(static_cast<long long>(y1) * wi + x0) * C4], d = base[(static_cast<long long>(y1) * wi + x1) * C4];
+        y[e] = make_float4(ref_blend(a.x, b.x, q.x, d.x, fh, fw), ref_blend(a.y, b.y, q.y, d.y, fh, fw),
+                           ref_blend(a.z, b.z, q.z, d.z, fh, fw), ref_blend(a.w, b.w, q.w, d.w, fh, fw));
+    }
+}
+
+// [n, hi, wi, 4] fp32 (pts3d xyz, confidence) -> pts3d [n, ho, wo, 3], conf [n, ho, wo]
+__global__ void upsample_ref_split_kernel(const float4* __restrict__ x, int n, int hi, int wi, int ho, int wo,
+                                          float* __restrict__ pts, float* __restrict__ conf) {
+    const long long total = static_cast<long long>(n) * ho * wo;
+    for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
+         e += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int ox = static_cast<int>(e % wo);
+        const int oy = static_cast<int>((e / wo) % ho);
+        const int im = static_cast<int>(e / (static_cast<long long>(wo) * ho));
+        int y0, y1, x0, x1;
+        float fh, fw;
+        ref_coord(oy, hi, ho, y0, y1, fh);
+        ref_coord(ox, wi, wo, x0, x1, fw);
+        const float4* base = x + static_cast<long long>(im) * hi * wi;
+        const float4 a = base[y0 * wi + x0], b = base[y0 * wi + x1], q = base[y1 * wi + x0], d = base[y1 * wi + x1];
+        pts[e * 3 + 0] = ref_blend(a.x, b.x, q.x, d.x, fh, fw);
+        pts[e * 3 + 1] = ref_blend(a.y, b.y, q.y, d.y, fh, fw);
+        pts[e * 3 + 2] = ref_blend(a.z, b.z, q.z, d.z, fh, fw);
+        conf[e] = ref_blend(a.w, b.w, q.w, d.w, fh, fw);
+    }
+}
+
 __global__ void head_split_kernel(const float* __restrict__ o4, int n, int h4, int w4, int H, int W,
                                   float* __restrict__ pts, float* __restrict__ conf) {
     const long long total = static_cast<long long>(n) * H * W;
@@ -369,6 +430,24 @@ void im2col_s2(cudaStream_t s, const void* x, int n, int h, int w, int C, void* 
     const long long total = static_cast<long long>(n) * ho * wo * 9 * (C / 8);
     im2col_s2_kernel<<<grid_for(total, 256), 256, 0, s>>>(static_cast<const uint16_t*>(x), n, h, w, C,
                                                           static_cast<uint16_t*>(out));
+    M3R_CUDA(cudaGetLastError());
+}
+
+void upsample_ref(cudaStream_t s, const float* x, int n, int hi, int wi, int C, int ho, int wo, float* y) {
+    M3R_REQUIRE(C % 4 == 0, "upsample_ref: channels must be a multiple of 4");
+    M3R_REQUIRE(((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0,
+                "upsample_ref: buffers must be 16-byte aligned");
+    const long long total = static_cast<long long>(n) * ho * wo * (C / 4);
+    upsample_ref_kernel<<<grid_for(total, 256), 256, 0, s>>>(reinterpret_cast<const float4*>(x), n, hi, wi, C / 4, ho,
+                                                              wo, reinterpret_cast<float4*>(y));
+    M3R_CUDA(cudaGetLastError());
+}
+
+void upsample_ref_split(cudaStream_t s, const float* x4, int n, int hi, int wi, int ho, int wo, float* pts3d,
+                        float* conf) {
+    const long long total = static_cast<long long>(n) * ho * wo;
+    upsample_ref_split_kernel<<<grid_for(total, 256), 256, 0, s>>>(reinterpret_cast<const float4*>(x4), n, hi, wi, ho,
+                                                                    wo, pts3d, conf);
     M3R_CUDA(cudaGetLastError());
 }
 

@@ -34,4 +34,11 @@ void im2col_s2(cudaStream_t s, const void* x, int n, int h, int w, int C, void* 
 // (half-pixel) when (h4, w4) != (H, W).
 void head_split(cudaStream_t s, const float* out4, int n, int h4, int w4, int H, int W, float* pts3d, float* conf);
 
+// The reference CPU head's bilinear resize (backends/python/dpt_head.py:72-116: src = i *
+// in / out, no half-pixel offset) of fp32 NHWC maps: [n, hi, wi, C] -> [n, ho, wo, C]
+// (C % 4 == 0), and of the 4-channel head output into pts3d [n, ho, wo, 3] + conf [n, ho, wo].
+void upsample_ref(cudaStream_t s, const float* x, int n, int hi, int wi, int C, int ho, int wo, float* y);
+void upsample_ref_split(cudaStream_t s, const float* x4, int n, int hi, int wi, int ho, int wo, float* pts3d,
+                        float* conf);
+
 }  // namespace m3r

@@ -48,18 +48,20 @@ def test_config_layout_matches_c(tmp_path):
         #include <stdio.h>
         #include "m3r_cuda.h"
         int main(void) {
-          printf("%zu %zu %zu %zu %d %d\\n", sizeof(m3r_config), offsetof(m3r_config, devices),
-                 offsetof(m3r_config, max_pairs), offsetof(m3r_config, dtype), M3R_T_COUNT, M3R_ABI_VERSION);
+          printf("%zu %zu %zu %zu %zu %d %d\\n", sizeof(m3r_config), offsetof(m3r_config, devices),
+                 offsetof(m3r_config, max_pairs), offsetof(m3r_config, dtype), offsetof(m3r_config, head),
+                 M3R_T_COUNT, M3R_ABI_VERSION);
           return 0;
         }
     """))
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
-    size, off_dev, off_mp, off_dt, tcount, ver = map(int, subprocess.run([str(exe)], capture_output=True, text=True,
-                                                                         check=True).stdout.split())
+    size, off_dev, off_mp, off_dt, off_head, tcount, ver = map(int, subprocess.run(
+        [str(exe)], capture_output=True, text=True, check=True).stdout.split())
     C = _lib.M3RConfig
     assert ctypes.sizeof(C) == size
     assert C.devices.offset == off_dev and C.max_pairs.offset == off_mp and C.dtype.offset == off_dt
+    assert C.head.offset == off_head
     assert tcount == len(_lib.TIMING_KEYS)
     assert _lib.load().m3r_version() == ver
 

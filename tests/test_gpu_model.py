@@ -200,3 +200,37 @@ def test_pipelined_infer_matches_resident(tmp_path):
     for k in ref:
         np.testing.assert_array_equal(again[k], ref[k])
     eng.close()
+
+
+@pytest.mark.parametrize("dims_name,hw", [("tiny", (64, 96)), ("dune_vit_small_336", (336, 336))])
+def test_reference_cpu_head_matches_oracle(tmp_path, dims_name, hw):
+    """head="ref_simple": the reference's own CPU head (mast3r_model.py:86-156) on the GPU,
+    against the oracle's restatement of it (pinned to the reference's outputs by
+    tests/test_oracle.py::test_ref_simple_head_matches_reference): 256-d unnormalised
+    descriptors, pts3d / confidence from convs at patch-grid resolution, bilinear
+    upsampling.  Bar: pts3d relative L2 <= 1e-2, descriptor cosine >= 0.999."""
+    from mast3r_runtime_b200 import NativeEngine, _lib, make_weights, save_safetensors
+    from mast3r_runtime_b200.weights import VARIANTS, tiny_dims
+    from oracle.model import Model
+
+    d = tiny_dims() if dims_name == "tiny" else VARIANTS[dims_name]
+    w = make_weights(d, seed=21, randomize_affine=True)
+    path = save_safetensors(tmp_path / "unified.safetensors", w)
+    rng = np.random.default_rng(22)
+    img1 = rng.integers(0, 256, (1, *hw, 3), dtype=np.uint8)
+    img2 = rng.integers(0, 256, (1, *hw, 3), dtype=np.uint8)
+    eng = NativeEngine(d, hw, [0], 1, _lib.DTYPE_F16, _lib.HEAD_REF_SIMPLE)
+    eng.load(str(path))
+    out, _ = eng.infer_batch(img1, img2)
+    eng.close()
+    ref = Model(w, d).forward(img1[0], img2[0], head="ref_simple")
+    for v in (1, 2):
+        assert out[f"desc_{v}"].shape == (1, *hw, 256)
+        e = rel_l2(out[f"pts3d_{v}"][0], ref[f"pts3d_{v}"])
+        ec = rel_l2(out[f"conf_{v}"][0], ref[f"conf_{v}"])
+        g = out[f"desc_{v}"][0].astype(np.float64)
+        r = np.asarray(ref[f"desc_{v}"], np.float64)
+        cos = (g * r).sum(-1) / np.maximum(np.linalg.norm(g, axis=-1) * np.linalg.norm(r, axis=-1), 1e-30)
+        print(dims_name, v, e, ec, cos.mean(), cos.min())
+        assert e <= 1e-2 and ec <= 1e-2
+        assert cos.mean() >= 0.999
