@@ -116,6 +116,8 @@ class NativeEngine:
         self.head = int(head)
         self.desc_dim = _lib.HEAD_DESC_DIM[self.head]  # output descriptor channels
         cfg = make_config(dims, self.image_hw, self.devices, self.max_pairs, self.dtype, self.head)
+        # pinned output sets recycled across infer_batch calls that allocate their outputs
+        self._pool = _lib.OutputPool(lambda n: self._out_arrays(n, alloc=_lib.pinned_empty))
         h = ctypes.c_void_p()
         _lib.check(self.lib.m3r_create(ctypes.byref(cfg), ctypes.byref(h)))
         self.h = h
@@ -158,10 +160,13 @@ class NativeEngine:
         return img1, img2
 
     def infer_batch(self, img1, img2, out=None):
-        """[N, H, W, 3] uint8 pairs -> dict of [N, ...] fp32 outputs and a timing dict."""
+        """[N, H, W, 3] uint8 pairs -> dict of [N, ...] fp32 outputs and a timing dict.
+
+        Without `out` the outputs are views of recycled page-locked buffers (OutputPool):
+        the device copies land in them directly."""
         img1, img2 = self._check_images(img1, img2)
         n = img1.shape[0]
-        o = out if out is not None else self._out_arrays(n)
+        o = out if out is not None else self._pool.get(n)
         t = np.zeros(len(_lib.TIMING_KEYS), np.float32)
         rc = self.lib.m3r_infer(self.h, _lib.ptr(img1), _lib.ptr(img2), n,
                                 _lib.ptr(o["pts3d_1"]), _lib.ptr(o["pts3d_2"]), _lib.ptr(o["desc_1"]),

@@ -162,6 +162,47 @@ def pinned_empty(shape, dtype) -> np.ndarray:
     return holder
 
 
+class OutputPool:
+    """Recycled page-locked output buffers for the calls that return fresh arrays.
+
+    get(n) returns views of one set of pinned arrays (allocated with `make(n)` when no
+    free set of that size exists); once every view of a set -- and every view made from
+    them -- has been garbage-collected, the set goes back to the free list (at most
+    `keep` free sets per size are kept; the rest are released).  Results the caller
+    still holds are never overwritten, and steady-state calls neither allocate host
+    memory nor fault fresh pages: copies land directly in page-locked memory.
+    """
+
+    def __init__(self, make, keep: int = 2):
+        self._make = make
+        self._keep = keep
+        self._free: dict[int, list] = {}
+        self._lock = threading.Lock()
+
+    def get(self, n: int) -> dict:
+        import weakref
+
+        with self._lock:
+            free = self._free.setdefault(n, [])
+            base = free.pop() if free else None
+        if base is None:
+            base = self._make(n)
+        views = {k: v.view(np.ndarray) for k, v in base.items()}
+        live = [len(views)]
+
+        def _done(_n=n, _base=base, _live=live):
+            _live[0] -= 1
+            if _live[0] == 0:
+                with self._lock:
+                    lst = self._free.setdefault(_n, [])
+                    if len(lst) < self._keep:
+                        lst.append(_base)
+
+        for v in views.values():
+            weakref.finalize(v, _done)
+        return views
+
+
 class _PinnedArray(np.ndarray):
     _owner = None
 

@@ -201,3 +201,34 @@ def test_reference_wrapper_drives_cuda_engine(monkeypatch, tmp_path):
     m = engine.match(res.desc_1, res.desc_2)
     assert m.num_matches == 3 and m.idx_1.dtype == np.int64
     sys.modules.pop("mast3r_runtime.backends._cuda", None)
+
+
+def test_output_pool_recycles_only_released_sets():
+    """OutputPool (pinned outputs of the drop-in calls): a set comes back only when every
+    view of it -- including views made from the returned arrays -- is gone."""
+    import gc
+
+    from mast3r_runtime_b200 import _lib
+
+    made = []
+
+    def make(n):
+        d = {"a": np.zeros((n, 4), np.float32), "b": np.zeros((n, 2), np.float32)}
+        made.append(d)
+        return d
+
+    pool = _lib.OutputPool(make, keep=1)
+    v1 = pool.get(3)
+    v1["a"][:] = 1
+    inner = v1["a"][0]          # a view of a view keeps the set in use
+    del v1
+    gc.collect()
+    v2 = pool.get(3)            # first set still referenced through `inner`
+    assert len(made) == 2 and np.all(inner == 1)
+    del inner, v2
+    gc.collect()
+    v3 = pool.get(3)            # a released set is reused (keep=1: one stays on the free list)
+    assert len(made) == 2
+    assert v3["a"].base is not None
+    v4 = pool.get(5)            # another size: a new set
+    assert len(made) == 3 and v4["a"].shape == (5, 4)

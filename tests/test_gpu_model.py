@@ -162,9 +162,10 @@ def test_profile_per_operation(tmp_path):
 def test_pipelined_infer_matches_resident(tmp_path):
     """infer_batch runs a device's pairs in sub-batches whose output copies overlap the
     next sub-batch's compute; the outputs equal one resident pass over all pairs, and
-    the staged inputs afterwards are the pairs of that call.  Ordinary numpy arrays go
-    through the pinned staging slots (four sub-batches: both slots reused), page-locked
-    ones are copied directly."""
+    the staged inputs afterwards are the pairs of that call.  Outputs allocated by the
+    call are recycled page-locked buffers (a set the caller still holds is not reused);
+    caller-owned ordinary numpy arrays go through the pinned staging slots (four
+    sub-batches: both slots reused); caller-owned page-locked ones are copied directly."""
     from mast3r_runtime_b200 import NativeEngine, make_weights, save_safetensors
     from mast3r_runtime_b200.weights import tiny_dims
 
@@ -180,10 +181,20 @@ def test_pipelined_infer_matches_resident(tmp_path):
     eng.run_resident(n)
     ref = eng.fetch(n)
     for _ in range(3):  # direct launches, then graph capture, then graph replay
-        got, timing = eng.infer_batch(img1, img2)
+        got, timing = eng.infer_batch(img1, img2)  # outputs: recycled pinned buffers
         for k in ref:
             np.testing.assert_array_equal(got[k], ref[k])
     assert timing["encoder_ms"] > 0 and timing["d2h_ms"] > 0
+    held = got
+    again_pool, _ = eng.infer_batch(img1[::-1].copy(), img2[::-1].copy())  # a set still held is not reused
+    for k in ref:
+        np.testing.assert_array_equal(held[k], ref[k])
+        np.testing.assert_array_equal(again_pool[k][::-1], ref[k])
+    # caller-owned pageable outputs go through the pinned staging slots
+    pageable = eng._out_arrays(n)
+    got, _ = eng.infer_batch(img1, img2, out=pageable)
+    for k in ref:
+        np.testing.assert_array_equal(got[k], ref[k])
     # page-locked caller buffers take the direct copies (no staging): same results
     from mast3r_runtime_b200 import _lib
 
