@@ -187,8 +187,7 @@ class OutputPool:
             base = free.pop() if free else None
         if base is None:
             base = self._make(n)
-        views = {k: v.view(np.ndarray) for k, v in base.items()}
-        live = [len(views)]
+        live = [len(base)]
 
         def _done(_n=n, _base=base, _live=live):
             _live[0] -= 1
@@ -198,9 +197,28 @@ class OutputPool:
                     if len(lst) < self._keep:
                         lst.append(_base)
 
-        for v in views.values():
-            weakref.finalize(v, _done)
+        views = {}
+        for k, b in base.items():
+            # every array handed out (and every view of it) reaches the memory through
+            # its lease object, so the lease dies only with the last of them (numpy
+            # collapses view chains onto the array that owns the memory, a lease is not one)
+            lease = _Lease(b)
+            weakref.finalize(lease, _done)
+            views[k] = np.frombuffer(lease, dtype=b.dtype).reshape(b.shape)
         return views
+
+
+class _Lease:
+    """Buffer-protocol handle on one pooled array (see OutputPool.get)."""
+
+    def __init__(self, arr: np.ndarray):
+        self._arr = arr
+
+    def __buffer__(self, flags):
+        return memoryview(self._arr)
+
+    def __release_buffer__(self, view):
+        view.release()
 
 
 class _PinnedArray(np.ndarray):
