@@ -121,6 +121,15 @@ int m3r_is_ready(const m3r_engine* engine);
 int m3r_infer(m3r_engine* engine, const uint8_t* img1, const uint8_t* img2, int n_pairs, float* pts3d_1,
               float* pts3d_2, float* desc_1, float* desc_2, float* conf_1, float* conf_2, float* timing_ms);
 
+/* ---- infer(img1, img2) for images of any size: the path the reference's engines take
+ * for an image whose size differs from the model's -- aspect-preserving bilinear resize
+ * and centre crop (csrc/cpu/preprocessing.cpp:29-63, 84-129; python_engine.py:158-174 with
+ * PIL) -- done on the device, bit-exact with the C++ preprocessing, then the forward pass.
+ * img1 [h1, w1, 3], img2 [h2, w2, 3] uint8; outputs as m3r_infer for one pair. */
+int m3r_infer_any(m3r_engine* engine, const uint8_t* img1, int h1, int w1, const uint8_t* img2, int h2, int w2,
+                  float* pts3d_1, float* pts3d_2, float* desc_1, float* desc_2, float* conf_1, float* conf_2,
+                  float* timing_ms);
+
 /* ---- match(desc_1, desc_2, top_k, reciprocal, confidence_threshold): replaces
  * native.match (native_wrapper.py:122-128) with the semantics of
  * csrc/cpu/matching.cpp:85-237.  desc_*: [height*width, desc_dim] fp32.
@@ -202,6 +211,9 @@ int m3r_conv3_test(int device, int dtype, const uint16_t* x, const uint16_t* w, 
  * normalised descriptors, and the row maxima best_12 [n1]. */
 int m3r_match_nn(int device, const float* desc_1, const float* desc_2, int64_t n1, int64_t n2, int desc_dim,
                  int32_t* nn_12, int32_t* nn_21, float* best_12, float* kernel_ms);
+
+/* The preprocessing kernel of m3r_infer_any alone: uint8 [h, w, 3] -> [out_h, out_w, 3]. */
+int m3r_resize_crop_test(int device, const uint8_t* src, int h, int w, uint8_t* dst, int out_h, int out_w);
 
 /* Self-test of the bounded device waits: a kernel waits on a barrier that nothing
  * signals, with the wait limit limit_ns (0 < limit_ns <= 10 s).  Returns M3R_ERR_TIMEOUT

@@ -174,6 +174,22 @@ class NativeEngine:
         _lib.check(rc, self.h)
         return o, dict(zip(_lib.TIMING_KEYS, map(float, t)))
 
+    def infer_any(self, img1, img2):
+        """One pair of uint8 [h, w, 3] images of any size: resized and centre-cropped to the
+        engine's size on the device (the reference's preprocessing, csrc/cpu/preprocessing.cpp
+        and python_engine.py:158-174), then the forward pass.  Returns ({k: [1, ...]}, timing)."""
+        a = np.ascontiguousarray(img1, dtype=np.uint8)
+        b = np.ascontiguousarray(img2, dtype=np.uint8)
+        if a.ndim != 3 or a.shape[2] != 3 or b.ndim != 3 or b.shape[2] != 3:
+            raise ValueError(f"Expected [H, W, 3] uint8 images, got {a.shape} / {b.shape}")
+        o = self._pool.get(1)
+        t = np.zeros(len(_lib.TIMING_KEYS), np.float32)
+        rc = self.lib.m3r_infer_any(self.h, _lib.ptr(a), a.shape[0], a.shape[1], _lib.ptr(b), b.shape[0], b.shape[1],
+                                    _lib.ptr(o["pts3d_1"]), _lib.ptr(o["pts3d_2"]), _lib.ptr(o["desc_1"]),
+                                    _lib.ptr(o["desc_2"]), _lib.ptr(o["conf_1"]), _lib.ptr(o["conf_2"]), _lib.ptr(t))
+        _lib.check(rc, self.h)
+        return o, dict(zip(_lib.TIMING_KEYS, map(float, t)))
+
     # device-resident stages (throughput measurement)
     def stage(self, img1, img2):
         img1, img2 = self._check_images(img1, img2)
@@ -268,10 +284,11 @@ class NativeEngine:
 class CUDAEngine:
     """``mast3r_runtime.backends._cuda.CUDAEngine``: the object NativeEngineWrapper drives.
 
-    Model dimensions come from ``variant`` (core/config.py:19-28 names); images of
-    ``resolution`` x ``resolution`` (the reference engines' convention) or of any other
-    size that is a multiple of the patch: an engine for a new size is created on first
-    use with the already-loaded weights file.  Devices: M3R_CUDA_DEVICES (default "0").
+    Model dimensions come from ``variant`` (core/config.py:19-28 names); the model input
+    is ``resolution`` x ``resolution`` (the reference engines' convention) or
+    ``image_size`` (any multiple of the patch, e.g. (384, 512)).  Images of another size
+    are resized and centre-cropped to it on the device, as the reference preprocesses
+    them.  Devices: M3R_CUDA_DEVICES (default "0").
     ``head``: "mast3r24" (the MASt3R DPT + local-feature head, 24-d L2-normalised
     descriptors) or "ref_simple" (the reference's CPU head MASt3RDPTHead,
     backends/python/mast3r_model.py:86-156: 256-d raw descriptors, convs at patch-grid
@@ -327,21 +344,34 @@ class CUDAEngine:
             self.infer(dummy, dummy)
 
     def infer(self, img1, img2):
+        """native.infer (native_wrapper.py:84-97).  Images of another size than the engine's
+        are resized and centre-cropped to it on the device, as the reference's engines
+        preprocess them (csrc/cpu/preprocessing.cpp:29-63)."""
         img1 = np.asarray(img1)
         img2 = np.asarray(img2)
         if img1.ndim != 3 or img1.shape[2] != 3 or img2.ndim != 3 or img2.shape[2] != 3:
             raise RuntimeError("Expected [H, W, 3] uint8 array")
-        if img1.shape != img2.shape:
-            raise RuntimeError(f"image shapes differ: {img1.shape} vs {img2.shape}")
-        out, timing = self.infer_batch(img1[None], img2[None])
+        if tuple(img1.shape[:2]) == self.image_hw and tuple(img2.shape[:2]) == self.image_hw:
+            out, timing = self.infer_batch(img1[None], img2[None])
+        else:
+            out, timing = self._engine(self.image_hw, 1).infer_any(img1, img2)
         return SimpleNamespace(**{k: v[0] for k, v in out.items()}, timing=timing)
 
     def infer_batch(self, img1, img2):
-        """[N, H, W, 3] pairs -> dict of [N, ...] outputs, timing (pairs sharded over devices)."""
+        """[N, H, W, 3] pairs -> dict of [N, ...] outputs, timing (pairs sharded over devices).
+        Pairs of another size than the engine's are preprocessed on the device one by one
+        (infer_any), as infer does."""
         img1 = np.asarray(img1)
+        img2 = np.asarray(img2)
         n = img1.shape[0]
+        if tuple(img1.shape[1:3]) != self.image_hw or tuple(img2.shape[1:3]) != self.image_hw:
+            eng = self._engine(self.image_hw, 1)
+            parts = [eng.infer_any(img1[i], img2[i]) for i in range(n)]
+            out = {k: np.concatenate([p[0][k] for p in parts]) for k in parts[0][0]}
+            timing = {k: sum(p[1][k] for p in parts) for k in parts[0][1]}
+            return out, timing
         per_dev = max(1, min(int(os.environ.get("M3R_PAIRS_PER_GPU", "16")), -(-n // len(self.devices))))
-        eng = self._engine(tuple(img1.shape[1:3]), per_dev)
+        eng = self._engine(self.image_hw, per_dev)
         return eng.infer_batch(img1, img2)
 
     def match(self, desc_1, desc_2, top_k: int = 512, reciprocal: bool = True, confidence_threshold: float = 0.5,

@@ -10,6 +10,7 @@
 #include "common.cuh"
 #include "engine.h"
 #include "gemm.h"
+#include "kernels.h"
 #include "matcher.h"
 
 struct m3r_engine {
@@ -164,6 +165,29 @@ int m3r_infer(m3r_engine* engine, const uint8_t* img1, const uint8_t* img2, int 
         M3R_REQUIRE(img1 && img2 && n_pairs >= 1, "infer: null image or n_pairs < 1");
         float* outs[6] = {pts3d_1, pts3d_2, desc_1, desc_2, conf_1, conf_2};
         engine->impl->infer(img1, img2, n_pairs, outs, timing_ms);
+    });
+}
+
+int m3r_infer_any(m3r_engine* engine, const uint8_t* img1, int h1, int w1, const uint8_t* img2, int h2, int w2,
+                  float* pts3d_1, float* pts3d_2, float* desc_1, float* desc_2, float* conf_1, float* conf_2,
+                  float* timing_ms) {
+    if (!engine) return M3R_ERR_ARG;
+    return guarded(engine, [&] {
+        float* outs[6] = {pts3d_1, pts3d_2, desc_1, desc_2, conf_1, conf_2};
+        engine->impl->infer_any(img1, h1, w1, img2, h2, w2, outs, timing_ms);
+    });
+}
+
+int m3r_resize_crop_test(int device, const uint8_t* src, int h, int w, uint8_t* dst, int out_h, int out_w) {
+    return guarded(nullptr, [&] {
+        M3R_REQUIRE(src && dst && h > 0 && w > 0 && out_h > 0 && out_w > 0, "resize_crop_test: bad arguments");
+        m3r::DeviceGuard g(device);
+        const size_t bi = static_cast<size_t>(h) * w * 3, bo = static_cast<size_t>(out_h) * out_w * 3;
+        DBuf din(bi), dout(bo);
+        M3R_CUDA(cudaMemcpy(din.p, src, bi, cudaMemcpyHostToDevice));
+        m3r::resize_crop(nullptr, din.as<uint8_t>(), h, w, dout.as<uint8_t>(), out_h, out_w);
+        M3R_CUDA(cudaDeviceSynchronize());
+        M3R_CUDA(cudaMemcpy(dst, dout.p, bo, cudaMemcpyDeviceToHost));
     });
 }
 

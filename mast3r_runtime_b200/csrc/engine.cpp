@@ -188,6 +188,7 @@ public:
         if (stream_) cudaStreamDestroy(stream_);
         for (void* p : {stage_in_, stage_out_[0], stage_out_[1]})
             if (p) cudaFreeHost(p);
+        if (raw_) cudaFree(raw_);
     }
 
     int dev() const { return dev_; }
@@ -859,6 +860,56 @@ public:
         }
     }
 
+    // One pair of images of any size: resize + centre crop on the device to the model
+    // size (the reference's preprocessing), then the forward pass (slot 0).
+    void infer_any(const uint8_t* img1, int h1, int w1, const uint8_t* img2, int h2, int w2, float* const outs[6],
+                   float* stage_ms, float* h2d_ms, float* d2h_ms) {
+        DeviceGuard g(dev_);
+        const size_t b1 = static_cast<size_t>(h1) * w1 * 3, b2 = static_cast<size_t>(h2) * w2 * 3;
+        if (raw_cap_ < b1 + b2) {
+            if (raw_) M3R_CUDA(cudaFree(raw_));
+            raw_ = nullptr;
+            raw_cap_ = 0;
+            M3R_CUDA(cudaMalloc(&raw_, b1 + b2));
+            raw_cap_ = b1 + b2;
+        }
+        cudaEvent_t* e = stage_ev_;  // 0-4: forward stages, 5-7: copies
+        M3R_CUDA(cudaEventRecord(e[5], stream_));
+        M3R_CUDA(cudaMemcpyAsync(raw_, img1, b1, cudaMemcpyHostToDevice, stream_));
+        M3R_CUDA(cudaMemcpyAsync(raw_ + b1, img2, b2, cudaMemcpyHostToDevice, stream_));
+        M3R_CUDA(cudaEventRecord(e[6], stream_));
+        resize_crop(stream_, raw_, h1, w1, img_slot(0, 0), d_.H, d_.W);
+        resize_crop(stream_, raw_ + b1, h2, w2, img_slot(1, 0), d_.H, d_.W);
+        const bool prof = profiling;
+        profiling = false;
+        float fwd[5];
+        try {
+            forward(1, fwd);
+        } catch (...) {
+            profiling = prof;
+            throw;
+        }
+        profiling = prof;
+        staged = 1;
+        M3R_CUDA(cudaEventElapsedTime(h2d_ms, e[5], e[6]));
+        float pre = 0;
+        M3R_CUDA(cudaEventElapsedTime(&pre, e[6], stage_ev_[0]));  // resizes (+ queueing)
+        for (int i = 0; i < 5; ++i) stage_ms[i] = fwd[i];
+        stage_ms[0] += pre;
+        const size_t px = static_cast<size_t>(d_.H) * d_.W;
+        const int per_px[3] = {3, d_.desc_dim, 1};
+        const float* bases[3] = {o_pts, o_desc, o_conf};
+        M3R_CUDA(cudaEventRecord(e[6], stream_));
+        for (int kind = 0; kind < 3; ++kind)
+            for (int view = 0; view < 2; ++view)
+                if (outs[2 * kind + view])
+                    M3R_CUDA(cudaMemcpyAsync(outs[2 * kind + view], out_slot(bases[kind], per_px[kind], view, 0),
+                                             sizeof(float) * px * per_px[kind], cudaMemcpyDeviceToHost, stream_));
+        M3R_CUDA(cudaEventRecord(e[7], stream_));
+        M3R_CUDA(cudaStreamSynchronize(stream_));
+        M3R_CUDA(cudaEventElapsedTime(d2h_ms, e[6], e[7]));
+    }
+
     static bool is_pageable(const void* p) {
         cudaPointerAttributes a;
         if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
@@ -907,6 +958,8 @@ private:
     int max_pairs_;
     cudaStream_t stream_ = nullptr;
     cudaStream_t copy_stream_ = nullptr;  // host <-> device copies of pipelined infer
+    uint8_t* raw_ = nullptr;              // device copies of images of any size (infer_any)
+    size_t raw_cap_ = 0;
     void* stage_in_ = nullptr;            // pinned staging of pageable caller buffers
     size_t stage_in_cap_ = 0;
     void* stage_out_[2] = {nullptr, nullptr};
@@ -1355,6 +1408,28 @@ void Engine::infer(const uint8_t* img1, const uint8_t* img2, int n_pairs, float*
         d2h += launch_d2h;
         staged_pairs_ = cnt;  // the input slots hold this launch's pairs, as after stage()
     }
+    if (timing) {
+        timing[M3R_T_PREPROCESS] = st[0];
+        timing[M3R_T_ENCODER] = st[1];
+        timing[M3R_T_DECODER] = st[2];
+        timing[M3R_T_HEADS] = st[3];
+        timing[M3R_T_H2D] = h2d;
+        timing[M3R_T_D2H] = d2h;
+        timing[M3R_T_INFERENCE] = st[4];
+        timing[M3R_T_TOTAL] =
+            static_cast<float>(std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count());
+    }
+}
+
+void Engine::infer_any(const uint8_t* img1, int h1, int w1, const uint8_t* img2, int h2, int w2, float* const outs[6],
+                       float* timing) {
+    if (!ready_) throw Error(kErrState, "engine is not loaded");
+    M3R_REQUIRE(img1 && img2 && h1 > 0 && w1 > 0 && h2 > 0 && w2 > 0, "infer_any: bad image");
+    const auto t0 = std::chrono::steady_clock::now();
+    float st[5] = {0, 0, 0, 0, 0}, h2d = 0, d2h = 0;
+    devs_[0]->infer_any(img1, h1, w1, img2, h2, w2, outs, st, &h2d, &d2h);
+    for (size_t i = 1; i < devs_.size(); ++i) devs_[i]->staged = 0;
+    staged_pairs_ = 1;
     if (timing) {
         timing[M3R_T_PREPROCESS] = st[0];
         timing[M3R_T_ENCODER] = st[1];

@@ -73,6 +73,9 @@ public:
     void load(const std::string& path);
     bool ready() const { return ready_; }
     void infer(const uint8_t* img1, const uint8_t* img2, int n_pairs, float* const outs[6], float* timing);
+    // one pair of images of any size, resized and centre-cropped on device 0
+    void infer_any(const uint8_t* img1, int h1, int w1, const uint8_t* img2, int h2, int w2, float* const outs[6],
+                   float* timing);
     void stage(const uint8_t* img1, const uint8_t* img2, int n_pairs);
     float run_resident(int n_pairs, float* stage_ms);
     void fetch(int n_pairs, float* const outs[6]);

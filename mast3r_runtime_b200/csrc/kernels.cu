@@ -269,6 +269,45 @@ __global__ void im2col_s2_kernel(const uint16_t* __restrict__ x, int n, int h, i
     }
 }
 
+// Resize + centre crop of a uint8 RGB image to the model size, bit-exact with the
+// reference's CPU preprocessing (csrc/cpu/preprocessing.cpp:29-63, 84-129): scale =
+// max(dh / sh, dw / sw), new = (int)(s * scale), bilinear resize to new (src = d * s / new,
+// truncated, clamped neighbours), crop [(new - d) / 2, +d); every multiply and add
+// separately rounded, the weighted sum clamped to [0, 255] and truncated.  Rows / columns
+// the reference would read past its resized buffer (new < d after truncation) are
+// clamped to the last one.  One thread per output pixel.
+__global__ void resize_crop_kernel(const uint8_t* __restrict__ src, int sh, int sw, uint8_t* __restrict__ dst, int dh,
+                                   int dw, int new_h, int new_w, float scale_y, float scale_x) {
+    const long long total = static_cast<long long>(dh) * dw;
+    const int start_h = (new_h - dh) / 2, start_w = (new_w - dw) / 2;
+    for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
+         e += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int x = static_cast<int>(e % dw), y = static_cast<int>(e / dw);
+        const int ry = min(start_h + y, new_h - 1), rx = min(start_w + x, new_w - 1);
+        const float syf = __fmul_rn(static_cast<float>(ry), scale_y);
+        const float sxf = __fmul_rn(static_cast<float>(rx), scale_x);
+        const int y0 = static_cast<int>(syf), x0 = static_cast<int>(sxf);
+        const int y1 = min(y0 + 1, sh - 1), x1 = min(x0 + 1, sw - 1);
+        const float fy = __fsub_rn(syf, static_cast<float>(y0)), fx = __fsub_rn(sxf, static_cast<float>(x0));
+        const float gy = __fsub_rn(1.0f, fy), gx = __fsub_rn(1.0f, fx);
+        const float w00 = __fmul_rn(gx, gy), w01 = __fmul_rn(fx, gy), w10 = __fmul_rn(gx, fy), w11 = __fmul_rn(fx, fy);
+        const uint8_t* p00 = src + (static_cast<long long>(y0) * sw + x0) * 3;
+        const uint8_t* p01 = src + (static_cast<long long>(y0) * sw + x1) * 3;
+        const uint8_t* p10 = src + (static_cast<long long>(y1) * sw + x0) * 3;
+        const uint8_t* p11 = src + (static_cast<long long>(y1) * sw + x1) * 3;
+        uint8_t* o = dst + e * 3;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            float v = __fmul_rn(w00, static_cast<float>(p00[c]));
+            v = __fadd_rn(v, __fmul_rn(w01, static_cast<float>(p01[c])));
+            v = __fadd_rn(v, __fmul_rn(w10, static_cast<float>(p10[c])));
+            v = __fadd_rn(v, __fmul_rn(w11, static_cast<float>(p11[c])));
+            v = fminf(fmaxf(v, 0.0f), 255.0f);
+            o[c] = static_cast<uint8_t>(v);
+        }
+    }
+}
+
 // Source rows / columns of output index i under the reference CPU head's bilinear
 // resize (backends/python/dpt_head.py:72-116): src = i * in / out (no half-pixel
 // offset), i0 = floor(src), i1 = min(i0 + 1, in - 1), f = src - i0; the rational src
@@ -430,6 +469,22 @@ void im2col_s2(cudaStream_t s, const void* x, int n, int h, int w, int C, void* 
     const long long total = static_cast<long long>(n) * ho * wo * 9 * (C / 8);
     im2col_s2_kernel<<<grid_for(total, 256), 256, 0, s>>>(static_cast<const uint16_t*>(x), n, h, w, C,
                                                           static_cast<uint16_t*>(out));
+    M3R_CUDA(cudaGetLastError());
+}
+
+void resize_crop(cudaStream_t s, const uint8_t* src, int sh, int sw, uint8_t* dst, int dh, int dw) {
+    M3R_REQUIRE(sh > 0 && sw > 0 && dh > 0 && dw > 0, "resize_crop: bad size");
+    // host side of preprocessing.cpp:34-41 (float arithmetic, as the reference)
+    const float sc_h = static_cast<float>(dh) / static_cast<float>(sh);
+    const float sc_w = static_cast<float>(dw) / static_cast<float>(sw);
+    const float scale = sc_h > sc_w ? sc_h : sc_w;
+    const int new_h = static_cast<int>(static_cast<float>(sh) * scale);
+    const int new_w = static_cast<int>(static_cast<float>(sw) * scale);
+    M3R_REQUIRE(new_h > 0 && new_w > 0, "resize_crop: degenerate resize");
+    const float scale_y = static_cast<float>(sh) / static_cast<float>(new_h);
+    const float scale_x = static_cast<float>(sw) / static_cast<float>(new_w);
+    const long long total = static_cast<long long>(dh) * dw;
+    resize_crop_kernel<<<grid_for(total, 256), 256, 0, s>>>(src, sh, sw, dst, dh, dw, new_h, new_w, scale_y, scale_x);
     M3R_CUDA(cudaGetLastError());
 }
 

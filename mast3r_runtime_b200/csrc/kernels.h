@@ -34,6 +34,10 @@ void im2col_s2(cudaStream_t s, const void* x, int n, int h, int w, int C, void* 
 // (half-pixel) when (h4, w4) != (H, W).
 void head_split(cudaStream_t s, const float* out4, int n, int h4, int w4, int H, int W, float* pts3d, float* conf);
 
+// Resize + centre crop of a uint8 [sh, sw, 3] image to [dh, dw, 3], bit-exact with the
+// reference's CPU preprocessing (csrc/cpu/preprocessing.cpp:29-63, 84-129).
+void resize_crop(cudaStream_t s, const uint8_t* src, int sh, int sw, uint8_t* dst, int dh, int dw);
+
 // The reference CPU head's bilinear resize (backends/python/dpt_head.py:72-116: src = i *
 // in / out, no half-pixel offset) of fp32 NHWC maps: [n, hi, wi, C] -> [n, ho, wo, C]
 // (C % 4 == 0), and of the 4-channel head output into pts3d [n, ho, wo, 3] + conf [n, ho, wo].

@@ -66,6 +66,11 @@ def lib() -> ctypes.CDLL:
         L.oracle_attention.argtypes = [_f32p, _f32p, _f32p, _f32p, ctypes.c_int64, ctypes.c_int,
                                        ctypes.c_int, ctypes.c_int, ctypes.c_float]
         L.oracle_attention.restype = None
+        _u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+        L.oracle_resize_crop.argtypes = [_u8p, ctypes.c_int, ctypes.c_int, _u8p, ctypes.c_int, ctypes.c_int]
+        L.oracle_resize_crop.restype = None
+        L.oracle_normalize_chw.argtypes = [_u8p, ctypes.c_int, ctypes.c_int, _f32p]
+        L.oracle_normalize_chw.restype = None
         _LIB = L
     return _LIB
 
@@ -86,6 +91,9 @@ def ref_lib() -> ctypes.CDLL | None:
                                                 ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
                                                 _i64p, _i64p, _f32p, _f32p, _f32p]
         L.ref_reciprocal_match_conf.restype = ctypes.c_int64
+        L.ref_preprocess.argtypes = [np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS"), ctypes.c_int,
+                                     ctypes.c_int, ctypes.c_int, _f32p]
+        L.ref_preprocess.restype = None
         L.ref_normalize.argtypes = [_f32p, ctypes.c_int, ctypes.c_int]
         L.ref_normalize.restype = None
         L.ref_multi_head_attention.argtypes = [_f32p, _f32p, _f32p, _f32p, ctypes.c_int,
@@ -211,6 +219,34 @@ def ref_match(desc_1: np.ndarray, desc_2: np.ndarray, top_k: int = 512, reciproc
         "idx_1": idx1[:m].copy(), "idx_2": idx2[:m].copy(), "confidence": conf[:m].copy(),
         "pts2d_1": p1[: 2 * m].reshape(m, 2).copy(), "pts2d_2": p2[: 2 * m].reshape(m, 2).copy(),
     }
+
+
+def resize_crop(img: np.ndarray, out_hw) -> np.ndarray:
+    """Restated resize + centre crop of csrc/cpu/preprocessing.cpp:29-63, 84-129 (uint8
+    [h, w, 3] -> uint8 [H, W, 3]; the reference's target is square, H == W)."""
+    src = np.ascontiguousarray(img, np.uint8)
+    out = np.zeros((int(out_hw[0]), int(out_hw[1]), 3), np.uint8)
+    lib().oracle_resize_crop(src, src.shape[0], src.shape[1], out, out.shape[0], out.shape[1])
+    return out
+
+
+def normalize_chw(img: np.ndarray) -> np.ndarray:
+    """preprocessing.cpp:65-82: (v / 255 - mean) / std, [h, w, 3] uint8 -> [3, h, w] float32."""
+    src = np.ascontiguousarray(img, np.uint8)
+    out = np.zeros((3, src.shape[0], src.shape[1]), np.float32)
+    lib().oracle_normalize_chw(src, src.shape[0], src.shape[1], out)
+    return out
+
+
+def ref_preprocess(img: np.ndarray, res: int):
+    """The reference's own Preprocessor(res).process (oracle/_ref), or None when unavailable."""
+    L = ref_lib()
+    if L is None:
+        return None
+    src = np.ascontiguousarray(img, np.uint8)
+    out = np.zeros((3, res, res), np.float32)
+    L.ref_preprocess(src, src.shape[0], src.shape[1], res, out)
+    return out
 
 
 def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float) -> np.ndarray:

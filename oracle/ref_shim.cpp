@@ -9,9 +9,11 @@
 //                                 the confidence maps, :110-119)
 //   csrc/cpu/matching.cpp:22      mast3r::cpu::normalize_descriptors
 //   csrc/cpu/attention.cpp:118    mast3r::cpu::multi_head_attention
+// and uses the reference's own Preprocessor class (csrc/cpu/preprocessing.hpp).
 #include <cstdint>
 #include <cstring>
 #include "common/types.hpp"
+#include "cpu/preprocessing.hpp"
 
 namespace mast3r {
 namespace cpu {
@@ -71,6 +73,17 @@ int64_t ref_reciprocal_match_conf(const float* d1, const float* d2, const float*
 }
 
 void ref_normalize(float* desc, int n, int d) { mast3r::cpu::normalize_descriptors(desc, n, d); }
+
+// Preprocessor(res).process: resize + centre crop to res x res, normalise, CHW float.
+void ref_preprocess(const uint8_t* img, int h, int w, int res, float* out_chw) {
+    mast3r::cpu::Preprocessor p(res);
+    mast3r::ImageView v;
+    v.data = img;
+    v.height = h;
+    v.width = w;
+    v.channels = 3;
+    p.process(v, out_chw);
+}
 
 void ref_multi_head_attention(const float* q, const float* k, const float* v, float* o,
                               int b, int h, int n, int d) {

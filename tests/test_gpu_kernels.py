@@ -262,3 +262,19 @@ def test_match_kats_gpu(matcher_engine):
     assert len(matcher_engine.match(empty, empty).idx_1) == 0
     one = rng.random((1, 1, 64)).astype(np.float32)
     assert len(matcher_engine.match(one, one).idx_1) <= 1
+
+
+# ---------------------------------------------------------------------------- preprocessing
+@pytest.mark.parametrize("h,w,oh,ow", [(300, 200, 224, 224), (336, 336, 336, 336), (1024, 768, 512, 512),
+                                       (97, 131, 64, 64), (640, 360, 336, 336), (480, 640, 384, 512),
+                                       (768, 1024, 384, 512), (50, 70, 64, 96)])
+def test_resize_crop_bit_exact_vs_oracle(lib, oracle_lib, h, w, oh, ow):
+    """Resize + centre crop of csrc/cpu/preprocessing.cpp (the oracle's restatement is pinned
+    to the reference's own C++ by tests/test_oracle.py), bit for bit, including upscaling
+    and rectangular model sizes."""
+    from mast3r_runtime_b200 import _lib
+
+    img = np.random.default_rng(h + w).integers(0, 256, (h, w, 3), dtype=np.uint8)
+    out = np.zeros((oh, ow, 3), np.uint8)
+    _lib.check(lib.m3r_resize_crop_test(0, P(img), h, w, P(out), oh, ow))
+    np.testing.assert_array_equal(out, oracle_lib.resize_crop(img, (oh, ow)))

@@ -245,3 +245,32 @@ def test_reference_cpu_head_matches_oracle(tmp_path, dims_name, hw):
         print(dims_name, v, e, ec, cos.mean(), cos.min())
         assert e <= 1e-2 and ec <= 1e-2
         assert cos.mean() >= 0.999
+
+
+def test_images_of_any_size_are_preprocessed_on_device(tmp_path):
+    """engine.infer with images of another size than the model's: resized and centre
+    cropped on the device exactly as the reference's C++ preprocessing (the oracle's
+    restatement), then the same forward pass as for pre-resized images."""
+    import oracle
+    from mast3r_runtime_b200 import CUDAEngine, NativeEngine, make_weights, save_safetensors
+    from mast3r_runtime_b200.weights import tiny_dims
+
+    d = tiny_dims()
+    path = save_safetensors(tmp_path / "u.safetensors", make_weights(d, seed=12, randomize_affine=True))
+    rng = np.random.default_rng(13)
+    big1 = rng.integers(0, 256, (120, 150, 3), dtype=np.uint8)
+    big2 = rng.integers(0, 256, (90, 200, 3), dtype=np.uint8)
+    eng = NativeEngine(d, (64, 96), [0], 1)
+    eng.load(str(path))
+    got, timing = eng.infer_any(big1, big2)
+    want, _ = eng.infer_batch(oracle.resize_crop(big1, (64, 96))[None], oracle.resize_crop(big2, (64, 96))[None])
+    for k in want:
+        np.testing.assert_array_equal(got[k], want[k])
+    assert timing["preprocess_ms"] > 0
+    eng.close()
+    ce = CUDAEngine.__new__(CUDAEngine)  # the drop-in object, sized like the engine above
+    CUDAEngine.__init__(ce, variant="dune_vit_small_336", image_size=(64, 96), devices=[0])
+    ce.dims = d
+    ce.load(str(path))
+    r = ce.infer(big1, big2)
+    np.testing.assert_array_equal(r.pts3d_1, want["pts3d_1"][0])

@@ -205,6 +205,31 @@ def test_matcher_pts3d_gather_as_numpy_path(oracle_lib):
     assert not z["pts3d_1"].any()
 
 
+def _resized_dims(h, w, res):
+    sc = max(np.float32(res) / np.float32(h), np.float32(res) / np.float32(w))
+    return int(np.float32(h) * sc), int(np.float32(w) * sc)
+
+
+@pytest.mark.parametrize("h,w,res", [(480, 640, 336), (300, 200, 224), (336, 336, 336), (1024, 768, 512),
+                                     (97, 131, 64), (640, 360, 336)])
+def test_preprocess_matches_reference_cpp(oracle_lib, h, w, res):
+    """Resize + centre crop + normalise (csrc/cpu/preprocessing.cpp) bit for bit."""
+    if oracle_lib.ref_lib() is None:
+        pytest.skip("oracle/_ref not built (reference tree absent)")
+    nh, nw = _resized_dims(h, w, res)
+    if nh < res or nw < res:
+        pytest.skip("the reference reads past its resized buffer here (truncated size below the target)")
+    img = np.random.default_rng(h * w).integers(0, 256, (h, w, 3), dtype=np.uint8)
+    got = oracle_lib.normalize_chw(oracle_lib.resize_crop(img, (res, res)))
+    want = oracle_lib.ref_preprocess(img, res)
+    assert got.tobytes() == want.tobytes()
+
+
+def test_preprocess_identity_at_model_size(oracle_lib):
+    img = np.random.default_rng(1).integers(0, 256, (64, 96, 3), dtype=np.uint8)
+    np.testing.assert_array_equal(oracle_lib.resize_crop(img, (64, 96)), img)
+
+
 def test_matcher_kats(oracle_lib):
     # tests/unit/test_matching.py:27-35: [3, 4] -> [0.6, 0.8]
     n = oracle_lib.normalize(np.array([[3.0, 4.0], [1.0, 0.0]], np.float32))
