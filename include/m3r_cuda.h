@@ -130,6 +130,16 @@ int m3r_infer_any(m3r_engine* engine, const uint8_t* img1, int h1, int w1, const
                   float* pts3d_1, float* pts3d_2, float* desc_1, float* desc_2, float* conf_1, float* conf_2,
                   float* timing_ms);
 
+/* ---- retrieval: replaces MPSGraphEngine::load_retrieval / encode_retrieval
+ * (csrc/mps/mpsgraph_engine.mm:758-1117, Metal only).  load: a safetensors file with
+ * prewhiten.m [enc_dim] and prewhiten.p [enc_dim, enc_dim], after m3r_load (the encoder
+ * weights are shared).  encode: images [n_images, H, W, 3] uint8 of the model size ->
+ * features [n_images, N, enc_dim] = (encoder output - m) P and attention [n_images, N] =
+ * ||feature row||^2 / (sum of them + 1e-8), fp32 (N = patch tokens). */
+int m3r_load_retrieval(m3r_engine* engine, const char* safetensors_path);
+int m3r_encode_retrieval(m3r_engine* engine, const uint8_t* images, int n_images, float* features, float* attention,
+                         float* timing_ms);
+
 /* ---- match(desc_1, desc_2, top_k, reciprocal, confidence_threshold): replaces
  * native.match (native_wrapper.py:122-128) with the semantics of
  * csrc/cpu/matching.cpp:85-237.  desc_*: [height*width, desc_dim] fp32.

@@ -190,6 +190,29 @@ class NativeEngine:
         _lib.check(rc, self.h)
         return o, dict(zip(_lib.TIMING_KEYS, map(float, t)))
 
+    def load_retrieval(self, path: str) -> None:
+        """Whitening weights (prewhiten.m, prewhiten.p) of the retrieval head
+        (csrc/mps/mpsgraph_engine.mm:758-787); the encoder weights are the loaded model's."""
+        _lib.check(self.lib.m3r_load_retrieval(self.h, str(path).encode()), self.h)
+
+    def encode_retrieval(self, images):
+        """[n, H, W, 3] (or [H, W, 3]) uint8 images of the model size -> (features
+        [n, N, enc_dim], attention [n, N]) fp32: the encoder output whitened as (x - m) P and
+        the per-token L2 weights (mpsgraph_engine.mm:1030-1117)."""
+        imgs = np.ascontiguousarray(images, dtype=np.uint8)
+        if imgs.ndim == 3:
+            imgs = imgs[None]
+        if imgs.ndim != 4 or tuple(imgs.shape[1:]) != (*self.image_hw, 3):
+            raise ValueError(f"Expected [N, {self.image_hw[0]}, {self.image_hw[1]}, 3] uint8 images, got {imgs.shape}")
+        n = imgs.shape[0]
+        ntok = (self.image_hw[0] // self.dims.patch) * (self.image_hw[1] // self.dims.patch)
+        feats = np.empty((n, ntok, self.dims.enc_dim), np.float32)
+        attn = np.empty((n, ntok), np.float32)
+        t = np.zeros(len(_lib.TIMING_KEYS), np.float32)
+        _lib.check(self.lib.m3r_encode_retrieval(self.h, _lib.ptr(imgs), n, _lib.ptr(feats), _lib.ptr(attn),
+                                                 _lib.ptr(t)), self.h)
+        return feats, attn
+
     # device-resident stages (throughput measurement)
     def stage(self, img1, img2):
         img1, img2 = self._check_images(img1, img2)
@@ -390,6 +413,25 @@ class CUDAEngine:
         r.timing["match_ms"] = (time.perf_counter() - t0) * 1000.0
         return r
 
+    # --- retrieval (MPSGraphEngine::load_retrieval / encode_retrieval, mpsgraph_engine.mm:758-1117)
+    def load_retrieval(self, path: str) -> None:
+        self._retrieval_path = str(path)
+        self._engine(self.image_hw, 1).load_retrieval(self._retrieval_path)
+
+    def encode_retrieval(self, img):
+        """One image -> SimpleNamespace(features [N, enc_dim], attention [N], num_patches,
+        feature_dim) (the fields of the reference's RetrievalResult); other sizes are
+        resized and centre-cropped first, as for infer."""
+        img = np.asarray(img)
+        if tuple(img.shape[:2]) != self.image_hw:
+            raise RuntimeError(f"encode_retrieval takes {self.image_hw} images (resize them first)")
+        eng = self._engine(self.image_hw, 1)
+        if getattr(self, "_retrieval_path", None) is None:
+            raise RuntimeError("retrieval weights are not loaded (call load_retrieval(path) first)")
+        feats, attn = eng.encode_retrieval(img)
+        return SimpleNamespace(features=feats[0], attention=attn[0], num_patches=feats.shape[1],
+                               feature_dim=feats.shape[2])
+
     # --- internals
     def _engine(self, hw, max_pairs: int) -> NativeEngine:
         if self._path is None:
@@ -402,6 +444,8 @@ class CUDAEngine:
                 self._engines.pop(k).close()
             eng = NativeEngine(self.dims, hw, self.devices, max_pairs, self.dtype, self.head)
             eng.load(self._path)
+            if getattr(self, "_retrieval_path", None):
+                eng.load_retrieval(self._retrieval_path)
             self._engines[key] = eng
         return eng
 

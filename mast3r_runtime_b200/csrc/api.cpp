@@ -178,6 +178,20 @@ int m3r_infer_any(m3r_engine* engine, const uint8_t* img1, int h1, int w1, const
     });
 }
 
+int m3r_load_retrieval(m3r_engine* engine, const char* path) {
+    if (!engine) return M3R_ERR_ARG;
+    return guarded(engine, [&] {
+        M3R_REQUIRE(path != nullptr, "path is null");
+        engine->impl->load_retrieval(path);
+    });
+}
+
+int m3r_encode_retrieval(m3r_engine* engine, const uint8_t* images, int n_images, float* features, float* attention,
+                         float* timing_ms) {
+    if (!engine) return M3R_ERR_ARG;
+    return guarded(engine, [&] { engine->impl->encode_retrieval(images, n_images, features, attention, timing_ms); });
+}
+
 int m3r_resize_crop_test(int device, const uint8_t* src, int h, int w, uint8_t* dst, int out_h, int out_w) {
     return guarded(nullptr, [&] {
         M3R_REQUIRE(src && dst && h > 0 && w > 0 && out_h > 0 && out_w > 0, "resize_crop_test: bad arguments");

@@ -228,6 +228,8 @@ public:
     Head head[2];
     float* rope_cos = nullptr;
     float* rope_sin = nullptr;
+    Lin whiten;               // retrieval whitening: W = P^T [D, D], bias = -(m P) (Engine::load_retrieval)
+    float* rattn = nullptr;   // retrieval attention weights [2 * max_pairs * N]
 
     // ------------------------------------------------------------ activations
     uint8_t* img = nullptr;
@@ -270,6 +272,7 @@ public:
         hook1 = bf(T * d_.dec_dim);
         hook2 = bf(T * d_.dec_dim);
         dec_out = bf(T * d_.dec_dim);
+        rattn = f32(T);
         lf1 = bf(Tv * d_.lf_hidden);
         o_pts = f32(2 * P * d_.H * d_.W * 3);
         o_conf = f32(2 * P * d_.H * d_.W);
@@ -860,6 +863,38 @@ public:
         }
     }
 
+    // Retrieval features of k <= 2 * max_pairs images of the model size (encode_retrieval,
+    // mpsgraph_engine.mm:1030-1117): the images fill the input slots as view 1 / view 2 of
+    // n = ceil(k / 2) pairs (an odd last slot repeats image 0), the patch and encoder stages
+    // run over all 2n, then the whitening GEMM (enc_out P + bias, fp32 into the encoder's
+    // residual buffer) and the attention weights.  feats [k, N, D], attn [k, N] (host).
+    void encode_retrieval(const uint8_t* imgs, int k, float* feats, float* attn) {
+        DeviceGuard g(dev_);
+        M3R_REQUIRE(k >= 1 && k <= 2 * max_pairs_, "encode_retrieval: image count out of range for this device");
+        M3R_REQUIRE(whiten.w != nullptr, "retrieval weights are not loaded (m3r_load_retrieval)");
+        const int n = (k + 1) / 2;
+        const size_t ib = static_cast<size_t>(d_.H) * d_.W * 3;
+        for (int i = 0; i < 2 * n; ++i) {
+            const int src = i < k ? i : 0;
+            M3R_CUDA(cudaMemcpyAsync(img_slot(i / n, i % n), imgs + src * ib, ib, cudaMemcpyHostToDevice, stream_));
+        }
+        const bool prof = profiling;
+        profiling = false;
+        const long long N = d_.ntok, T = 2LL * n * N;
+        const int D = d_.enc_dim;
+        enqueue_stage(0, n, 0);
+        enqueue_stage(1, n, 0);
+        linear("ret.whiten", enc_out, T, whiten, EPI_F32, xenc, D);
+        retrieval_attention(stream_, xenc, 2 * n, static_cast<int>(N), D, rattn);
+        profiling = prof;
+        // image i is sequence i of the launch (view 1 slots 0..n-1, then view 2)
+        M3R_CUDA(cudaMemcpyAsync(feats, xenc, sizeof(float) * k * N * D, cudaMemcpyDeviceToHost, stream_));
+        M3R_CUDA(cudaMemcpyAsync(attn, rattn, sizeof(float) * k * N, cudaMemcpyDeviceToHost, stream_));
+        M3R_CUDA(cudaStreamSynchronize(stream_));
+        staged = 0;
+        check_error();
+    }
+
     // One pair of images of any size: resize + centre crop on the device to the model
     // size (the reference's preprocessing), then the forward pass (slot 0).
     void infer_any(const uint8_t* img1, int h1, int w1, const uint8_t* img2, int h2, int w2, float* const outs[6],
@@ -1416,6 +1451,50 @@ void Engine::infer(const uint8_t* img1, const uint8_t* img2, int n_pairs, float*
         timing[M3R_T_H2D] = h2d;
         timing[M3R_T_D2H] = d2h;
         timing[M3R_T_INFERENCE] = st[4];
+        timing[M3R_T_TOTAL] =
+            static_cast<float>(std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count());
+    }
+}
+
+void Engine::load_retrieval(const std::string& path) {
+    if (!ready_) throw Error(kErrState, "load the model before the retrieval weights");
+    SafetensorsFile f(path);
+    const int D = d_.enc_dim;
+    const std::vector<float> m = f.load_f32("prewhiten.m", {D});
+    const std::vector<float> P = f.load_f32("prewhiten.p", {D, D});
+    // (x - m) P = x P - m P: the GEMM's weight is P^T ([out, in]) and its bias -(m P)
+    std::vector<float> wt(static_cast<size_t>(D) * D), bias(D);
+    for (int j = 0; j < D; ++j) {
+        double acc = 0.0;
+        for (int i = 0; i < D; ++i) {
+            wt[static_cast<size_t>(j) * D + i] = P[static_cast<size_t>(i) * D + j];
+            acc += static_cast<double>(m[i]) * P[static_cast<size_t>(i) * D + j];
+        }
+        bias[j] = static_cast<float>(-acc);
+    }
+    const HostLin h = to16(d_.dt, wt, D, D, bias);
+    for (auto& dp : devs_) {
+        DeviceGuard g(dp->dev());
+        dp->whiten = dp->upload(h);
+        M3R_CUDA(cudaDeviceSynchronize());
+    }
+    retrieval_ready_ = true;
+}
+
+void Engine::encode_retrieval(const uint8_t* imgs, int k, float* feats, float* attn, float* timing) {
+    if (!ready_ || !retrieval_ready_) throw Error(kErrState, "retrieval weights are not loaded");
+    M3R_REQUIRE(imgs && feats && attn && k >= 1, "encode_retrieval: bad arguments");
+    const auto t0 = std::chrono::steady_clock::now();
+    const size_t ib = static_cast<size_t>(d_.H) * d_.W * 3;
+    const size_t fb = static_cast<size_t>(d_.ntok) * d_.enc_dim;
+    const int per = 2 * cfg_.max_pairs;
+    for (int first = 0; first < k; first += per) {
+        const int c = std::min(per, k - first);
+        devs_[0]->encode_retrieval(imgs + first * ib, c, feats + first * fb, attn + static_cast<size_t>(first) * d_.ntok);
+    }
+    staged_pairs_ = 0;
+    if (timing) {
+        for (int i = 0; i < M3R_T_COUNT; ++i) timing[i] = 0.0f;
         timing[M3R_T_TOTAL] =
             static_cast<float>(std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count());
     }

@@ -77,6 +77,9 @@ public:
     void infer_any(const uint8_t* img1, int h1, int w1, const uint8_t* img2, int h2, int w2, float* const outs[6],
                    float* timing);
     void stage(const uint8_t* img1, const uint8_t* img2, int n_pairs);
+    // retrieval: whitening weights, then features + attention weights of k images
+    void load_retrieval(const std::string& path);
+    void encode_retrieval(const uint8_t* imgs, int k, float* feats, float* attn, float* timing);
     float run_resident(int n_pairs, float* stage_ms);
     void fetch(int n_pairs, float* const outs[6]);
     int match(const float* d1, const float* d2, int h, int w, int d, int top_k, int reciprocal, float thr,
@@ -101,6 +104,7 @@ private:
     std::vector<std::unique_ptr<Device>> devs_;
     std::vector<void*> nccl_comms_;  // ncclComm_t per device, created on the first multi-device match
     bool ready_ = false;
+    bool retrieval_ready_ = false;
     bool profiling_ = false;
     int staged_pairs_ = 0;
 };

@@ -308,6 +308,38 @@ __global__ void resize_crop_kernel(const uint8_t* __restrict__ src, int sh, int 
     }
 }
 
+// Retrieval attention weights (csrc/mps/mpsgraph_engine.mm:843-850): per image of N
+// whitened tokens w [N, D], a[r] = ||w_r||^2 / (sum_r ||w_r||^2 + 1e-8).  One block per
+// image; a warp per row for the squared norms, then a block sum.
+__global__ void retrieval_attention_kernel(const float* __restrict__ w, int N, int D, float* __restrict__ attn) {
+    __shared__ float s_part[32];
+    __shared__ float s_total;
+    const int img = blockIdx.x;
+    const float* base = w + static_cast<long long>(img) * N * D;
+    float* a = attn + static_cast<long long>(img) * N;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    float local = 0.0f;
+    for (int r = warp; r < N; r += nw) {
+        const float* row = base + static_cast<long long>(r) * D;
+        float acc = 0.0f;
+        for (int c = lane; c < D; c += 32) acc += row[c] * row[c];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) a[r] = acc;
+        local += acc;
+    }
+    if (lane == 0) s_part[warp] = local;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int i = 0; i < nw; ++i) t += s_part[i];
+        s_total = t + 1e-8f;
+    }
+    __syncthreads();
+    const float inv_total = s_total;
+    for (int r = threadIdx.x; r < N; r += blockDim.x) a[r] = a[r] / inv_total;
+}
+
 // Source rows / columns of output index i under the reference CPU head's bilinear
 // resize (backends/python/dpt_head.py:72-116): src = i * in / out (no half-pixel
 // offset), i0 = floor(src), i1 = min(i0 + 1, in - 1), f = src - i0; the rational src
@@ -469,6 +501,12 @@ void im2col_s2(cudaStream_t s, const void* x, int n, int h, int w, int C, void* 
     const long long total = static_cast<long long>(n) * ho * wo * 9 * (C / 8);
     im2col_s2_kernel<<<grid_for(total, 256), 256, 0, s>>>(static_cast<const uint16_t*>(x), n, h, w, C,
                                                           static_cast<uint16_t*>(out));
+    M3R_CUDA(cudaGetLastError());
+}
+
+void retrieval_attention(cudaStream_t s, const float* w, int n_img, int N, int D, float* attn) {
+    if (n_img <= 0) return;
+    retrieval_attention_kernel<<<n_img, 512, 0, s>>>(w, N, D, attn);
     M3R_CUDA(cudaGetLastError());
 }
 

@@ -34,6 +34,10 @@ void im2col_s2(cudaStream_t s, const void* x, int n, int h, int w, int C, void* 
 // (half-pixel) when (h4, w4) != (H, W).
 void head_split(cudaStream_t s, const float* out4, int n, int h4, int w4, int H, int W, float* pts3d, float* conf);
 
+// Retrieval attention weights of n_img images of N whitened tokens [N, D] (fp32):
+// ||w_r||^2 / (sum_r ||w_r||^2 + 1e-8) (csrc/mps/mpsgraph_engine.mm:843-850).
+void retrieval_attention(cudaStream_t s, const float* w, int n_img, int N, int D, float* attn);
+
 // Resize + centre crop of a uint8 [sh, sw, 3] image to [dh, dw, 3], bit-exact with the
 // reference's CPU preprocessing (csrc/cpu/preprocessing.cpp:29-63, 84-129).
 void resize_crop(cudaStream_t s, const uint8_t* src, int sh, int sw, uint8_t* dst, int dh, int dw);

@@ -210,6 +210,16 @@ def make_weights(d: ModelDims, seed: int = 0, std: float = 0.02,
     return out
 
 
+def make_retrieval_weights(d: ModelDims, seed: int = 0) -> dict[str, np.ndarray]:
+    """Seeded whitening weights of a retrieval checkpoint (the reference's
+    retrieval.safetensors, csrc/mps/mpsgraph_engine.mm:770-787): prewhiten.m [enc_dim] (the
+    feature mean) and prewhiten.p [enc_dim, enc_dim] (the whitening projection)."""
+    rng = np.random.default_rng(seed)
+    e = d.enc_dim
+    return {"prewhiten.m": (0.1 * rng.standard_normal(e)).astype(np.float32),
+            "prewhiten.p": (rng.standard_normal((e, e)) / np.sqrt(e)).astype(np.float32)}
+
+
 def save_safetensors(path: str | Path, tensors: dict[str, np.ndarray]) -> Path:
     """Write ``tensors`` as an F32 safetensors file (the checkpoint format the loader reads)."""
     from safetensors.numpy import save_file

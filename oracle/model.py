@@ -20,6 +20,8 @@ measured against.  Every function cites the reference code it restates:
                     local features: MLP(enc || dec) -> pixel shuffle -> L2 norm)
   ref_simple head   backends/python/mast3r_model.py:86-156 with
                     backends/python/dpt_head.py:20-116 (the reference's own CPU head)
+  retrieval         csrc/mps/mpsgraph_engine.mm:767-850, 1030-1117 (encoder output whitened,
+                    L2 attention weights)
 
 The 24-d head has no runnable reference here (Metal only), so its parity is pinned
 only through the encoder/decoder fixtures; see the golden-vector script in
@@ -316,6 +318,16 @@ class Model:
         x = interpolate_bilinear_ref(x, *out_hw)
         desc = interpolate_bilinear_ref(raw[:, :256].reshape(hg, wg, 256), *out_hw)
         return x[..., :3], desc, x[..., 3]
+
+    def retrieval(self, img: np.ndarray, m: np.ndarray, p: np.ndarray):
+        """Retrieval features of one image (csrc/mps/mpsgraph_engine.mm:767-850, encode_retrieval
+        :1030-1117): the encoder output x [N, D] (after enc_norm) whitened as (x - m) @ P, and
+        the per-token weights ||w||^2 / (sum over tokens of ||w||^2 + 1e-8).  No runnable
+        reference exists for this (Metal only): restated from the graph source."""
+        x, _ = self.encode(preprocess(img))
+        w = (x - np.asarray(m, self.dt).reshape(1, -1)) @ np.asarray(p, self.dt)
+        sq = (w * w).sum(-1)
+        return w, sq / (sq.sum() + 1e-8)
 
     def forward(self, img1: np.ndarray, img2: np.ndarray, head: str = "mast3r24"):
         """Full pair: uint8 [H, W, 3] x2 -> dict of pts3d/conf/desc per view (float64)."""

@@ -274,3 +274,32 @@ def test_images_of_any_size_are_preprocessed_on_device(tmp_path):
     ce.load(str(path))
     r = ce.infer(big1, big2)
     np.testing.assert_array_equal(r.pts3d_1, want["pts3d_1"][0])
+
+
+def test_retrieval_features_match_oracle(tmp_path):
+    """Retrieval (MPSGraphEngine::encode_retrieval, mpsgraph_engine.mm:767-1117): encoder output
+    whitened as (x - m) P and the per-token L2 weights, for an odd number of images (the last
+    slot of the encoder pass repeats image 0), against the oracle's restatement."""
+    from mast3r_runtime_b200 import NativeEngine, make_weights, save_safetensors
+    from mast3r_runtime_b200.weights import make_retrieval_weights, tiny_dims
+    from oracle.model import Model
+
+    d = tiny_dims()
+    w = make_weights(d, seed=31, randomize_affine=True)
+    rw = make_retrieval_weights(d, seed=32)
+    path = save_safetensors(tmp_path / "unified.safetensors", w)
+    rpath = save_safetensors(tmp_path / "retrieval.safetensors", rw)
+    eng = NativeEngine(d, (64, 96), [0], 2)
+    eng.load(str(path))
+    with pytest.raises(RuntimeError):
+        eng.encode_retrieval(np.zeros((1, 64, 96, 3), np.uint8))  # weights not loaded yet
+    eng.load_retrieval(str(rpath))
+    imgs = np.random.default_rng(33).integers(0, 256, (3, 64, 96, 3), dtype=np.uint8)
+    feats, attn = eng.encode_retrieval(imgs)
+    eng.close()
+    m = Model(w, d)
+    for i in range(3):
+        fr, ar = m.retrieval(imgs[i], rw["prewhiten.m"], rw["prewhiten.p"])
+        assert rel_l2(feats[i], fr) < 1e-2, rel_l2(feats[i], fr)
+        assert rel_l2(attn[i], ar) < 1e-2
+        assert abs(float(attn[i].sum()) - 1.0) < 1e-4
