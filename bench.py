@@ -459,9 +459,10 @@ def run_ours(args):
         # the call the drop-in engine makes: ordinary numpy images in, outputs from the
         # engine's recycled page-locked buffers (the previous step's are released first)
         del outs
+        res, _ = eng.infer_batch(img1, img2)  # the pool's first set is allocated (and pinned) here
+        res = None
         barrier()
         t0 = time.perf_counter()
-        res = None
         for _ in range(max(1, args.steps // 2)):
             res = None
             res, _ = eng.infer_batch(img1, img2)

@@ -843,10 +843,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const StoreMaps maps{{&mapC0, &mapC1, &mapC2}};
         uint4 pre[8];  // EPI_F32_RESID: residual block of the next unit, fetched ahead
         uint32_t tcount = 0, h4count = 0;
+        // EPI_F32_RESID: the first column group's warps bulk-prefetch into L2 the residual
+        // rows (one row per lane, the tile's whole width) of the tile after the one they
+        // are about to process, so the register fetches of the epilogue hit L2
+        auto prefetch_resid = [&](int tt) {
+            if (EPI != EPI_F32_RESID || grp != 0 || tt >= num_tiles) return;
+            const TileGeom gn = tile_geom<AMODE, CG>(p, tt, rank);
+            if (!gn.live) return;
+            long long grow;
+            bool valid;
+            tile_row<AMODE>(p, gn, r, grow, valid);
+            const int col0 = gn.n_idx * BN;
+            const int cols = p.N - col0 < BN ? p.N - col0 : BN;
+            const char* src = reinterpret_cast<const char*>(p.resid + grow * p.ldr + col0);
+            if (valid && cols > 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0 && (cols * 4) % 16 == 0)
+                prefetch_l2_bulk(src, static_cast<uint32_t>(cols * 4));
+        };
+        prefetch_resid(unit);
         for (int t = unit; t < num_tiles; t += num_units, ++tcount) {
             const uint32_t buf = tcount & 1;
             const uint32_t tph = (tcount >> 1) & 1;
             const TileGeom g = tile_geom<AMODE, CG>(p, t, rank);
+            prefetch_resid(t + num_units);
             if (EPI == EPI_F32_RESID && g.live) {
                 // the residual does not depend on the accumulator: fetch before waiting for it
                 long long grow;

@@ -105,6 +105,10 @@ constexpr int kTI = 128;  // rows per CTA tile
 constexpr int kTJ = 128;  // columns per j-tile
 constexpr int kKC = 32;   // k chunk held in shared memory
 constexpr int kPitch = 128 + 4;
+#ifndef M3R_ARGMAX_UNROLL
+#define M3R_ARGMAX_UNROLL 4
+#endif
+constexpr int kArgmaxUnroll = M3R_ARGMAX_UNROLL;
 
 // Thread (tr, tc) of a 16 x 16 grid owns rows tr*8 .. +8 and columns
 // {tc*4 .. +4} U {64 + tc*4 .. +4} of the 128 x 128 tile.  Warp w holds
@@ -141,6 +145,10 @@ __global__ void __launch_bounds__(256, 2)
     }
 
     const bool a_resident = D <= kKC;
+    // rows of this thread that exist (fixed for the CTA)
+    bool rv[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) rv[r] = i0 + tr * 8 + r < row1;
     // confidence weighting (matching.cpp:110-119): sim * (conf_1[i] * conf_2[j]); the
     // row confidences of this thread's 8 rows stay in registers
     const bool weighted = C1 != nullptr && C2 != nullptr;
@@ -178,7 +186,9 @@ __global__ void __launch_bounds__(256, 2)
             }
             __syncthreads();
             const int KN = DFIX > 0 ? (DFIX < kKC ? DFIX : kKC) : kKC;
-#pragma unroll
+            // a partial unroll keeps the loop body inside the instruction cache (a full
+            // unroll of 24 steps of 128 multiply / add instructions stalled on fetch)
+#pragma unroll kArgmaxUnroll
             for (int k = 0; k < KN; ++k) {
                 if (DFIX == 0 && k >= kn) break;
                 const float4 a0 = *reinterpret_cast<const float4*>(&sA[k][tr * 8]);
@@ -194,11 +204,16 @@ __global__ void __launch_bounds__(256, 2)
             }
         }
 
+        // columns of this thread that exist in this tile (32-bit offsets within the tile)
+        const long long jleft = n2 - j0;
+        bool cv[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) cv[c] = (c < 4 ? tc * 4 + c : 64 + tc * 4 + c - 4) < jleft;
         if (weighted) {
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
                 const long long j = j0 + (c < 4 ? tc * 4 + c : 64 + tc * 4 + c - 4);
-                const float cc = j < n2 ? C2[j] : 1.0f;
+                const float cc = cv[c] ? C2[j] : 1.0f;
 #pragma unroll
                 for (int r = 0; r < 8; ++r) s[r][c] = __fmul_rn(s[r][c], __fmul_rn(cr[r], cc));
             }
@@ -215,11 +230,10 @@ __global__ void __launch_bounds__(256, 2)
             int mc = -1;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
-                const long long j = j0 + (c < 4 ? tc * 4 + c : 64 + tc * 4 + c - 4);
                 if (c == 0 && seed_col0) {
                     m = s[r][0];
                     mc = 0;
-                } else if (j < n2 && s[r][c] > m) {
+                } else if (cv[c] && s[r][c] > m) {
                     m = s[r][c];
                     mc = c;
                 }
@@ -243,7 +257,7 @@ __global__ void __launch_bounds__(256, 2)
                 if (r == 0 && seed_row0) {
                     m = s[0][c];
                     mr = 0;
-                } else if (i0 + tr * 8 + r < row1 && s[r][c] > m) {
+                } else if (rv[r] && s[r][c] > m) {
                     m = s[r][c];
                     mr = r;
                 }

@@ -268,9 +268,8 @@ def test_images_of_any_size_are_preprocessed_on_device(tmp_path):
         np.testing.assert_array_equal(got[k], want[k])
     assert timing["preprocess_ms"] > 0
     eng.close()
-    ce = CUDAEngine.__new__(CUDAEngine)  # the drop-in object, sized like the engine above
-    CUDAEngine.__init__(ce, variant="dune_vit_small_336", image_size=(64, 96), devices=[0])
-    ce.dims = d
+    ce = CUDAEngine(variant="mast3r_vit_large", image_size=(64, 96), devices=[0])  # patch 16, as tiny_dims
+    ce.dims = d  # the drop-in object with the tiny model's dimensions
     ce.load(str(path))
     r = ce.infer(big1, big2)
     np.testing.assert_array_equal(r.pts3d_1, want["pts3d_1"][0])
