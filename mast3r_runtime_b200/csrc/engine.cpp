@@ -577,28 +577,42 @@ public:
         // normalised projected encoder output of both views (norm_y's affine part lives
         // in the K/V projection weights)
         ln("dec.ln", encp, T, Dd, unit_norm, yn);
+        // The two views' blocks are independent within a block (the cross attention reads
+        // the other view's projected encoder output, constant over blocks), so each
+        // attention runs once over both views' 2n sequences; the projections and MLPs
+        // keep their per-view weights (dec_blocks / dec_blocks2).  View v's sequences,
+        // tokens and head-major Q/K/V planes start at v * Tv rows.
+        auto xv = [&](int view) { return xdec + view * Tv * Dd; };
+        auto xnv = [&](int view) { return xn + view * Tv * Dd; };
+        auto aov = [&](int view) { return ao + view * Tv * Dd; };
+        auto qv = [&](uint16_t* base, int view) { return base + view * Tv * Dd; };
         for (int i = 0; i < d.dec_depth; ++i) {
+            // self attention
             for (int view = 0; view < 2; ++view) {
                 const DecBlock& B = dec[view][i];
-                float* xv = xdec + view * Tv * Dd;
+                ln("dec.ln", xv(view), Tv, Dd, B.n1, xnv(view));
+                linear_heads("dec.qkv", xnv(view), Tv, B.qkv, Dd, qv(q, view), 1, qv(k, view), 1, qv(v, view), 0);
+            }
+            attn("dec.attn_self", q, k, v, ao, 2 * n, d.dec_heads);
+            for (int view = 0; view < 2; ++view)
+                linear("dec.proj", aov(view), Tv, dec[view][i].proj, EPI_F32_RESID, xv(view), Dd, ACT_NONE, xv(view));
+            // cross attention: queries from this view, keys/values from the other view's
+            // projected encoder output
+            for (int view = 0; view < 2; ++view) {
+                const DecBlock& B = dec[view][i];
                 const uint16_t* yno = yn + (1 - view) * Tv * Dd;  // the other view
-                uint16_t* xnv = xn + view * Tv * Dd;
-                uint16_t* aov = ao + view * Tv * Dd;
-                // self attention
-                ln("dec.ln", xv, Tv, Dd, B.n1, xnv);
-                linear_heads("dec.qkv", xnv, Tv, B.qkv, Dd, q, 1, k, 1, v, 0);
-                attn("dec.attn_self", q, k, v, aov, n, d.dec_heads);
-                linear("dec.proj", aov, Tv, B.proj, EPI_F32_RESID, xv, Dd, ACT_NONE, xv);
-                // cross attention: queries from this view, keys/values from the other view's projected encoder output
-                ln("dec.ln", xv, Tv, Dd, B.n2, xnv);
-                linear_heads("dec.q", xnv, Tv, B.q, Dd, q, 1, nullptr, 0, nullptr, 0);
-                linear_heads("dec.kv", yno, Tv, B.kv, Dd, k, 1, v, 0, nullptr, 0);
-                attn("dec.attn_cross", q, k, v, aov, n, d.dec_heads);
-                linear("dec.cproj", aov, Tv, B.cproj, EPI_F32_RESID, xv, Dd, ACT_NONE, xv);
+                ln("dec.ln", xv(view), Tv, Dd, B.n2, xnv(view));
+                linear_heads("dec.q", xnv(view), Tv, B.q, Dd, qv(q, view), 1, nullptr, 0, nullptr, 0);
+                linear_heads("dec.kv", yno, Tv, B.kv, Dd, qv(k, view), 1, qv(v, view), 0, nullptr, 0);
+            }
+            attn("dec.attn_cross", q, k, v, ao, 2 * n, d.dec_heads);
+            for (int view = 0; view < 2; ++view) {
+                const DecBlock& B = dec[view][i];
+                linear("dec.cproj", aov(view), Tv, B.cproj, EPI_F32_RESID, xv(view), Dd, ACT_NONE, xv(view));
                 // MLP
-                ln("dec.ln", xv, Tv, Dd, B.n3, xnv);
-                linear("dec.fc1", xnv, Tv, B.fc1, EPI_BF16, h, d.dec_mlp, ACT_GELU);
-                linear("dec.fc2", h, Tv, B.fc2, EPI_F32_RESID, xv, Dd, ACT_NONE, xv);
+                ln("dec.ln", xv(view), Tv, Dd, B.n3, xnv(view));
+                linear("dec.fc1", xnv(view), Tv, B.fc1, EPI_BF16, h, d.dec_mlp, ACT_GELU);
+                linear("dec.fc2", h, Tv, B.fc2, EPI_F32_RESID, xv(view), Dd, ACT_NONE, xv(view));
             }
             if (i == d.hook1) launch(kOther, 0, "dec.hook_cast", [&] { cast16(stream_, d_.dt, xdec, T * Dd, hook1); });
             if (i == d.hook2) launch(kOther, 0, "dec.hook_cast", [&] { cast16(stream_, d_.dt, xdec, T * Dd, hook2); });
