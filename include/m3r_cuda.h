@@ -212,6 +212,12 @@ int m3r_attention_fwd(int device, int dtype, const uint16_t* q, const uint16_t* 
 int m3r_gemm_test(int device, int dtype, const uint16_t* a, const uint16_t* w, const float* bias, float* c, int M,
                   int N, int K, int bn, int cta_pair, int iters, float* kernel_ms);
 
+/* Residual GEMM as in the transformer blocks' output projections and MLP outputs
+ * (backends/python/croco_encoder.py:120-140): c[M, N] += A[M, K] * W[N, K]^T + bias,
+ * in place in fp32 (c holds the residual stream on entry).  N a multiple of 4. */
+int m3r_gemm_resid_test(int device, int dtype, const uint16_t* a, const uint16_t* w, const float* bias, float* c,
+                        int M, int N, int K, int bn, int cta_pair);
+
 /* 3x3 conv, stride 1, pad 1, NHWC: x [n, h, w, c], w [cout, 9 * cpad] (tap-major,
  * channel padded to cpad = ceil(c / 64) * 64) -> y [n, h, w, cout] fp32 (bias added). */
 int m3r_conv3_test(int device, int dtype, const uint16_t* x, const uint16_t* w, const float* bias, float* y, int n,

@@ -95,6 +95,7 @@ SIGNATURES = {
     "m3r_host_free": (None, [_P]),
     "m3r_attention_fwd": (_I, [_I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _F, _I, ctypes.POINTER(_F)]),
     "m3r_gemm_test": (_I, [_I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, ctypes.POINTER(_F)]),
+    "m3r_gemm_resid_test": (_I, [_I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I]),
     "m3r_conv3_test": (_I, [_I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I]),
     "m3r_match_nn": (_I, [_I, _P, _P, _I64, _I64, _I, _P, _P, _P, ctypes.POINTER(_F)]),
     "m3r_match_nn_static": (_I, [_I, _P, _P, _I64, _I64, _I, _P, _P, _P, _P]),

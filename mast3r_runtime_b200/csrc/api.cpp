@@ -369,6 +369,33 @@ int m3r_gemm_test(int device, int dtype, const uint16_t* a, const uint16_t* w, c
     });
 }
 
+int m3r_gemm_resid_test(int device, int dtype, const uint16_t* a, const uint16_t* w, const float* bias, float* c,
+                        int M, int N, int K, int bn, int cta_pair) {
+    return guarded(nullptr, [&] {
+        M3R_REQUIRE(a && w && c && M > 0 && N > 0 && K > 0 && K % 8 == 0 && N % 4 == 0,
+                    "gemm_resid_test: bad arguments");
+        m3r::DeviceGuard g(device);
+        DBuf da(static_cast<size_t>(M) * K * 2), dw(static_cast<size_t>(N) * K * 2), dc(static_cast<size_t>(M) * N * 4),
+            db(static_cast<size_t>(N) * 4), derr(sizeof(m3r::DevStatus));
+        M3R_CUDA(cudaMemcpy(da.p, a, static_cast<size_t>(M) * K * 2, cudaMemcpyHostToDevice));
+        M3R_CUDA(cudaMemcpy(dw.p, w, static_cast<size_t>(N) * K * 2, cudaMemcpyHostToDevice));
+        M3R_CUDA(cudaMemcpy(dc.p, c, static_cast<size_t>(M) * N * 4, cudaMemcpyHostToDevice));
+        if (bias) M3R_CUDA(cudaMemcpy(db.p, bias, static_cast<size_t>(N) * 4, cudaMemcpyHostToDevice));
+        M3R_CUDA(cudaMemset(derr.p, 0, sizeof(m3r::DevStatus)));
+        m3r::GemmParams p = m3r::gemm_params();
+        p.bias = bias ? db.as<float>() : nullptr;
+        p.out = dc.p;
+        p.ldo = N;
+        p.resid = dc.as<float>();
+        p.ldr = N;
+        p.err = derr.as<int>();
+        m3r::gemm_rows(nullptr, dtype, bn, m3r::EPI_F32_RESID, da.p, K, M, K, dw.p, K, N, p, cta_pair);
+        M3R_CUDA(cudaDeviceSynchronize());
+        check_dev_err(derr.as<int>());
+        M3R_CUDA(cudaMemcpy(c, dc.p, static_cast<size_t>(M) * N * 4, cudaMemcpyDeviceToHost));
+    });
+}
+
 int m3r_conv3_test(int device, int dtype, const uint16_t* x, const uint16_t* w, const float* bias, float* y, int n,
                    int h, int wd, int c, int cout, int bn, int cta_pair) {
     return guarded(nullptr, [&] {

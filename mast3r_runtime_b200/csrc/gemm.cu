@@ -32,7 +32,7 @@ struct Maps {
 
 template <class T, int BN, int AMODE, int EPI, int CG>
 void launch(cudaStream_t s, const Maps& m, const GemmParams& p) {
-    using C = GemmCfg<BN, CG, AMODE>;
+    using C = GemmCfg<BN, CG, AMODE, epi_ring<EPI, CG>()>;
     auto kern = gemm_tc_kernel<T, BN, AMODE, EPI, CG>;
     static std::once_flag once;  // per instantiation; the attribute is set on every device
     std::call_once(once, [&] {
@@ -89,6 +89,8 @@ void dispatch_t(cudaStream_t s, int bn, int amode, int epi, int cg, const Maps& 
     M3R_GEMM_CASE(128, A_PLAIN, EPI_F32)
     M3R_GEMM_CASE(256, A_PLAIN, EPI_F32_RESID)
     M3R_GEMM_CASE(128, A_PLAIN, EPI_F32_RESID)
+    M3R_GEMM_CASE(256, A_PLAIN, EPI_F32_RESID_LK)
+    M3R_GEMM_CASE(128, A_PLAIN, EPI_F32_RESID_LK)
     M3R_GEMM_CASE(256, A_PLAIN, EPI_HEADS)
     M3R_GEMM_CASE(128, A_PLAIN, EPI_HEADS)
     M3R_GEMM_CASE(192, A_PLAIN, EPI_DESC)
@@ -127,19 +129,30 @@ int pick_cg(int cta_pair, int tiles_m) {
     return tiles_m >= 2 ? 2 : 1;
 }
 
-// Epilogue TMA-store maps: BF16 / F32 / F32_RESID outputs as a [rows, N] matrix and
-// EPI_HEADS sections as [seq * heads, n_tok, 64], with 32-row boxes.  p.c_tma stays 0
-// (row-staged thread stores) when the layout does not allow whole 32-row boxes.
+// Epilogue TMA maps: BF16 / F32 / F32_RESID outputs as a [rows, N] matrix (and the
+// F32_RESID residual, loaded by TMA, as map 1) and EPI_HEADS sections as
+// [seq * heads, n_tok, 64], with 32-row boxes.  p.c_tma stays 0 (row-staged thread
+// stores) when the layout does not allow whole 32-row boxes; EPI_F32_RESID has no
+// such fallback and requires 16-byte aligned rows.
 void out_maps(int dt, int epi, long long rows, bool rows_consecutive, GemmParams& p, Maps& m) {
     std::memset(m.c, 0, sizeof(m.c));
     p.c_tma = 0;
-    if (!rows_consecutive) return;
     const bool out_ok = p.out != nullptr && reinterpret_cast<uintptr_t>(p.out) % 16 == 0;
+    if (epi == EPI_F32_RESID) {
+        M3R_REQUIRE(rows_consecutive && out_ok && (p.ldo * 4) % 16 == 0 && p.resid != nullptr &&
+                        reinterpret_cast<uintptr_t>(p.resid) % 16 == 0 && (p.ldr * 4) % 16 == 0,
+                    "gemm: the residual epilogue needs 16-byte aligned output and residual rows");
+        m.c[0] = tmap_2d_f32(p.out, rows, p.N, p.ldo, 32);
+        m.c[1] = tmap_2d_f32(p.resid, rows, p.N, p.ldr, 32);
+        p.c_tma = 1;
+        return;
+    }
+    if (!rows_consecutive) return;
     if (epi == EPI_BF16) {
         if (!out_ok || (p.ldo * 2) % 16 != 0) return;
         m.c[0] = tmap_2d(dt, p.out, rows, p.N, p.ldo, 32);
         p.c_tma = 1;
-    } else if (epi == EPI_F32 || epi == EPI_F32_RESID) {
+    } else if (epi == EPI_F32) {
         if (!out_ok || (p.ldo * 4) % 16 != 0) return;
         m.c[0] = tmap_2d_f32(p.out, rows, p.N, p.ldo, 32);
         p.c_tma = 1;
@@ -171,6 +184,8 @@ void gemm_rows(cudaStream_t s, int dt, int bn, int epi, const void* A, long long
     m.a0 = m.a1 = tmap_2d(dt, A, M, K, lda, 128);
     m.b = tmap_2d(dt, W, N, K, ldw, bn / cg);
     out_maps(dt, epi, M, true, p, m);
+    // residual epilogue: the long-K instantiation above 16 k-blocks (see epi_ring)
+    if (epi == EPI_F32_RESID && p.num_kb > 16) epi = EPI_F32_RESID_LK;
     dispatch(s, dt, bn, A_PLAIN, epi, cg, m, p);
 }
 

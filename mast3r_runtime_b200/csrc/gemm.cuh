@@ -38,6 +38,8 @@ enum Epi : int {
     EPI_DESC = 4,       // + bias, pixel shuffle, L2-normalise groups of 24 -> fp32 descriptors
     EPI_HEAD4 = 5,      // + bias, ReLU, fused 1x1 conv 128 -> 4 (+ bias4) -> fp32 [pixel, 4]
     EPI_CONVT = 6,      // + bias, transposed conv (kernel == stride) scatter -> T NHWC
+    EPI_F32_RESID_LK = 7,  // EPI_F32_RESID for long K, chosen by the launcher: fewer residual
+                           // buffers, more operand stages
 };
 
 enum Act : int { ACT_NONE = 0, ACT_GELU = 1, ACT_RELU = 2 };
@@ -90,10 +92,25 @@ constexpr int kGemmMmaWarp = kGemmEpiWarps + 1;
 // in which each CTA stages its own 128 rows of A and half of the tile's BN rows
 // of B, and holds its 128 x BN accumulator rows in its own TMEM.
 // A_CONV3W stages one 136-pixel A box and the B blocks of three taps per stage.
-template <int BN, int CG, int AMODE = A_PLAIN>
+// Residual epilogues: 4 KB residual buffers per epilogue warp (a ring; see
+// resid_epilogue), traded against operand stages.  Short K (the attention output
+// projections, K <= 1024) is bound by the residual traffic: CTA pairs keep 3 buffers
+// (4 operand stages at BN = 256).  Long K (the MLP outputs) is bound by the MMAs and
+// keeps 2 (5 stages); so do single CTAs.
+template <int EPI, int CG>
+constexpr int epi_ring() {
+    return EPI == EPI_F32_RESID ? (CG == 2 ? 3 : 2) : EPI == EPI_F32_RESID_LK ? 2 : 1;
+}
+template <int EPI>
+constexpr bool epi_resid() {
+    return EPI == EPI_F32_RESID || EPI == EPI_F32_RESID_LK;
+}
+
+template <int BN, int CG, int AMODE = A_PLAIN, int RING = 1>
 struct GemmCfg {
     static constexpr int BM = 128;
     static constexpr int BK = 64;
+    static constexpr int RING_BUFS = RING;
     static constexpr int B_ROWS = BN / CG;  // rows of B staged by each CTA
     static constexpr int WIDE_ROWS = 136;   // A_CONV3W box: 128 pixels + 2 halo, rounded to 8 rows
     static constexpr int TAPS = AMODE == A_CONV3W ? 3 : 1;  // B blocks per stage
@@ -101,10 +118,12 @@ struct GemmCfg {
     static constexpr int B_TAP_BYTES = B_ROWS * BK * 2;
     static constexpr int B_BYTES = TAPS * B_TAP_BYTES;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    // per-epilogue-warp row staging, 4 KB each (EPI_HEAD4 keeps its partial sums there)
-    static constexpr int EPI_STAGE_BYTES = kGemmEpiWarps * 4096;
-    // stages | epilogue staging | barriers, TMEM slot, abort flag (256 B); + 1 KB alignment slack
-    static constexpr int FIXED_BYTES = 1024 + EPI_STAGE_BYTES + 256;
+    // per-epilogue-warp row staging, RING x 4 KB each (EPI_HEAD4 keeps its partial sums there)
+    static constexpr int EPI_STAGE_BYTES = kGemmEpiWarps * 4096 * RING;
+    // stages | epilogue staging | barriers, TMEM slot, abort flag (256 B) | ring barriers;
+    // + 1 KB alignment slack
+    static constexpr int RING_BAR_BYTES = RING > 1 ? kGemmEpiWarps * RING * 8 : 0;
+    static constexpr int FIXED_BYTES = 1024 + EPI_STAGE_BYTES + 256 + RING_BAR_BYTES;
     static constexpr int MAX_SMEM = 227 * 1024;  // per-block opt-in limit of sm_100
     static constexpr int STAGES =
         ((MAX_SMEM - FIXED_BYTES) / STAGE_BYTES) > 8 ? 8 : ((MAX_SMEM - FIXED_BYTES) / STAGE_BYTES);
@@ -221,32 +240,6 @@ struct RowStage {
 #pragma unroll
         for (int c = 0; c < 8; ++c) v[c] = *at(lane, c);
     }
-    // Row-contiguous global loads of the 32 rows (src = each thread's own row pointer,
-    // null = row absent -> zeros; `bytes` = valid bytes per row, a multiple of 4).
-    __device__ __forceinline__ void fetch(const char* src, int bytes, uint4 (&r)[8]) const {
-        const int c = lane & 7;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int row = i * 4 + (lane >> 3);
-            const char* s = reinterpret_cast<const char*>(
-                __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(src), row));
-            r[i] = make_uint4(0u, 0u, 0u, 0u);
-            if (s != nullptr) {
-                if ((c + 1) * 16 <= bytes) {
-                    r[i] = *reinterpret_cast<const uint4*>(s + c * 16);
-                } else if (c * 16 < bytes) {
-                    uint32_t w[4] = {0u, 0u, 0u, 0u};
-                    for (int b = 0; b < 4 && c * 16 + 4 * b < bytes; ++b)
-                        w[b] = *reinterpret_cast<const uint32_t*>(s + c * 16 + 4 * b);
-                    r[i] = make_uint4(w[0], w[1], w[2], w[3]);
-                }
-            }
-        }
-    }
-    __device__ __forceinline__ void deposit(const uint4 (&r)[8]) const {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) *at(i * 4 + (lane >> 3), lane & 7) = r[i];
-    }
     // Row-contiguous global stores of the staged rows (dst = each thread's own row
     // pointer, null = skip; `bytes` = valid bytes per row, a multiple of 2).
     __device__ __forceinline__ void store(char* dst, int bytes) const {
@@ -297,19 +290,9 @@ __device__ __forceinline__ void tile_row(const GemmParams& p, const TileGeom& g,
     }
 }
 
-// EPI_F32_RESID: row-contiguous fetch of the residual block of the unit at tile
-// column c0 (32 fp32 columns) into registers; issued one unit ahead of its use.
-template <int BN>
-__device__ __forceinline__ void fetch_resid(const GemmParams& p, const RowStage& st, long long grow, bool valid,
-                                            int col0, uint4 (&r)[8]) {
-    const int bytes = (col0 + 32 <= p.N ? 32 : p.N - col0) * 4;
-    st.fetch(valid && col0 < p.N ? reinterpret_cast<const char*>(p.resid + grow * p.ldr + col0) : nullptr, bytes, r);
-}
-
 template <class T, int BN, int AMODE, int EPI>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeom& g, uint32_t tacc, int r, int grp,
-                                              const Head4Sync& h4, const RowStage& st, uint4 (&pre)[8],
-                                              const StoreMaps& maps) {
+                                              const Head4Sync& h4, const RowStage& st, const StoreMaps& maps) {
     long long grow;
     bool valid;
     tile_row<AMODE>(p, g, r, grow, valid);
@@ -321,19 +304,13 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
     tile_row<AMODE>(p, g, r - st.lane, wrow0, wok);
     const int lane = st.lane;
 
-    if constexpr (EPI == EPI_F32 || EPI == EPI_F32_RESID) {
+    if constexpr (EPI == EPI_F32) {
         // units of 32 fp32 columns = 128 bytes per row, staged and stored row-contiguously
 #pragma unroll 1
         for (int c0 = grp * 32; c0 < BN; c0 += 64) {
             const int col0 = n0 + c0;
             if (col0 >= p.N) break;  // warp-uniform
             const bool full = col0 + 32 <= p.N;
-            uint4 cur[8];
-            if constexpr (EPI == EPI_F32_RESID) {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) cur[i] = pre[i];
-                if (c0 + 64 < BN) fetch_resid<BN>(p, st, grow, valid, col0 + 64, pre);
-            }
             uint32_t raw[32];
             tmem_ld32(tacc + c0, raw);
             tmem_wait_ld();
@@ -342,19 +319,6 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
             for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(raw[i]);
             if (p.c_tma && lane == 0) bulk_wait_read_all();
             __syncwarp();  // the previous unit's reads of the stage (threads or TMA) are done
-            if constexpr (EPI == EPI_F32_RESID) {
-                st.deposit(cur);
-                __syncwarp();
-                uint4 rr[8];
-                st.get_own(rr);
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    v[4 * q] += __uint_as_float(rr[q].x);
-                    v[4 * q + 1] += __uint_as_float(rr[q].y);
-                    v[4 * q + 2] += __uint_as_float(rr[q].z);
-                    v[4 * q + 3] += __uint_as_float(rr[q].w);
-                }
-            }
             add_bias32(v, p.bias, col0, p.N, full);
             uint4 o[8];
 #pragma unroll
@@ -610,6 +574,138 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileGeo
 // thread issues the M = 256 MMAs; both CTAs run producer and epilogue roles on
 // the same tile sequence.  A wait that runs out raises the abort flag of both
 // CTAs; neither CTA leaves before the other (cluster barrier at the end).
+// EPI_F32_RESID epilogue of one warp over all of its tiles: out = (acc + resid) + bias
+// in fp32 (resid may alias out).  The warp's units are 32 rows x 32 columns (4 KB):
+// columns grp * 32 + 64 j of each tile.  Each unit's residual block arrives by TMA in
+// one of RING 4 KB buffers, each with its own mbarrier; lane 0 issues the load of unit
+// u + RING - 1 once unit u has been stored, across tile boundaries (the residual does
+// not depend on the accumulator), so RING - 1 blocks per warp stay in flight from HBM
+// while the warp works.  The sum overwrites the residual in the same buffer (one row
+// per thread; the 128-byte swizzle of the box keeps row-per-thread accesses free of
+// bank conflicts) and leaves by TMA store.  The tile's TMEM buffer is released after
+// its last tcgen05.ld.
+template <int BN, int AMODE, int CG, int RING, class Abort>
+__device__ __forceinline__ void resid_epilogue(const GemmParams& p, uint32_t tmem_base, uint64_t* tfull,
+                                               uint64_t* tempty, uint32_t tempty_c, uint64_t* rbar, uint8_t* ring,
+                                               const CUtensorMap* map_out, const CUtensorMap* map_resid,
+                                               volatile int* abort_flag, Abort&& abort_pair, int quarter, int grp,
+                                               int lane, int rank, int unit, int num_units, int num_tiles) {
+    static_assert(AMODE == A_PLAIN && RING >= 2, "residual epilogue: plain A, at least two buffers");
+    constexpr uint32_t kAccCols = BN <= 128 ? 128 : 256;
+    // units of this warp in a tile (0 when its row block does not exist)
+    auto tile_units = [&](const TileGeom& g) -> int {
+        if (!g.live) return 0;
+        const int lim = p.N - g.n_idx * BN < BN ? p.N - g.n_idx * BN : BN;
+        return lim > grp * 32 ? (lim - grp * 32 + 63) / 64 : 0;
+    };
+    // load cursor (lane 0): tile lt, unit lj of it, lu units issued so far
+    int lt = unit, lj = 0;
+    uint32_t lu = 0;
+    auto issue = [&]() {
+        while (lt < num_tiles) {
+            const TileGeom g = tile_geom<AMODE, CG>(p, lt, rank);
+            if (lj < tile_units(g)) {
+                const int b = static_cast<int>(lu % RING);
+                const int row0 = g.m_idx * 128 + quarter * 32;
+                if (row0 < p.M) {
+                    mbar_arrive_expect_tx(&rbar[b], 4096);
+                    tma_load_2d(ring + b * 4096, map_resid, &rbar[b], g.n_idx * BN + grp * 32 + 64 * lj, row0);
+                } else {
+                    mbar_arrive(&rbar[b]);  // rows past the end: nothing to load or store
+                }
+                ++lj;
+                ++lu;
+                return;
+            }
+            lt += num_units;
+            lj = 0;
+        }
+    };
+    if (lane == 0)
+        for (int i = 0; i < RING - 1; ++i) issue();
+
+    uint32_t cu = 0, tcount = 0;  // units consumed, tiles visited
+    bool ok = true;
+    for (int t = unit; t < num_tiles && ok; t += num_units, ++tcount) {
+        const uint32_t buf = tcount & 1;
+        const TileGeom g = tile_geom<AMODE, CG>(p, t, rank);
+        if (!mbar_wait(&tfull[buf], (tcount >> 1) & 1, abort_flag, kDevTimeoutEpilogue, p.err)) {
+            abort_pair();
+            ok = false;
+            break;
+        }
+        tc_fence_after();
+        const int nu = tile_units(g);
+        const int row0 = g.m_idx * 128 + quarter * 32;
+        const bool rows_ok = row0 < p.M;
+        const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * kAccCols;
+        auto release = [&]() {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if (CG == 2)
+                    mbar_arrive_cluster(tempty_c + buf * 8);
+                else
+                    mbar_arrive(&tempty[buf]);
+            }
+        };
+        if (nu == 0) release();
+#pragma unroll 1
+        for (int j = 0; j < nu; ++j, ++cu) {
+            const int c0 = grp * 32 + 64 * j;
+            const int col0 = g.n_idx * BN + c0;
+            uint32_t raw[32];
+            tmem_ld32(tacc + c0, raw);
+            tmem_wait_ld();
+            if (j == nu - 1) release();
+            const int b = static_cast<int>(cu % RING);
+            if (!mbar_wait(&rbar[b], (cu / RING) & 1, abort_flag, kDevTimeoutEpilogue, p.err)) {
+                abort_pair();
+                ok = false;
+                break;
+            }
+            const RowStage rs{ring + b * 4096, lane};
+            uint4 rr[8];
+            rs.get_own(rr);
+            float v[32];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                v[4 * q] = __uint_as_float(raw[4 * q]) + __uint_as_float(rr[q].x);
+                v[4 * q + 1] = __uint_as_float(raw[4 * q + 1]) + __uint_as_float(rr[q].y);
+                v[4 * q + 2] = __uint_as_float(raw[4 * q + 2]) + __uint_as_float(rr[q].z);
+                v[4 * q + 3] = __uint_as_float(raw[4 * q + 3]) + __uint_as_float(rr[q].w);
+            }
+            add_bias32(v, p.bias, col0, p.N, col0 + 32 <= p.N);
+            uint4 o[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                o[q] = make_uint4(__float_as_uint(v[4 * q]), __float_as_uint(v[4 * q + 1]), __float_as_uint(v[4 * q + 2]),
+                                  __float_as_uint(v[4 * q + 3]));
+            rs.put_own(o);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                // the buffer refilled next, (cu + RING - 1) % RING, was stored from by the
+                // previous unit: its store must have finished reading it
+                if (rows_ok) {
+                    tma_store_2d(map_out, rs.buf, col0, row0);
+                    bulk_commit();
+                    bulk_wait_read_1();
+                } else {
+                    bulk_wait_read_all();
+                }
+                issue();
+            }
+        }
+    }
+    if (!ok && lane == 0) {
+        // wait (bounded) for the residual loads still in flight before the CTA may leave
+        volatile int no_abort = 0;
+        for (uint32_t u = cu; u < lu; ++u)
+            mbar_wait(&rbar[u % RING], (u / RING) & 1, &no_abort, kDevTimeoutEpilogue, p.err);
+    }
+}
+
 template <class T, int BN, int AMODE, int EPI, int CG>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_constant__ CUtensorMap mapA1,
@@ -617,7 +713,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                    const __grid_constant__ CUtensorMap mapC1, const __grid_constant__ CUtensorMap mapC2,
                    const __grid_constant__ GemmParams p) {
     static_assert(CG == 1 || CG == 2, "one CTA or a CTA pair per tile");
-    using C = GemmCfg<BN, CG, AMODE>;
+    using C = GemmCfg<BN, CG, AMODE, epi_ring<EPI, CG>()>;
     constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -634,6 +730,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t* h4_empty = bars + 2 * STAGES + 6;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 7);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    uint64_t* ring_bars = bars + 32;  // EPI_F32_RESID: RING per epilogue warp, after the 256-byte block
     float* head4_part = reinterpret_cast<float*>(epi_stage);
     float* head4_wts = reinterpret_cast<float*>(epi_stage + 2048);  // EPI_HEAD4: 640 floats
 
@@ -657,6 +754,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         mbar_init(mma_done, 1);
         mbar_init(h4_full, 128);
         mbar_init(h4_empty, 128);
+        if (epi_resid<EPI>())
+            for (int b = 0; b < kGemmEpiWarps * C::RING_BUFS; ++b) mbar_init(&ring_bars[b], 1);
         *abort_flag = 0;
         fence_barrier_init();
         prefetch_tmap(&mapA0);
@@ -839,56 +938,39 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int quarter = warp & 3;
         const int grp = warp >> 2;
         const int r = quarter * 32 + lane;
-        const RowStage st{epi_stage + warp * 4096, lane};
-        const StoreMaps maps{{&mapC0, &mapC1, &mapC2}};
-        uint4 pre[8];  // EPI_F32_RESID: residual block of the next unit, fetched ahead
-        uint32_t tcount = 0, h4count = 0;
-        // EPI_F32_RESID: the first column group's warps bulk-prefetch into L2 the residual
-        // rows (one row per lane, the tile's whole width) of the tile after the one they
-        // are about to process, so the register fetches of the epilogue hit L2
-        auto prefetch_resid = [&](int tt) {
-            if (EPI != EPI_F32_RESID || grp != 0 || tt >= num_tiles) return;
-            const TileGeom gn = tile_geom<AMODE, CG>(p, tt, rank);
-            if (!gn.live) return;
-            long long grow;
-            bool valid;
-            tile_row<AMODE>(p, gn, r, grow, valid);
-            const int col0 = gn.n_idx * BN;
-            const int cols = p.N - col0 < BN ? p.N - col0 : BN;
-            const char* src = reinterpret_cast<const char*>(p.resid + grow * p.ldr + col0);
-            if (valid && cols > 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0 && (cols * 4) % 16 == 0)
-                prefetch_l2_bulk(src, static_cast<uint32_t>(cols * 4));
-        };
-        prefetch_resid(unit);
-        for (int t = unit; t < num_tiles; t += num_units, ++tcount) {
-            const uint32_t buf = tcount & 1;
-            const uint32_t tph = (tcount >> 1) & 1;
-            const TileGeom g = tile_geom<AMODE, CG>(p, t, rank);
-            prefetch_resid(t + num_units);
-            if (EPI == EPI_F32_RESID && g.live) {
-                // the residual does not depend on the accumulator: fetch before waiting for it
-                long long grow;
-                bool valid;
-                tile_row<AMODE>(p, g, r, grow, valid);
-                fetch_resid<BN>(p, st, grow, valid, g.n_idx * BN + grp * 32, pre);
-            }
-            if (!mbar_wait(&tfull[buf], tph, abort_flag, kDevTimeoutEpilogue, p.err)) {
-                abort_pair();
-                break;
-            }
-            tc_fence_after();
-            if (g.live) {
-                const uint32_t tacc = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * C::ACC_COLS;
-                const Head4Sync h4{head4_part, head4_wts, h4_full, h4_empty, abort_flag, h4count++};
-                epilogue_tile<T, BN, AMODE, EPI>(p, g, tacc, r, grp, h4, st, pre, maps);
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                if (CG == 2)
-                    mbar_arrive_cluster(tempty_c + buf * 8);
-                else
-                    mbar_arrive(&tempty[buf]);
+        if constexpr (epi_resid<EPI>()) {
+            resid_epilogue<BN, AMODE, CG, C::RING_BUFS>(p, tmem_base, tfull, tempty, tempty_c,
+                                                      ring_bars + warp * C::RING_BUFS,
+                                                      epi_stage + warp * 4096 * C::RING_BUFS, &mapC0, &mapC1,
+                                                      abort_flag, abort_pair, quarter, grp, lane, rank, unit,
+                                                      num_units, num_tiles);
+        } else {
+            const RowStage st{epi_stage + warp * 4096, lane};
+            const StoreMaps maps{{&mapC0, &mapC1, &mapC2}};
+            uint32_t tcount = 0, h4count = 0;
+            for (int t = unit; t < num_tiles; t += num_units, ++tcount) {
+                const uint32_t buf = tcount & 1;
+                const uint32_t tph = (tcount >> 1) & 1;
+                const TileGeom g = tile_geom<AMODE, CG>(p, t, rank);
+                if (!mbar_wait(&tfull[buf], tph, abort_flag, kDevTimeoutEpilogue, p.err)) {
+                    abort_pair();
+                    break;
+                }
+                tc_fence_after();
+                if (g.live) {
+                    const uint32_t tacc =
+                        tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + buf * C::ACC_COLS;
+                    const Head4Sync h4{head4_part, head4_wts, h4_full, h4_empty, abort_flag, h4count++};
+                    epilogue_tile<T, BN, AMODE, EPI>(p, g, tacc, r, grp, h4, st, maps);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    if (CG == 2)
+                        mbar_arrive_cluster(tempty_c + buf * 8);
+                    else
+                        mbar_arrive(&tempty[buf]);
+                }
             }
         }
         if (lane == 0) bulk_wait_all();  // TMA stores of this warp complete before the CTA ends

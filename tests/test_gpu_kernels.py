@@ -58,6 +58,33 @@ def test_gemm_matches_fp64(lib, M, N, K, bn, dtype, pair):
     assert np.abs(c - ref).max() < 1e-4 * np.sqrt(K) * (np.abs(ref).max() + 1)
 
 
+@pytest.mark.parametrize("pair", [0, 1], ids=["cta", "pair"])
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+@pytest.mark.parametrize("M,N,K,bn", [
+    (128, 256, 64, 256),
+    (300, 200, 136, 128),   # ragged M and N: zero-filled residual loads, clipped stores
+    (389, 516, 256, 256),   # a last column unit 4 wide
+    (1000, 96, 96, 128),    # second column group idle in every tile
+    (2048, 768, 3072, 256),
+    (4500, 1024, 1024, 256),  # several tiles per CTA: the residual ring crosses tiles
+])
+def test_gemm_residual_matches_fp64(lib, M, N, K, bn, dtype, pair):
+    """c += A W^T + bias in place: the residual epilogue (TMA-loaded residual ring)."""
+    from mast3r_runtime_b200 import _lib
+
+    rng = np.random.default_rng(M * 7 + N + K)
+    a = round16(rng.standard_normal((M, K)).astype(np.float32), dtype)
+    w = round16(rng.standard_normal((N, K)).astype(np.float32) * 0.05, dtype)
+    bias = rng.standard_normal(N).astype(np.float32)
+    resid = (rng.standard_normal((M, N)) * 4).astype(np.float32)
+    c = resid.copy()
+    _lib.check(lib.m3r_gemm_resid_test(0, DTYPES[dtype], P(to16(a, dtype)), P(to16(w, dtype)), P(bias), P(c), M, N, K,
+                                       bn, pair))
+    ref = resid.astype(np.float64) + a.astype(np.float64) @ w.astype(np.float64).T + bias
+    assert rel_l2(c, ref) < 1e-5, rel_l2(c, ref)
+    assert np.abs(c - ref).max() < 1e-4 * np.sqrt(K) * (np.abs(ref).max() + 1)
+
+
 def _conv3_ref(x, w, b):
     n, h, wd, c = x.shape
     co = w.shape[0]
