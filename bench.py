@@ -274,7 +274,7 @@ def run_attention(dtype, iters=20):
     return flop, res
 
 
-def cpu_baseline_attention(slices=24):
+def cpu_baseline_attention(slices=384):
     """The reference's own multi_head_attention (csrc/cpu/attention.cpp, OpenMP, compiled into
     oracle/_ref) on `slices` of the 1536 (sequence, head) slices; GFLOP/s of that sample."""
     import oracle
@@ -291,7 +291,7 @@ def cpu_baseline_attention(slices=24):
     flop = 4.0 * ATT_TOK * ATT_TOK * 64 * slices
     return {"value": flop / t / 1e9, "unit": "GFLOP/s", "cores": oracle.cpu_count(), "kind": "reference",
             "sample": f"{slices} of 1536 (sequence, head) slices through the reference's multi_head_attention "
-                      f"(oracle/_ref), {t:.1f} s"}
+                      f"(oracle/_ref), {t:.2f} s"}
 
 
 def cpu_baseline_port(dims, hw, n_pairs=1, budget_s=60.0):
