@@ -294,7 +294,29 @@ def cpu_baseline_attention(slices=384):
                       f"(oracle/_ref), {t:.2f} s"}
 
 
-def cpu_baseline_port(dims, hw, n_pairs=1, budget_s=60.0):
+def run_small_config(variant, hw, pairs, dtype_name, device, steps, warmup):
+    """Device-resident pairs/s of another model configuration on one GPU (rank 0 only)."""
+    from mast3r_runtime_b200 import NativeEngine, _lib
+    from mast3r_runtime_b200.weights import VARIANTS
+
+    d = VARIANTS[variant]
+    path = weights_file(d, 0, None)
+    img1, img2 = make_inputs(0, pairs, hw)
+    dt = {"fp16": _lib.DTYPE_F16, "bf16": _lib.DTYPE_BF16}[dtype_name]
+    eng = NativeEngine(d, hw, [device], pairs, dt)
+    eng.load(str(path))
+    eng.stage(img1, img2)
+    for _ in range(warmup):
+        eng.run_resident(pairs)
+    ms = [eng.run_resident(pairs) for _ in range(steps)]
+    eng.close()
+    total = sum(ms)
+    return {"value": pairs * steps / (total / 1000.0), "unit": "pairs/s", "pairs_per_pass": pairs,
+            "ms_per_pass": total / steps, "dtype": dtype_name,
+            "model_tflops": flops_per_pair(d, hw) * pairs * steps / (total / 1000.0) / 1e12}
+
+
+def cpu_baseline_port(dims, hw, n_pairs=1, budget_s=60.0, workload="the 64-pair workload"):
     """The oracle (numpy float32, all host cores) on one pair: a bounded sample of the workload."""
     from mast3r_runtime_b200 import make_weights
     from oracle.model import Model
@@ -312,7 +334,7 @@ def cpu_baseline_port(dims, hw, n_pairs=1, budget_s=60.0):
         if time.perf_counter() - t_start > budget_s:
             break
     return {"value": len(times) / sum(times), "unit": "pairs/s", "cores": oracle.cpu_count(), "kind": "port",
-            "sample": f"{len(times)} pair(s) of the 64-pair workload through oracle/model.py (numpy float32, "
+            "sample": f"{len(times)} pair(s) of {workload} through oracle/model.py (numpy float32, "
                       f"all host cores), {sum(times):.1f} s"}
 
 
@@ -527,6 +549,24 @@ def run_ours(args):
                                      f"(24x24 grid) x 64, {args.dtype}, Q/K/V ~ N(0,1) (RoPE is applied by the "
                                      f"producing QKV GEMM's epilogue in this design)", "flop_per_launch": flop, **res}
 
+    # ---------------- the smaller configurations, device-resident on rank 0's GPU
+    small = None
+    if rank == 0 and not args.no_matcher:
+        small = {
+            "config0": {"workload": "DUNE ViT-S/14 encoder + MASt3R decoder and heads, 336x336, 1 pair per pass "
+                                    "(precision fp32 runs fp16 operands with fp32 accumulation)",
+                        **run_small_config("dune_vit_small_336", (336, 336), 1, "fp16", local_rank, args.steps,
+                                           args.warmup)},
+            "config2": {"workload": "DUNE ViT-B/14 encoder + MASt3R decoder and heads, 336x336, bf16: the 4-pair "
+                                    "share of one GPU when 32 pairs are sharded over 8, and the whole 32-pair "
+                                    "batch on one GPU",
+                        "per_gpu_share": run_small_config("dune_vit_base_336", (336, 336), 4, "bf16", local_rank,
+                                                          args.steps, args.warmup),
+                        "whole_batch": run_small_config("dune_vit_base_336", (336, 336), 32, "bf16", local_rank,
+                                                        args.steps, args.warmup)},
+        }
+    barrier()
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and total_pairs == GLOBAL_PAIRS:
         cpu = cpu_baseline_port(d, IMAGE_HW)
@@ -534,6 +574,11 @@ def run_ours(args):
             matcher["cpu_baseline"] = cpu_baseline_matcher()
         if attention_iso is not None:
             attention_iso["cpu_baseline"] = cpu_baseline_attention()
+        if small is not None:
+            from mast3r_runtime_b200.weights import VARIANTS
+
+            small["config0"]["cpu_baseline"] = cpu_baseline_port(VARIANTS["dune_vit_small_336"], (336, 336),
+                                                                 workload="the 1-pair DUNE-S/14 336 workload")
 
     if rank == 0:
         pk, src = peaks()
@@ -576,6 +621,7 @@ def run_ours(args):
                           "ms_per_step": prof["attn_ms"], "launches_per_step": int(prof["attn_launches"])},
             "attention_isolated": attention_iso,
             "matcher": matcher,
+            "small_configs": small,
             "model_tflops": fpp * total_pairs * args.steps / (total_ms / 1000.0) / 1e12,
             "kernel_ms_per_step": {"gemm": prof["gemm_ms"], "attention": prof["attn_ms"], "other": prof["other_ms"]},
             # per operation of the model: [device ms per step, TFLOP/s (0 for non-contractions)]
@@ -608,7 +654,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end pass (profiling runs)")
     ap.add_argument("--dtype", choices=("fp16", "bf16"), default="fp16", help="operand type of the headline line")
     ap.add_argument("--no-other-dtype", action="store_true", help="skip the pass in the other 16-bit type")
-    ap.add_argument("--no-matcher", action="store_true", help="skip the matcher and isolated-attention lines")
+    ap.add_argument("--no-matcher", action="store_true",
+                    help="skip the matcher, isolated-attention and small-configuration lines")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
