@@ -395,6 +395,10 @@ def run_ours(args):
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                  device_id=torch.device("cuda", local_rank))
         dist = tdist
+        # host-side waits while rank 0 drives every GPU (the sharded matcher): an NCCL
+        # barrier would leave a spinning kernel on each waiting rank's GPU, time-sliced
+        # against rank 0's kernels there
+        host_group = tdist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=600))
 
     def allmax(x: float) -> float:
         if dist is None:
@@ -408,6 +412,10 @@ def run_ours(args):
     def barrier():
         if dist is not None:
             dist.barrier()
+
+    def host_barrier():
+        if dist is not None:
+            dist.barrier(group=host_group)
 
     from mast3r_runtime_b200 import NativeEngine, _lib
     from mast3r_runtime_b200.weights import VARIANTS
@@ -537,9 +545,10 @@ def run_ours(args):
     # ---------------- matcher at N = 196,608 (rank 0 drives all N GPUs; the others wait)
     matcher = None
     barrier()
+    host_barrier()
     if rank == 0 and not args.no_matcher:
         matcher = run_matcher(list(range(world)), args.steps, clk["sm_mhz"] if clk else None)
-    barrier()
+    host_barrier()
 
     # ---------------- isolated attention (128 seqs x 12 heads x 576 x 64), one GPU
     attention_iso = None
