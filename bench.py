@@ -480,12 +480,14 @@ def run_ours(args):
             d2h.append(tm["d2h_ms"])
         e2e_s = allmax(time.perf_counter() - t0)
         out_bytes = int(sum(o.nbytes for o in outs.values()))
+        d2h_max_ms = allmax(statistics.median(d2h))  # every rank copies at once: the host's aggregate rate
         e2e_line = {"value": total_pairs * args.steps / e2e_s, "unit": "pairs/s",
                     "h2d_bytes_per_step": int(p1.nbytes + p2.nbytes) * world,
                     "d2h_bytes_per_step": out_bytes * world,
                     "host_buffers": "pinned (m3r_host_alloc)",
                     "rank0_h2d_ms": statistics.median(h2d), "rank0_d2h_ms": statistics.median(d2h),
-                    "rank0_d2h_gbs": out_bytes / (statistics.median(d2h) * 1e-3) / 1e9 if d2h[0] > 0 else None}
+                    "rank0_d2h_gbs": out_bytes / (statistics.median(d2h) * 1e-3) / 1e9 if d2h[0] > 0 else None,
+                    "all_ranks_d2h_gbs": out_bytes * world / (d2h_max_ms * 1e-3) / 1e9 if d2h_max_ms > 0 else None}
         # the call the drop-in engine makes: ordinary numpy images in, outputs from the
         # engine's recycled page-locked buffers (the previous step's are released first)
         del outs
