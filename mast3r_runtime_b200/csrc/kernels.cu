@@ -161,6 +161,68 @@ __device__ __forceinline__ void bilerp_acc(const T* base, int hi, int wi, int C,
     }
 }
 
+// Mixed-precision multiply-add (sm_100 fma.rn.f32.{f16,bf16}): d = a * w + c with 16-bit a
+// and w of the operand type T, fp32 c and d, one rounding.  Interpolation weights that are
+// multiples of 1/256 (the 2x / 4x / 8x half-pixel fractions and their products) are exact in
+// both 16-bit types and their products with a 16-bit value exact in fp32, so the
+// interpolations below need no 16 -> 32-bit conversions and round once per term.
+template <class T>
+struct Mix;
+template <>
+struct Mix<__half> {
+    // (d0, d1) = (lo(pair), hi(pair)) * w + (c0, c1)
+    __device__ static __forceinline__ void fma2(uint32_t pair, uint16_t w, float c0, float c1, float& d0, float& d1) {
+        asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+            "fma.rn.f32.f16 %0, lo, %3, %4;\n\tfma.rn.f32.f16 %1, hi, %3, %5;\n\t}"
+            : "=f"(d0), "=f"(d1)
+            : "r"(pair), "h"(w), "f"(c0), "f"(c1));
+    }
+    __device__ static __forceinline__ uint16_t bits(float w) { return __half_as_ushort(__float2half_rn(w)); }
+};
+template <>
+struct Mix<__nv_bfloat16> {
+    __device__ static __forceinline__ void fma2(uint32_t pair, uint16_t w, float c0, float c1, float& d0, float& d1) {
+        asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+            "fma.rn.f32.bf16 %0, lo, %3, %4;\n\tfma.rn.f32.bf16 %1, hi, %3, %5;\n\t}"
+            : "=f"(d0), "=f"(d1)
+            : "r"(pair), "h"(w), "f"(c0), "f"(c1));
+    }
+    __device__ static __forceinline__ uint16_t bits(float w) {
+        return __bfloat16_as_ushort(__float2bfloat16_rn(w));
+    }
+};
+
+__device__ __forceinline__ uint4 ld16(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ uint32_t word(const uint4& u, int q) {
+    return q == 0 ? u.x : q == 1 ? u.y : q == 2 ? u.z : u.w;
+}
+
+// acc += bilinear sample (half-pixel centres, clamped) of an 8-channel chunk, weights
+// w00..w11 in the operand type (exact for the power-of-two ratios it is used with)
+template <class T>
+__device__ __forceinline__ void bilerp_mix(const T* base, int hi, int wi, int C, int Ho, int Wo, int y, int x, int c8,
+                                           float (&acc)[8]) {
+    int y0, y1, x0, x1;
+    float fy, fx;
+    src_coord(y, hi, Ho, y0, y1, fy);
+    src_coord(x, wi, Wo, x0, x1, fx);
+    const uint16_t w00 = Mix<T>::bits((1.0f - fx) * (1.0f - fy)), w01 = Mix<T>::bits(fx * (1.0f - fy));
+    const uint16_t w10 = Mix<T>::bits((1.0f - fx) * fy), w11 = Mix<T>::bits(fx * fy);
+    const uint4 a = ld16(base + (static_cast<long long>(y0) * wi + x0) * C + c8);
+    const uint4 b = ld16(base + (static_cast<long long>(y0) * wi + x1) * C + c8);
+    const uint4 c = ld16(base + (static_cast<long long>(y1) * wi + x0) * C + c8);
+    const uint4 d = ld16(base + (static_cast<long long>(y1) * wi + x1) * C + c8);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        float& s0 = acc[2 * q];
+        float& s1 = acc[2 * q + 1];
+        Mix<T>::fma2(word(a, q), w00, s0, s1, s0, s1);
+        Mix<T>::fma2(word(b, q), w01, s0, s1, s0, s1);
+        Mix<T>::fma2(word(c, q), w10, s0, s1, s0, s1);
+        Mix<T>::fma2(word(d, q), w11, s0, s1, s0, s1);
+    }
+}
+
 // Grid of the NHWC elementwise kernels below: blockIdx.z = image, blockIdx.y =
 // (output) row, x = (pixel in the row, 8-channel chunk); no 64-bit division.
 struct RowGrid {
@@ -193,6 +255,35 @@ __global__ void dpt_fuse_kernel(const T* __restrict__ f0, const T* __restrict__ 
     store8(out + ((im * H0 + y) * W0 + x) * C + c8, acc);
 }
 
+// dpt_fuse_kernel for levels at exactly 1/2, 1/4 and 1/8 of the output size (the DPT
+// pyramid of every model size here): mixed-precision accumulation, no conversions.
+template <class T>
+__global__ void dpt_fuse_pow2_kernel(const T* __restrict__ f0, const T* __restrict__ f1, const T* __restrict__ f2,
+                                     const T* __restrict__ f3, int H0, int W0, int C, T* __restrict__ out) {
+    int x, c8;
+    if (!RowGrid{C / 8}.at(W0, x, c8)) return;
+    const int y = blockIdx.y;
+    const long long im = blockIdx.z;
+    float acc[8];
+    const uint4 u = ld16(f0 + ((im * H0 + y) * W0 + x) * C + c8);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float2 f = Elem<T>::unpack(word(u, q));
+        acc[2 * q] = f.x;
+        acc[2 * q + 1] = f.y;
+    }
+    const int h1 = H0 / 2, w1 = W0 / 2, h2 = H0 / 4, w2 = W0 / 4, h3 = H0 / 8, w3 = W0 / 8;
+    bilerp_mix(f1 + im * h1 * w1 * C, h1, w1, C, H0, W0, y, x, c8, acc);
+    bilerp_mix(f2 + im * h2 * w2 * C, h2, w2, C, H0, W0, y, x, c8, acc);
+    bilerp_mix(f3 + im * h3 * w3 * C, h3, w3, C, H0, W0, y, x, c8, acc);
+    uint4 o;
+    o.x = Elem<T>::pack(acc[0], acc[1]);
+    o.y = Elem<T>::pack(acc[2], acc[3]);
+    o.z = Elem<T>::pack(acc[4], acc[5]);
+    o.w = Elem<T>::pack(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(out + ((im * H0 + y) * W0 + x) * C + c8) = o;
+}
+
 template <class T>
 __global__ void resize_kernel(const T* __restrict__ x, int hi, int wi, int C, int ho, int wo, T* __restrict__ y) {
     int ox, c8;
@@ -209,39 +300,81 @@ __global__ void resize_kernel(const T* __restrict__ x, int hi, int wi, int C, in
 // Exact 2x upsampling (half-pixel centres): output row 2i takes input rows i-1, i
 // with weights 0.25, 0.75 and row 2i+1 takes i, i+1 with 0.75, 0.25, the
 // neighbours clamped at the borders (which reproduces the clamped source
-// coordinate of bilerp_acc); the same along x.  The thread of input pixel
-// (iy, ix) writes the four output pixels (2iy + a, 2ix + b) from its clamped 3x3
-// neighbourhood.
+// coordinate of bilerp_acc); the same along x.  A thread owns one 8-channel chunk of
+// input column ix over kResizeRows input rows: it keeps the x-interpolated values of
+// rows iy-1, iy, iy+1 in registers (a sliding window, three 16-byte loads per input
+// row) and writes the four output pixels (2iy + a, 2ix + b) of each row.
+constexpr int kResizeRows = 4;
+
+// (o0, o1) = 0.75 * (c0, c1) + 0.25 * (e0, e1) in two packed fp32 operations
+__device__ __forceinline__ void lerp_q2(float c0, float c1, float e0, float e1, float& o0, float& o1) {
+    asm("{\n\t.reg .b64 c, e, k1, k3, t;\n\t"
+        "mov.b64 c, {%2, %3};\n\tmov.b64 e, {%4, %5};\n\t"
+        "mov.b64 k1, {%6, %6};\n\tmov.b64 k3, {%7, %7};\n\t"
+        "mul.rn.f32x2 t, e, k1;\n\tfma.rn.f32x2 t, c, k3, t;\n\t"
+        "mov.b64 {%0, %1}, t;\n\t}"
+        : "=f"(o0), "=f"(o1)
+        : "f"(c0), "f"(c1), "f"(e0), "f"(e1), "f"(0.25f), "f"(0.75f));
+}
+
+// x-interpolation of one input row at column ix: h[b][i] = output column 2ix + b
+template <class T>
+__device__ __forceinline__ void resize2x_row(const T* row, int C, int xl, int xc, int xr, uint16_t q1, uint16_t q3,
+                                             float (&h)[2][8]) {
+    const uint4 l = ld16(row + static_cast<long long>(xl) * C);
+    const uint4 m = ld16(row + static_cast<long long>(xc) * C);
+    const uint4 r = ld16(row + static_cast<long long>(xr) * C);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        float t0, t1;
+        Mix<T>::fma2(word(m, q), q3, 0.0f, 0.0f, t0, t1);  // 0.75 * centre: exact in fp32
+        Mix<T>::fma2(word(l, q), q1, t0, t1, h[0][2 * q], h[0][2 * q + 1]);
+        Mix<T>::fma2(word(r, q), q1, t0, t1, h[1][2 * q], h[1][2 * q + 1]);
+    }
+}
+
 template <class T>
 __global__ void resize2x_kernel(const T* __restrict__ x, int hi, int wi, int C, T* __restrict__ y) {
     int ix, c8;
     if (!RowGrid{C / 8}.at(wi, ix, c8)) return;
-    const int iy = blockIdx.y;
+    const int iy0 = blockIdx.y * kResizeRows;
     const long long im = blockIdx.z;
     const T* base = x + im * hi * wi * C + c8;
     const int ho = 2 * hi, wo = 2 * wi;
-    const int ry[3] = {max(iy - 1, 0), iy, min(iy + 1, hi - 1)};
-    const int rx[3] = {max(ix - 1, 0), ix, min(ix + 1, wi - 1)};
-    F8 nb[3][3];
+    const int xl = max(ix - 1, 0), xr = min(ix + 1, wi - 1);
+    const uint16_t q1 = Mix<T>::bits(0.25f), q3 = Mix<T>::bits(0.75f);
+    float hp[2][8], hc[2][8], hn[2][8];  // rows iy - 1, iy, iy + 1 (clamped)
+    resize2x_row(base + static_cast<long long>(max(iy0 - 1, 0)) * wi * C, C, xl, ix, xr, q1, q3, hp);
+    resize2x_row(base + static_cast<long long>(iy0) * wi * C, C, xl, ix, xr, q1, q3, hc);
 #pragma unroll
-    for (int a = 0; a < 3; ++a)
+    for (int k = 0; k < kResizeRows; ++k) {
+        const int iy = iy0 + k;
+        if (iy >= hi) break;
+        resize2x_row(base + static_cast<long long>(min(iy + 1, hi - 1)) * wi * C, C, xl, ix, xr, q1, q3, hn);
 #pragma unroll
-        for (int b = 0; b < 3; ++b) load8(base + (static_cast<long long>(ry[a]) * wi + rx[b]) * C, nb[a][b]);
-    constexpr float kF[2] = {0.75f, 0.25f};  // fraction towards the second tap, output phase 0 / 1
+        for (int a = 0; a < 2; ++a) {
 #pragma unroll
-    for (int a = 0; a < 2; ++a) {
+            for (int b = 0; b < 2; ++b) {
+                // row 2iy: 0.75 row iy + 0.25 row iy-1; row 2iy + 1: 0.75 row iy + 0.25 row iy+1
+                const float(&e)[2][8] = a == 0 ? hp : hn;
+                float o[8];
 #pragma unroll
-        for (int b = 0; b < 2; ++b) {
-            const float fy = kF[a], fx = kF[b];
-            F8 o;
+                for (int i = 0; i < 8; i += 2) lerp_q2(hc[b][i], hc[b][i + 1], e[b][i], e[b][i + 1], o[i], o[i + 1]);
+                uint4 u;
+                u.x = Elem<T>::pack(o[0], o[1]);
+                u.y = Elem<T>::pack(o[2], o[3]);
+                u.z = Elem<T>::pack(o[4], o[5]);
+                u.w = Elem<T>::pack(o[6], o[7]);
+                *reinterpret_cast<uint4*>(y + ((im * ho + 2 * iy + a) * wo + 2 * ix + b) * C + c8) = u;
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < 2; ++b)
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                const float top = nb[a][b].v[i] * (1.0f - fx) + nb[a][b + 1].v[i] * fx;
-                const float bot = nb[a + 1][b].v[i] * (1.0f - fx) + nb[a + 1][b + 1].v[i] * fx;
-                o.v[i] = top * (1.0f - fy) + bot * fy;
+                hp[b][i] = hc[b][i];
+                hc[b][i] = hn[b][i];
             }
-            store8(y + ((im * ho + 2 * iy + a) * wo + 2 * ix + b) * C + c8, o);
-        }
     }
 }
 
@@ -476,9 +609,15 @@ void dpt_fuse(cudaStream_t s, int dt, const void* f0, const void* f1, int h1, in
               const void* f3, int h3, int w3, int n, int H0, int W0, int C, void* out) {
     M3R_REQUIRE(C % 8 == 0, "dpt_fuse: C % 8");
     M3R_REQUIRE(n <= 65535 && H0 <= 65535, "dpt_fuse: grid too large");
-    M3R_BY_DT(dt, dpt_fuse_kernel<T><<<row_grid(n, H0, W0, C / 8, 128), 128, 0, s>>>(
-                      static_cast<const T*>(f0), static_cast<const T*>(f1), h1, w1, static_cast<const T*>(f2), h2, w2,
-                      static_cast<const T*>(f3), h3, w3, H0, W0, C, static_cast<T*>(out)));
+    if (H0 == 2 * h1 && W0 == 2 * w1 && H0 == 4 * h2 && W0 == 4 * w2 && H0 == 8 * h3 && W0 == 8 * w3) {
+        M3R_BY_DT(dt, dpt_fuse_pow2_kernel<T><<<row_grid(n, H0, W0, C / 8, 128), 128, 0, s>>>(
+                          static_cast<const T*>(f0), static_cast<const T*>(f1), static_cast<const T*>(f2),
+                          static_cast<const T*>(f3), H0, W0, C, static_cast<T*>(out)));
+    } else {
+        M3R_BY_DT(dt, dpt_fuse_kernel<T><<<row_grid(n, H0, W0, C / 8, 128), 128, 0, s>>>(
+                          static_cast<const T*>(f0), static_cast<const T*>(f1), h1, w1, static_cast<const T*>(f2), h2,
+                          w2, static_cast<const T*>(f3), h3, w3, H0, W0, C, static_cast<T*>(out)));
+    }
     M3R_CUDA(cudaGetLastError());
 }
 
@@ -486,7 +625,8 @@ void resize16(cudaStream_t s, int dt, const void* x, int n, int hi, int wi, int 
     M3R_REQUIRE(C % 8 == 0, "resize16: C % 8");
     M3R_REQUIRE(n <= 65535 && ho <= 65535, "resize16: grid too large");
     if (ho == 2 * hi && wo == 2 * wi) {
-        M3R_BY_DT(dt, resize2x_kernel<T><<<row_grid(n, hi, wi, C / 8, 128), 128, 0, s>>>(
+        M3R_BY_DT(dt, resize2x_kernel<T><<<row_grid(n, (hi + kResizeRows - 1) / kResizeRows, wi, C / 8, 128), 128, 0,
+                                           s>>>(
                           static_cast<const T*>(x), hi, wi, C, static_cast<T*>(y)));
     } else {
         M3R_BY_DT(dt, resize_kernel<T><<<row_grid(n, ho, wo, C / 8, 128), 128, 0, s>>>(
