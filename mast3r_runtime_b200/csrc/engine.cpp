@@ -754,7 +754,7 @@ public:
     }
 
     // Whole inference of n pairs on this device with host buffers: the pairs run in
-    // sub-batches (input / output slots k * c), all inputs are copied in first on the
+    // sub-batches of decreasing size (input / output slots first[k] ..), all inputs are copied in first on the
     // copy stream, and each sub-batch's outputs are copied back there as soon as its
     // heads are done, overlapping the next sub-batch's compute.  outs[] point at this
     // device's first pair.  stage_ms[5] (summed over sub-batches), *h2d_ms (input
@@ -770,8 +770,19 @@ public:
                          float* h2d_ms, float* d2h_ms) {
         DeviceGuard g(dev_);
         M3R_REQUIRE(n >= 1 && n <= max_pairs_, "infer: pair count out of range for this device");
-        const int nsub = n >= 32 ? 4 : (n >= 16 ? 2 : 1);
-        const int c = (n + nsub - 1) / nsub;
+        // Sub-batches of decreasing size: every sub-batch's output copy overlaps the
+        // next one's compute, so only the last copy is exposed -- keep it small.
+        static constexpr int kW5[5] = {4, 4, 3, 2, 1}, kW3[3] = {3, 2, 1}, kW2[2] = {2, 1}, kW1[1] = {1};
+        const int* w = n >= 40 ? kW5 : n >= 16 ? kW3 : n >= 6 ? kW2 : kW1;
+        const int nsub = n >= 40 ? 5 : n >= 16 ? 3 : n >= 6 ? 2 : 1;
+        int first[6] = {0}, wsum = 0, wacc = 0;
+        for (int k = 0; k < nsub; ++k) wsum += w[k];
+        for (int k = 0; k < nsub; ++k) {
+            wacc += w[k];
+            first[k + 1] = (n * wacc + wsum / 2) / wsum;
+        }
+        int c = 0;  // largest sub-batch
+        for (int k = 0; k < nsub; ++k) c = std::max(c, first[k + 1] - first[k]);
         while (chunk_ev_.size() < static_cast<size_t>(kChunkEvents * nsub + 1)) {
             cudaEvent_t e;
             M3R_CUDA(cudaEventCreate(&e));
@@ -802,8 +813,8 @@ public:
                 for (int sslot = 0; sslot < 2; ++sslot) pinned(stage_out_[sslot], stage_out_cap_[sslot], c * pair_out_bytes);
             M3R_CUDA(cudaEventRecord(chunk_ev_[0], copy_stream_));
             for (int k = 0; k < nsub; ++k) {
-                const int slot = k * c, nk = std::min(c, n - slot);
-                if (nk <= 0) break;
+                const int slot = first[k], nk = first[k + 1] - first[k];
+                if (nk <= 0) continue;
                 M3R_CUDA(cudaMemcpyAsync(img_slot(0, slot), src1 + slot * ib, nk * ib, cudaMemcpyHostToDevice, copy_stream_));
                 M3R_CUDA(cudaMemcpyAsync(img_slot(1, slot), src2 + slot * ib, nk * ib, cudaMemcpyHostToDevice, copy_stream_));
                 M3R_CUDA(cudaEventRecord(ev(k, 5), copy_stream_));
@@ -811,7 +822,7 @@ public:
             // destination of output kind/view of sub-batch k: the caller's array, or the
             // staging slot k % 2 (laid out as the caller's arrays for nk pairs)
             auto out_dst = [&](int k, int kind, int view, int nk) -> float* {
-                const int slot = k * c;
+                const int slot = first[k];
                 if (!out_pageable) return outs[2 * kind + view] + slot * px * per_px[kind];
                 float* base = static_cast<float*>(stage_out_[k % 2]);
                 size_t off = 0;
@@ -820,7 +831,7 @@ public:
             };
             // staged sub-batch k -> the caller's arrays (host threads)
             auto unstage = [&](int k) {
-                const int slot = k * c, nk = std::min(c, n - slot);
+                const int slot = first[k], nk = first[k + 1] - first[k];
                 M3R_CUDA(cudaEventSynchronize(ev(k, 7)));
                 for (int kind = 0; kind < 3; ++kind)
                     for (int view = 0; view < 2; ++view)
@@ -830,8 +841,8 @@ public:
             };
             int last = 0;
             for (int k = 0; k < nsub; ++k) {
-                const int slot = k * c, nk = std::min(c, n - slot);
-                if (nk <= 0) break;
+                const int slot = first[k], nk = first[k + 1] - first[k];
+                if (nk <= 0) continue;
                 last = k;
                 M3R_CUDA(cudaStreamWaitEvent(stream_, ev(k, 5), 0));
                 const cudaEvent_t sev[5] = {ev(k, 0), ev(k, 1), ev(k, 2), ev(k, 3), ev(k, 4)};
