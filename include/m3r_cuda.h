@@ -228,6 +228,17 @@ int m3r_conv3_test(int device, int dtype, const uint16_t* x, const uint16_t* w, 
 int m3r_match_nn(int device, const float* desc_1, const float* desc_2, int64_t n1, int64_t n2, int desc_dim,
                  int32_t* nn_12, int32_t* nn_21, float* best_12, float* kernel_ms);
 
+/* The DPT head's 2x upsampling alone (mpsgraph_engine.mm:402-422, graph_builder.hpp:285-299):
+ * x [n, h, w, c] -> y [n, 2h, 2w, c], 16-bit of `dtype`, NHWC, bilinear with half-pixel
+ * centres and clamped borders.  c a multiple of 8. */
+int m3r_resize2x_test(int device, int dtype, const uint16_t* x, int n, int h, int w, int c, uint16_t* y);
+
+/* The DPT fusion alone (same lines): out [n, H, W, c] = f0 + up(f1) + up(f2) + up(f3), each
+ * f_i [n, h_i, w_i, c] upsampled as above to H x W.  c a multiple of 8. */
+int m3r_dpt_fuse_test(int device, int dtype, const uint16_t* f0, const uint16_t* f1, int h1, int w1,
+                      const uint16_t* f2, int h2, int w2, const uint16_t* f3, int h3, int w3, int n, int H, int W,
+                      int c, uint16_t* out);
+
 /* The preprocessing kernel of m3r_infer_any alone: uint8 [h, w, 3] -> [out_h, out_w, 3]. */
 int m3r_resize_crop_test(int device, const uint8_t* src, int h, int w, uint8_t* dst, int out_h, int out_w);
 

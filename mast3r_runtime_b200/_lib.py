@@ -82,6 +82,8 @@ SIGNATURES = {
     "m3r_load_retrieval": (_I, [_P, ctypes.c_char_p]),
     "m3r_encode_retrieval": (_I, [_P, _P, _I, _P, _P, _P]),
     "m3r_infer_any": (_I, [_P, _P, _I, _I, _P, _I, _I, _P, _P, _P, _P, _P, _P, _P]),
+    "m3r_resize2x_test": (_I, [_I, _I, _P, _I, _I, _I, _I, _P]),
+    "m3r_dpt_fuse_test": (_I, [_I, _I, _P, _P, _I, _I, _P, _I, _I, _P, _I, _I, _I, _I, _I, _I, _P]),
     "m3r_resize_crop_test": (_I, [_I, _P, _I, _I, _P, _I, _I]),
     "m3r_match_ex": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P, _P,
                           ctypes.POINTER(_I), _P]),

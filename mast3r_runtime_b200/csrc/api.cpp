@@ -205,6 +205,40 @@ int m3r_resize_crop_test(int device, const uint8_t* src, int h, int w, uint8_t* 
     });
 }
 
+int m3r_resize2x_test(int device, int dtype, const uint16_t* x, int n, int h, int w, int c, uint16_t* y) {
+    return guarded(nullptr, [&] {
+        M3R_REQUIRE(x && y && n > 0 && h > 0 && w > 0 && c > 0 && c % 8 == 0, "resize2x_test: bad arguments");
+        m3r::DeviceGuard g(device);
+        const size_t bi = static_cast<size_t>(n) * h * w * c * 2, bo = 4 * bi;
+        DBuf din(bi), dout(bo);
+        M3R_CUDA(cudaMemcpy(din.p, x, bi, cudaMemcpyHostToDevice));
+        m3r::resize16(nullptr, dtype, din.p, n, h, w, c, 2 * h, 2 * w, dout.p);
+        M3R_CUDA(cudaDeviceSynchronize());
+        M3R_CUDA(cudaMemcpy(y, dout.p, bo, cudaMemcpyDeviceToHost));
+    });
+}
+
+int m3r_dpt_fuse_test(int device, int dtype, const uint16_t* f0, const uint16_t* f1, int h1, int w1,
+                      const uint16_t* f2, int h2, int w2, const uint16_t* f3, int h3, int w3, int n, int H, int W,
+                      int c, uint16_t* out) {
+    return guarded(nullptr, [&] {
+        M3R_REQUIRE(f0 && f1 && f2 && f3 && out && n > 0 && H > 0 && W > 0 && h1 > 0 && w1 > 0 && h2 > 0 &&
+                        w2 > 0 && h3 > 0 && w3 > 0 && c > 0 && c % 8 == 0,
+                    "dpt_fuse_test: bad arguments");
+        m3r::DeviceGuard g(device);
+        const size_t e = static_cast<size_t>(n) * c * 2;
+        const size_t b0 = e * H * W, b1 = e * h1 * w1, b2 = e * h2 * w2, b3 = e * h3 * w3;
+        DBuf d0(b0), d1(b1), d2(b2), d3(b3), dout(b0);
+        M3R_CUDA(cudaMemcpy(d0.p, f0, b0, cudaMemcpyHostToDevice));
+        M3R_CUDA(cudaMemcpy(d1.p, f1, b1, cudaMemcpyHostToDevice));
+        M3R_CUDA(cudaMemcpy(d2.p, f2, b2, cudaMemcpyHostToDevice));
+        M3R_CUDA(cudaMemcpy(d3.p, f3, b3, cudaMemcpyHostToDevice));
+        m3r::dpt_fuse(nullptr, dtype, d0.p, d1.p, h1, w1, d2.p, h2, w2, d3.p, h3, w3, n, H, W, c, dout.p);
+        M3R_CUDA(cudaDeviceSynchronize());
+        M3R_CUDA(cudaMemcpy(out, dout.p, b0, cudaMemcpyDeviceToHost));
+    });
+}
+
 int m3r_match(m3r_engine* engine, const float* desc_1, const float* desc_2, int height, int width, int desc_dim,
               int top_k, int reciprocal, float confidence_threshold, int64_t* idx_1, int64_t* idx_2,
               float* confidence, float* pts2d_1, float* pts2d_2, int* n_matches, float* timing_ms) {

@@ -85,6 +85,82 @@ def test_gemm_residual_matches_fp64(lib, M, N, K, bn, dtype, pair):
     assert np.abs(c - ref).max() < 1e-4 * np.sqrt(K) * (np.abs(ref).max() + 1)
 
 
+def _upsample_ref(x, ho, wo):
+    """Bilinear NHWC upsampling with half-pixel centres and clamped borders, float64 (the
+    source coordinate (o + 0.5) * n_in / n_out - 0.5, clamped to [0, n_in - 1])."""
+    n, hi, wi, c = x.shape
+
+    def taps(n_in, n_out):
+        s = np.maximum((np.arange(n_out) + 0.5) * (n_in / n_out) - 0.5, 0.0)
+        i0 = np.minimum(np.floor(s).astype(np.int64), n_in - 1)
+        i1 = np.minimum(i0 + 1, n_in - 1)
+        return i0, i1, s - i0
+
+    y0, y1, fy = taps(hi, ho)
+    x0, x1, fx = taps(wi, wo)
+    xd = x.astype(np.float64)
+    fy = fy[None, :, None, None]
+    fx = fx[None, None, :, None]
+    top = xd[:, y0][:, :, x0] * (1 - fx) + xd[:, y0][:, :, x1] * fx
+    bot = xd[:, y1][:, :, x0] * (1 - fx) + xd[:, y1][:, :, x1] * fx
+    return top * (1 - fy) + bot * fy
+
+
+def _within_one_ulp(got, ref, mag, dtype):
+    """Every value within one unit in the last place of the 16-bit type (one rounding of an
+    fp32 result) plus the fp32 accumulation error, bounded by 2^-21 x the sum of the terms'
+    magnitudes `mag` (it matters only where the terms cancel)."""
+    mant = 10 if dtype == "fp16" else 7
+    ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(ref), 2.0 ** -14))) - mant)
+    tol = ulp + 2.0 ** -21 * mag
+    err = np.abs(got.astype(np.float64) - ref)
+    assert np.all(err <= tol), float((err / tol).max())
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+@pytest.mark.parametrize("n,h,w,c", [(2, 5, 7, 16), (1, 24, 32, 256), (3, 9, 4, 8)])
+def test_resize2x_matches_fp64(lib, n, h, w, c, dtype):
+    """The DPT head's 2x upsampling kernel (sliding rows, mixed-precision weights)."""
+    from mast3r_runtime_b200 import _lib
+
+    rng = np.random.default_rng(n * 100 + h + w + c)
+    x = round16(rng.standard_normal((n, h, w, c)).astype(np.float32) * 3, dtype)
+    y = np.zeros((n, 2 * h, 2 * w, c), np.uint16)
+    _lib.check(lib.m3r_resize2x_test(0, DTYPES[dtype], P(to16(x, dtype)), n, h, w, c, P(y)))
+    _within_one_ulp(from16(y, dtype), _upsample_ref(x, 2 * h, 2 * w), _upsample_ref(np.abs(x), 2 * h, 2 * w), dtype)
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+@pytest.mark.parametrize("n,H,W,c,pyramid", [
+    (2, 48, 64, 32, True),    # levels at 1/2, 1/4, 1/8: the mixed-precision kernel
+    (1, 96, 128, 256, True),  # the ViT-L 512x384 head's sizes, one image
+    (2, 40, 56, 16, False),   # other ratios: the general kernel
+])
+def test_dpt_fuse_matches_fp64(lib, n, H, W, c, pyramid, dtype):
+    """f0 + up(f1) + up(f2) + up(f3) (the DPT fusion kernel)."""
+    from mast3r_runtime_b200 import _lib
+
+    rng = np.random.default_rng(n + H + W + c)
+    sizes = [(H // 2, W // 2), (H // 4, W // 4), (H // 8, W // 8)] if pyramid else [(H // 2, W // 2), (7, 9), (3, 5)]
+    f0 = round16(rng.standard_normal((n, H, W, c)).astype(np.float32), dtype)
+    fs = [round16(rng.standard_normal((n, hh, ww, c)).astype(np.float32), dtype) for hh, ww in sizes]
+    out = np.zeros((n, H, W, c), np.uint16)
+    args = []
+    for f, (hh, ww) in zip(fs, sizes):
+        args += [P(to16(f, dtype)), hh, ww]
+    _lib.check(lib.m3r_dpt_fuse_test(0, DTYPES[dtype], P(to16(f0, dtype)), *args, n, H, W, c, P(out)))
+    ref = f0.astype(np.float64) + sum(_upsample_ref(f, H, W) for f in fs)
+    got = from16(out, dtype)
+    if pyramid:
+        mag = np.abs(f0).astype(np.float64) + sum(_upsample_ref(np.abs(f), H, W) for f in fs)
+        _within_one_ulp(got, ref, mag, dtype)
+    else:
+        # fp32 interpolation weights that are not exact in 16 bits: one 16-bit rounding plus
+        # fp32 arithmetic, judged against the sum's magnitude
+        tol = (2.0 ** -10 if dtype == "fp16" else 2.0 ** -7) * (np.abs(ref) + 1.0)
+        assert np.all(np.abs(got - ref) <= tol)
+
+
 def _conv3_ref(x, w, b):
     n, h, wd, c = x.shape
     co = w.shape[0]
