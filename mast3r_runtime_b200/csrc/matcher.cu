@@ -24,6 +24,7 @@
 //                  the top_k largest (conf, -i) keys, then a bitonic sort of
 //                  those, i.e. confidence descending, idx_1 ascending on ties.
 #include <algorithm>
+#include <type_traits>
 #include <vector>
 
 #include "matcher.h"
@@ -179,10 +180,25 @@ __global__ void __launch_bounds__(256, 2)
                     sA[k][rr] = gi < row1 ? A[gi * D + kc + k] : 0.0f;
                 }
             }
-            for (int e = tid; e < kTJ * kn; e += 256) {
-                const int cc = e / kn, k = e - cc * kn;
-                const long long gj = j0 + cc;
-                sB[k][cc] = gj < n2 ? B[gj * D + kc + k] : 0.0f;
+            if (DFIX > 0 && DFIX <= kKC && DFIX % 4 == 0) {
+                // whole 16-byte pieces of the rows (rows are D * 4 bytes, 16-byte aligned)
+                constexpr int kQ = DFIX / 4;
+                for (int e = tid; e < kTJ * kQ; e += 256) {
+                    const int cc = e / kQ, q = e - cc * kQ;
+                    const long long gj = j0 + cc;
+                    const float4 v = gj < n2 ? *reinterpret_cast<const float4*>(B + gj * D + 4 * q)
+                                             : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    sB[4 * q][cc] = v.x;
+                    sB[4 * q + 1][cc] = v.y;
+                    sB[4 * q + 2][cc] = v.z;
+                    sB[4 * q + 3][cc] = v.w;
+                }
+            } else {
+                for (int e = tid; e < kTJ * kn; e += 256) {
+                    const int cc = e / kn, k = e - cc * kn;
+                    const long long gj = j0 + cc;
+                    sB[k][cc] = gj < n2 ? B[gj * D + kc + k] : 0.0f;
+                }
             }
             __syncthreads();
             const int KN = DFIX > 0 ? (DFIX < kKC ? DFIX : kKC) : kKC;
@@ -219,57 +235,68 @@ __global__ void __launch_bounds__(256, 2)
             }
         }
 
-        // ---- rows: first (lowest j) maximum over this thread's columns, in increasing j.
-        // The reference seeds every row with column 0 and replaces it only on a strictly
-        // greater value (matching.cpp:128-139), so column 0 is taken even when it is NaN
-        // or -inf; a NaN seed is never replaced (its key, all ones, is the largest).
-        const bool seed_col0 = j0 == 0 && tc == 0;  // this thread holds column 0 (first tile of segment 0)
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
-            float m = -INFINITY;
-            int mc = -1;
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                if (c == 0 && seed_col0) {
-                    m = s[r][0];
-                    mc = 0;
-                } else if (cv[c] && s[r][c] > m) {
-                    m = s[r][c];
-                    mc = c;
-                }
-            }
-            if (mc >= 0 && (seed_col0 || m > rbest[r])) {
-                rbest[r] = m;
-                ridx[r] = static_cast<uint32_t>(j0 + (mc < 4 ? tc * 4 + mc : 64 + tc * 4 + mc - 4));
-            }
-        }
-
-        // ---- columns: first (lowest i) maximum over this thread's rows, keyed; row 0
-        // seeds every column as in matching.cpp:144-155
-        const bool seed_row0 = i0 == 0 && tr == 0;
+        // The row / column arg-max below runs in two instantiations: kEdge for the tiles
+        // that hold a seed (column 0 or row 0) or ragged rows / columns, and a
+        // predicate-free one for every interior tile (the condition is uniform per CTA).
         unsigned long long ck[8];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            float m = -INFINITY;
-            int mr = -1;
+        auto argmax_tile = [&](auto edge_tag) {
+            constexpr bool kEdge = decltype(edge_tag)::value;
+            // ---- rows: first (lowest j) maximum over this thread's columns, in increasing j.
+            // The reference seeds every row with column 0 and replaces it only on a strictly
+            // greater value (matching.cpp:128-139), so column 0 is taken even when it is NaN
+            // or -inf; a NaN seed is never replaced (its key, all ones, is the largest).
+            // this thread holds column 0 (first tile of segment 0)
+            const bool seed_col0 = kEdge && j0 == 0 && tc == 0;
 #pragma unroll
             for (int r = 0; r < 8; ++r) {
-                if (r == 0 && seed_row0) {
-                    m = s[0][c];
-                    mr = 0;
-                } else if (rv[r] && s[r][c] > m) {
-                    m = s[r][c];
-                    mr = r;
+                float m = -INFINITY;
+                int mc = -1;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    if (c == 0 && seed_col0) {
+                        m = s[r][0];
+                        mc = 0;
+                    } else if ((!kEdge || cv[c]) && s[r][c] > m) {
+                        m = s[r][c];
+                        mc = c;
+                    }
+                }
+                if (mc >= 0 && (seed_col0 || m > rbest[r])) {
+                    rbest[r] = m;
+                    ridx[r] = static_cast<uint32_t>(j0 + (mc < 4 ? tc * 4 + mc : 64 + tc * 4 + mc - 4));
                 }
             }
-            ck[c] = mr >= 0 ? make_key(m, static_cast<uint32_t>(i0 + tr * 8 + mr)) : 0ull;
-            // reduce over the 4 row groups of this warp (lanes differing in bits 3, 4)
+
+            // ---- columns: first (lowest i) maximum over this thread's rows, keyed; row 0
+            // seeds every column as in matching.cpp:144-155
+            const bool seed_row0 = kEdge && i0 == 0 && tr == 0;
 #pragma unroll
-            for (int o = 8; o <= 16; o <<= 1) {
-                const unsigned long long other = __shfl_xor_sync(0xffffffffu, ck[c], o);
-                ck[c] = other > ck[c] ? other : ck[c];
+            for (int c = 0; c < 8; ++c) {
+                float m = -INFINITY;
+                int mr = -1;
+#pragma unroll
+                for (int r = 0; r < 8; ++r) {
+                    if (r == 0 && seed_row0) {
+                        m = s[0][c];
+                        mr = 0;
+                    } else if ((!kEdge || rv[r]) && s[r][c] > m) {
+                        m = s[r][c];
+                        mr = r;
+                    }
+                }
+                ck[c] = mr >= 0 ? make_key(m, static_cast<uint32_t>(i0 + tr * 8 + mr)) : 0ull;
+                // reduce over the 4 row groups of this warp (lanes differing in bits 3, 4)
+#pragma unroll
+                for (int o = 8; o <= 16; o <<= 1) {
+                    const unsigned long long other = __shfl_xor_sync(0xffffffffu, ck[c], o);
+                    ck[c] = other > ck[c] ? other : ck[c];
+                }
             }
-        }
+        };
+        if (j0 == 0 || i0 == 0 || jleft < kTJ || i0 + kTI > row1)
+            argmax_tile(std::true_type{});
+        else
+            argmax_tile(std::false_type{});
         if ((lane >> 3) == 0) {
 #pragma unroll
             for (int c = 0; c < 8; ++c) sCol[warp >> 1][c < 4 ? tc * 4 + c : 64 + tc * 4 + c - 4] = ck[c];
