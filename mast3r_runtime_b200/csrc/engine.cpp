@@ -1626,8 +1626,7 @@ int Engine::match(const float* d1, const float* d2, int hh, int ww, int dd, int 
             M3R_CUDA(cudaMemcpyAsync(D.mws.c2, ex->conf_2, sizeof(float) * n, cudaMemcpyHostToDevice, s));
         }
         M3R_CUDA(cudaEventRecord(ev.e[0], s));
-        match_normalize(s, D.mws.a, D.mws.a, n, dd);
-        match_normalize(s, D.mws.b, D.mws.b, n, dd);
+        match_normalize2(s, D.mws.a, D.mws.a, n, D.mws.b, D.mws.b, n, dd);
         M3R_CUDA(cudaEventRecord(ev.e[1], s));
         match_argmax(s, D.mws.a, D.mws.b, 0, n, n, dd, D.mws.rowkey, D.mws.colkey, true,
                      weighted ? D.mws.c1 : nullptr, weighted ? D.mws.c2 : nullptr);
@@ -1716,8 +1715,7 @@ int Engine::match_multi(const float* d1, const float* d2, const float* c1, const
             M3R_CUDA(cudaMemcpyAsync(D.mws.c2, c2, sizeof(float) * n, cudaMemcpyHostToDevice, s));
         }
         M3R_CUDA(cudaEventRecord(P.ev->e[0], s));
-        match_normalize(s, D.mws.a, D.mws.a, nr, dd);
-        match_normalize(s, D.mws.b, D.mws.b, n, dd);
+        match_normalize2(s, D.mws.a, D.mws.a, nr, D.mws.b, D.mws.b, n, dd);
         M3R_CUDA(cudaEventRecord(P.ev->e[1], s));
         // A is addressed by global row: rows [r0, r1) live at mws.a[0 .. nr)
         match_argmax(s, D.mws.a - P.r0 * dd, D.mws.b, P.r0, P.r1, n, dd, D.mws.rowkey, D.mws.colkey, true,

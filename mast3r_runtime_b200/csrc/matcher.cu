@@ -101,6 +101,69 @@ __global__ void normalize24_kernel(const float4* in, float4* out, long long n) {
     }
 }
 
+// Both descriptor sets in one launch: a set is a few tens of MB, so one launch instead
+// of two halves the ramp-up and tail.  A warp takes 32 consecutive rows of one set
+// (3 KB): it loads them with coalesced 16-byte loads into shared memory, each lane
+// normalises one row there (the sequential arithmetic of normalize24_kernel), and the
+// warp stores the block back with coalesced 16-byte stores.
+constexpr int kNormWarps = 8;
+__global__ void __launch_bounds__(kNormWarps * 32)
+    normalize24_pair_kernel(const float4* in1, float4* out1, long long n1, const float4* in2, float4* out2,
+                            long long n2) {
+    __shared__ float4 stage[kNormWarps][32 * 6];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    float4* sw = stage[w];
+    const long long t1 = (n1 + 31) / 32, tasks = t1 + (n2 + 31) / 32;
+    for (long long task = blockIdx.x * static_cast<long long>(kNormWarps) + w; task < tasks;
+         task += static_cast<long long>(gridDim.x) * kNormWarps) {
+        const bool first = task < t1;
+        const long long r0 = 32 * (first ? task : task - t1);
+        const long long n = first ? n1 : n2;
+        const float4* in = (first ? in1 : in2) + r0 * 6;
+        float4* out = (first ? out1 : out2) + r0 * 6;
+        const int rows = n - r0 < 32 ? static_cast<int>(n - r0) : 32;
+#pragma unroll
+        for (int q = 0; q < 6; ++q) {
+            const int f = lane + 32 * q;
+            if (f < 6 * rows) sw[f] = in[f];
+        }
+        __syncwarp();
+        if (lane < rows) {
+            float4 x[6];
+#pragma unroll
+            for (int q = 0; q < 6; ++q) x[q] = sw[lane * 6 + q];
+            float s = 0.0f;
+#pragma unroll
+            for (int q = 0; q < 6; ++q) {
+                s = __fadd_rn(s, __fmul_rn(x[q].x, x[q].x));
+                s = __fadd_rn(s, __fmul_rn(x[q].y, x[q].y));
+                s = __fadd_rn(s, __fmul_rn(x[q].z, x[q].z));
+                s = __fadd_rn(s, __fmul_rn(x[q].w, x[q].w));
+            }
+            s = sqrtf(s);
+            if (s > 1e-8f) {
+                const float inv = 1.0f / s;
+#pragma unroll
+                for (int q = 0; q < 6; ++q) {
+                    x[q].x = __fmul_rn(x[q].x, inv);
+                    x[q].y = __fmul_rn(x[q].y, inv);
+                    x[q].z = __fmul_rn(x[q].z, inv);
+                    x[q].w = __fmul_rn(x[q].w, inv);
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < 6; ++q) sw[lane * 6 + q] = x[q];
+        }
+        __syncwarp();
+#pragma unroll
+        for (int q = 0; q < 6; ++q) {
+            const int f = lane + 32 * q;
+            if (f < 6 * rows) out[f] = sw[f];
+        }
+        __syncwarp();  // the next task's loads overwrite the stage
+    }
+}
+
 // ------------------------------------------------------------------ argmax
 constexpr int kTI = 128;  // rows per CTA tile
 constexpr int kTJ = 128;  // columns per j-tile
@@ -648,6 +711,25 @@ void match_normalize(cudaStream_t s, const float* in, float* out, long long n, i
                                                                reinterpret_cast<float4*>(out), n);
     else
         normalize_kernel<<<blocks_for(n, 256), 256, 0, s>>>(in, out, n, d);
+    M3R_CUDA(cudaGetLastError());
+}
+
+void match_normalize2(cudaStream_t s, const float* in1, float* out1, long long n1, const float* in2, float* out2,
+                      long long n2, int d) {
+    const bool aligned =
+        ((reinterpret_cast<uintptr_t>(in1) | reinterpret_cast<uintptr_t>(out1) | reinterpret_cast<uintptr_t>(in2) |
+          reinterpret_cast<uintptr_t>(out2)) %
+         16) == 0;
+    if (d != 24 || !aligned || n1 == 0 || n2 == 0) {
+        match_normalize(s, in1, out1, n1, d);
+        match_normalize(s, in2, out2, n2, d);
+        return;
+    }
+    long long blocks = ((n1 + 31) / 32 + (n2 + 31) / 32 + kNormWarps - 1) / kNormWarps;
+    if (blocks > 148LL * 8) blocks = 148LL * 8;
+    normalize24_pair_kernel<<<static_cast<int>(blocks), kNormWarps * 32, 0, s>>>(
+        reinterpret_cast<const float4*>(in1), reinterpret_cast<float4*>(out1), n1, reinterpret_cast<const float4*>(in2),
+        reinterpret_cast<float4*>(out2), n2);
     M3R_CUDA(cudaGetLastError());
 }
 

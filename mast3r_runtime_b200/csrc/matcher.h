@@ -35,6 +35,9 @@ struct MatchWorkspace {
 
 // Reference normalisation (csrc/cpu/matching.cpp:22-44), out may alias in.
 void match_normalize(cudaStream_t s, const float* in, float* out, long long n, int d);
+// Both sets in one launch where the layout allows (d == 24, 16-byte aligned), else two.
+void match_normalize2(cudaStream_t s, const float* in1, float* out1, long long n1, const float* in2, float* out2,
+                      long long n2, int d);
 
 // Row keys of rows [row0, row1) of A (rowkey[i - row0]) and column keys of all n2
 // columns of B (colkey[j], merged with atomicMax; cleared first when asked).  With
