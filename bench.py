@@ -382,6 +382,24 @@ def run_reference(args):
     return 0
 
 
+def shard_pairs(total_pairs: int, world: int, rank: int):
+    """(first pair, pairs) of this rank: the global batch split evenly, in rank order."""
+    per = total_pairs // world
+    assert per * world == total_pairs, "global batch must divide over the GPUs"
+    return rank * per, per
+
+
+def all_max(dist, x: float, device=None) -> float:
+    """Maximum of x over the ranks of the default group (x itself without one)."""
+    if dist is None:
+        return x
+    import torch
+
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def run_ours(args):
     rank, local_rank, world = env_rank()
     dist = None
@@ -401,13 +419,7 @@ def run_ours(args):
         host_group = tdist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=600))
 
     def allmax(x: float) -> float:
-        if dist is None:
-            return x
-        import torch
-
-        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local_rank}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return all_max(dist, x, f"cuda:{local_rank}")
 
     def barrier():
         if dist is not None:
@@ -422,12 +434,11 @@ def run_ours(args):
 
     d = VARIANTS[VARIANT]
     total_pairs = args.pairs
-    per = total_pairs // world
-    assert per * world == total_pairs, "global batch must divide over the GPUs"
+    first, per = shard_pairs(total_pairs, world, rank)
     dtypes = {"fp16": _lib.DTYPE_F16, "bf16": _lib.DTYPE_BF16}
     main_dt = dtypes[args.dtype]
     path = weights_file(d, rank, dist)
-    img1, img2 = make_inputs(rank * per, per, IMAGE_HW)
+    img1, img2 = make_inputs(first, per, IMAGE_HW)
 
     def resident(eng, sample_clocks):
         """W warm-up + K timed resident passes; (device ms summed over K, max over ranks), wall s, clocks."""
