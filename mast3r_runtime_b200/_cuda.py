@@ -393,7 +393,7 @@ class CUDAEngine:
             out = {k: np.concatenate([p[0][k] for p in parts]) for k in parts[0][0]}
             timing = {k: sum(p[1][k] for p in parts) for k in parts[0][1]}
             return out, timing
-        per_dev = max(1, min(int(os.environ.get("M3R_PAIRS_PER_GPU", "16")), -(-n // len(self.devices))))
+        per_dev = max(1, min(int(os.environ.get("M3R_PAIRS_PER_GPU", "64")), -(-n // len(self.devices))))
         eng = self._engine(self.image_hw, per_dev)
         return eng.infer_batch(img1, img2)
 
