@@ -174,7 +174,7 @@ def test_pipelined_infer_matches_resident(tmp_path):
     d = tiny_dims()
     path = save_safetensors(tmp_path / "u.safetensors", make_weights(d, seed=8, randomize_affine=True))
     rng = np.random.default_rng(12)
-    n = 33  # four sub-batches: 9, 9, 9, 6
+    n = 40  # four sub-batches of decreasing size: 15, 13, 10, 2
     img1 = rng.integers(0, 256, (n, 64, 96, 3), dtype=np.uint8)
     img2 = rng.integers(0, 256, (n, 64, 96, 3), dtype=np.uint8)
     eng = NativeEngine(d, (64, 96), [0], n)
