@@ -312,6 +312,27 @@ __global__ void __launch_bounds__(256, 2)
             const bool seed_col0 = kEdge && j0 == 0 && tc == 0;
 #pragma unroll
             for (int r = 0; r < 8; ++r) {
+                if constexpr (!kEdge) {
+                    // interior tile: the row's running best rarely improves, so take the
+                    // maximum (fmaxf ignores NaN, as the strict comparison does) and look for
+                    // its first column only when it beats the running best
+                    const float m = fmaxf(fmaxf(fmaxf(s[r][0], s[r][1]), fmaxf(s[r][2], s[r][3])),
+                                          fmaxf(fmaxf(s[r][4], s[r][5]), fmaxf(s[r][6], s[r][7])));
+                    if (m > rbest[r]) {
+                        // first column equal to the maximum, and its own bits (-0 vs +0)
+                        int mc = 7;
+                        float mv = s[r][7];
+#pragma unroll
+                        for (int c = 6; c >= 0; --c) {
+                            const bool eq = s[r][c] == m;
+                            mc = eq ? c : mc;
+                            mv = eq ? s[r][c] : mv;
+                        }
+                        rbest[r] = mv;
+                        ridx[r] = static_cast<uint32_t>(j0 + (mc < 4 ? tc * 4 + mc : 64 + tc * 4 + mc - 4));
+                    }
+                    continue;
+                }
                 float m = -INFINITY;
                 int mc = -1;
 #pragma unroll
