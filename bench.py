@@ -570,6 +570,9 @@ def run_ours(args):
         attention_iso = {"workload": f"{ATT_SEQS} seqs (64 pairs x 2 views) x {ATT_HEADS} heads x {ATT_TOK} tokens "
                                      f"(24x24 grid) x 64, {args.dtype}, Q/K/V ~ N(0,1) (RoPE is applied by the "
                                      f"producing QKV GEMM's epilogue in this design)", "flop_per_launch": flop, **res}
+        # the operand type the configuration states (bf16) beside the headline's
+        oname = "bf16" if args.dtype == "fp16" else "fp16"
+        attention_iso[oname] = run_attention(dtypes[oname])[1]
 
     # ---------------- the smaller configurations, device-resident on rank 0's GPU
     small = None
@@ -616,6 +619,9 @@ def run_ours(args):
         if attention_iso is not None:
             for k in ("self", "cross"):
                 attention_iso[k]["frac_of_burst"] = attention_iso[k]["tflops"] / peak_burst
+                for other_dt in ("fp16", "bf16"):
+                    if other_dt in attention_iso:
+                        attention_iso[other_dt][k]["frac_of_burst"] = attention_iso[other_dt][k]["tflops"] / peak_burst
         line = {
             "metric": METRIC, "value": value, "unit": "pairs/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
