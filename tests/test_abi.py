@@ -39,6 +39,33 @@ def test_library_exports_every_declared_symbol():
     assert sorted(_lib.SIGNATURES) == names
 
 
+def declared_prototypes():
+    """name -> (return type text, parameter count) of every declaration in the header."""
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    protos = {}
+    for ret, name, params in re.findall(r"([A-Za-z_][A-Za-z0-9_ ]*?\**)\s*\b(m3r_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text):
+        params = params.strip()
+        n = 0 if params in ("", "void") else params.count(",") + 1
+        protos[name] = (ret.split()[-1] if ret.split() else ret, n)
+    return protos
+
+
+def test_ctypes_signatures_match_the_header():
+    """Every binding in _lib.SIGNATURES takes as many arguments as its C declaration, and
+    the int-returning entry points are bound as returning int."""
+    from mast3r_runtime_b200 import _lib
+
+    protos = declared_prototypes()
+    assert sorted(protos) == sorted(_lib.SIGNATURES)
+    for name, (res, args) in _lib.SIGNATURES.items():
+        ret, n = protos[name]
+        assert len(args) == n, f"{name}: {len(args)} ctypes arguments, {n} in include/m3r_cuda.h"
+        if ret == "int":
+            assert res is ctypes.c_int, name
+        elif ret == "void":
+            assert res is None, name
+
+
 def test_config_layout_matches_c(tmp_path):
     from mast3r_runtime_b200 import _lib
 
