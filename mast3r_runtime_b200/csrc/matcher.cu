@@ -170,7 +170,7 @@ constexpr int kTJ = 128;  // columns per j-tile
 constexpr int kKC = 32;   // k chunk held in shared memory
 constexpr int kPitch = 128 + 4;
 #ifndef M3R_ARGMAX_UNROLL
-#define M3R_ARGMAX_UNROLL 4
+#define M3R_ARGMAX_UNROLL 2
 #endif
 constexpr int kArgmaxUnroll = M3R_ARGMAX_UNROLL;
 
